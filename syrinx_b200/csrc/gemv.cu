@@ -1,0 +1,439 @@
+// gemv.cu — fused dequant-GEMV for decode: y = x . W^T over Q8_0 / Q4_K / F32 weights.
+//
+// Replaces the quantized linear of the reference hot path (`Weights::linear`,
+// crates/syrinx-fish/src/s2/nn.rs:61-68; `Qwen2Lm::linear` over candle QMatMul,
+// crates/syrinx-lm/src/cv2/mod.rs:195-211) at M = 1..8 tokens, with the neighbouring
+// element-wise ops fused in:
+//   prologue  RMSNorm of x with a gain vector (rms_norm_w, s2/nn.rs:100-106)
+//   epilogue  + bias, residual add (s2/slow_ar.rs:195,198), SiLU(g)*u (s2/nn.rs:452-457),
+//             or the greedy argmax of the head (sampling.rs:189-245 with top_k = 1).
+//
+// Memory-bound design (one pass over the weights, HBM roofline):
+//   * a warp owns RPW weight rows; each lane streams 128-bit chunks of those rows with
+//     ld.global.nc.L1::no_allocate, UNROLL chunks per row in flight;
+//   * Q8_0 / Q4_K values are unpacked in registers (byte-permute into the 2^23 mantissa,
+//     exact) and multiplied on the packed f32x2 FMA pipe against x held in shared memory;
+//   * per-block scales are applied to 16/32-element partial dots; fp32 accumulation;
+//   * the cross-lane reduction is a warp shuffle butterfly;
+//   * the first weight chunks are requested before griddepcontrol.wait, so with
+//     programmatic dependent launch the weight stream of this kernel overlaps the tail of
+//     the kernel that produces x.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "sx_device.cuh"
+#include "sx_internal.hpp"
+
+namespace sx {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+
+// Elements covered by one lane-chunk (16 bytes of packed weights).
+template <int WT> struct Unit;
+template <> struct Unit<SX_DTYPE_Q8_0> { static constexpr int elems = 16; };
+template <> struct Unit<SX_DTYPE_Q4_K> { static constexpr int elems = 32; };
+template <> struct Unit<SX_DTYPE_F32> { static constexpr int elems = 4; };
+
+template <int WT> struct Frag;
+template <> struct Frag<SX_DTYPE_Q8_0> {
+  uint4 q;
+  float d;
+};
+template <> struct Frag<SX_DTYPE_Q4_K> {
+  uint4 q;
+  uint4 meta;
+};
+template <> struct Frag<SX_DTYPE_F32> {
+  uint4 q;
+};
+
+__device__ __forceinline__ int phys_row(const GemvArgs& a, int i) {
+  return i < a.n_range ? a.row_base + i : a.extra[i - a.n_range];
+}
+
+template <int WT>
+__device__ __forceinline__ void load_frag(const GemvArgs& a, int prow, int unit, Frag<WT>& f) {
+  const int64_t K = a.w.cols;
+  if constexpr (WT == SX_DTYPE_Q8_0) {
+    const int8_t* q = (const int8_t*)a.w.q + (size_t)prow * K + (size_t)unit * 16;
+    f.q = ldg_stream(q);
+    f.d = __half2float(a.w.s[(size_t)prow * (K / 32) + (unit >> 1)]);
+  } else if constexpr (WT == SX_DTYPE_Q4_K) {
+    const uint8_t* q = (const uint8_t*)a.w.q + (size_t)prow * (K / 2) + (size_t)unit * 16;
+    f.q = ldg_stream(q);
+    f.meta = __ldg((const uint4*)(a.w.meta + ((size_t)prow * (K / 256) + (unit >> 3)) * 16));
+  } else {
+    const float* q = (const float*)a.w.q + (size_t)prow * K + (size_t)unit * 4;
+    f.q = ldg_stream(q);
+  }
+}
+
+// Q4_K 6-bit sub-block scale / min of sub-block j from the 12 packed bytes.
+__device__ __forceinline__ void q4k_sm(const uint8_t* sc12, int j, float& sc, float& m) {
+  uint32_t s, mm;
+  if (j < 4) {
+    s = sc12[j] & 63;
+    mm = sc12[j + 4] & 63;
+  } else {
+    s = (sc12[j + 4] & 0xF) | ((sc12[j - 4] >> 6) << 4);
+    mm = (sc12[j + 4] >> 4) | ((sc12[j] >> 6) << 4);
+  }
+  sc = (float)s;
+  m = (float)mm;
+}
+
+// Dot of one fragment with M token vectors held in shared memory.
+template <int WT, int M>
+__device__ __forceinline__ void frag_dot(const Frag<WT>& f, const float* xs, int K, int unit,
+                                         const float* xsum16, float (&acc)[M]) {
+  if constexpr (WT == SX_DTYPE_Q8_0) {
+    unsigned long long w[8];
+    const uint32_t words[4] = {f.q.x, f.q.y, f.q.z, f.q.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) i8x4_to_f32x2x2(words[j], w[2 * j], w[2 * j + 1]);
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const ulonglong2* xv = (const ulonglong2*)(xs + (size_t)m * K + unit * 16);
+      unsigned long long s0 = 0, s1 = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const ulonglong2 x2 = xv[j];
+        s0 = fma2(w[2 * j], x2.x, s0);
+        s1 = fma2(w[2 * j + 1], x2.y, s1);
+      }
+      float a0, a1, b0, b1;
+      unpack2(s0, a0, a1);
+      unpack2(s1, b0, b1);
+      acc[m] = fmaf(f.d, (a0 + a1) + (b0 + b1), acc[m]);
+    }
+  } else if constexpr (WT == SX_DTYPE_Q4_K) {
+    // unit u: super-block sb = u/8, chunk c = u%8 -> 64-group j = c/2, offset l0 = 16*(c%2)
+    const int c = unit & 7;
+    const int jj = c >> 1;
+    const int e_lo = (unit >> 3) * 256 + jj * 64 + (c & 1) * 16;  // first low-nibble element
+    const __half2 dd = *reinterpret_cast<const __half2*>(&f.meta.x);
+    const float d = __low2float(dd), dmin = __high2float(dd);
+    const uint8_t* sc12 = reinterpret_cast<const uint8_t*>(&f.meta) + 4;
+    float sc_lo, m_lo, sc_hi, m_hi;
+    q4k_sm(sc12, 2 * jj, sc_lo, m_lo);
+    q4k_sm(sc12, 2 * jj + 1, sc_hi, m_hi);
+    const float dl = d * sc_lo, ml = dmin * m_lo, dh = d * sc_hi, mh = dmin * m_hi;
+    unsigned long long wl[8], wh[8];
+    const uint32_t words[4] = {f.q.x, f.q.y, f.q.z, f.q.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      u4x4_to_f32x2x2(words[j] & 0x0F0F0F0Fu, wl[2 * j], wl[2 * j + 1]);
+      u4x4_to_f32x2x2((words[j] >> 4) & 0x0F0F0F0Fu, wh[2 * j], wh[2 * j + 1]);
+    }
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const ulonglong2* xl = (const ulonglong2*)(xs + (size_t)m * K + e_lo);
+      const ulonglong2* xh = (const ulonglong2*)(xs + (size_t)m * K + e_lo + 32);
+      unsigned long long sl = 0, sh = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const ulonglong2 a2 = xl[j], b2 = xh[j];
+        sl = fma2(wl[2 * j], a2.x, sl);
+        sl = fma2(wl[2 * j + 1], a2.y, sl);
+        sh = fma2(wh[2 * j], b2.x, sh);
+        sh = fma2(wh[2 * j + 1], b2.y, sh);
+      }
+      float a0, a1, b0, b1;
+      unpack2(sl, a0, a1);
+      unpack2(sh, b0, b1);
+      const float* xsm = xsum16 + (size_t)m * (K / 16);
+      float r = dl * (a0 + a1) - ml * xsm[e_lo >> 4];
+      r += dh * (b0 + b1) - mh * xsm[(e_lo + 32) >> 4];
+      acc[m] += r;
+    }
+  } else {
+    const unsigned long long w0 = pack2u(f.q.x, f.q.y), w1 = pack2u(f.q.z, f.q.w);
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const ulonglong2 x2 = *(const ulonglong2*)(xs + (size_t)m * K + unit * 4);
+      unsigned long long s = fma2(w0, x2.x, 0ull);
+      s = fma2(w1, x2.y, s);
+      float a0, a1;
+      unpack2(s, a0, a1);
+      acc[m] += a0 + a1;
+    }
+  }
+}
+
+template <int WT, int M, int RPW, int UNROLL, int EPI>
+__global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  constexpr int UE = Unit<WT>::elems;
+  const int K = (int)a.w.cols;
+  const int units = K / UE;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_logical = a.n_range + a.n_extra;
+  const int row0 = (blockIdx.x * kWarps + warp) * RPW;
+
+  pdl_launch_dependents();
+
+  int prow[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; r++) {
+    const int i = row0 + r;
+    prow[r] = phys_row(a, i < n_logical ? i : n_logical - 1);
+  }
+
+  // First weight chunks do not depend on the previous kernel: request them now.
+  Frag<WT> fr[UNROLL][RPW];
+#pragma unroll
+  for (int u = 0; u < UNROLL; u++) {
+    const int unit = u * 32 + lane;
+    if (unit < units)
+#pragma unroll
+      for (int r = 0; r < RPW; r++) load_frag<WT>(a, prow[r], unit, fr[u][r]);
+  }
+
+  pdl_wait();
+
+  // ---- stage x (optionally RMS-normalised) into shared memory ----
+  float* xs = smem;                       // [M][K]
+  float* xsum16 = smem + (size_t)M * K;   // [M][K/16] (Q4_K only)
+  __shared__ float red[kWarps][kMaxTok];
+  __shared__ float den[kMaxTok];
+  if (a.norm_w) {
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) ss[m] = 0.f;
+    for (int k = threadIdx.x; k < K; k += kThreads)
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float v = (m < a.M) ? a.x[(size_t)m * K + k] : 0.f;
+        ss[m] = fmaf(v, v, ss[m]);
+      }
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const float t = warp_sum(ss[m]);
+      if (lane == 0) red[warp][m] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x < M) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
+      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)K), a.eps));
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < K; k += kThreads) {
+      const float g = a.norm_w[k];
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float v = (m < a.M) ? a.x[(size_t)m * K + k] : 0.f;
+        xs[(size_t)m * K + k] = __fmul_rn(__fdiv_rn(v, den[m]), g);
+      }
+    }
+  } else {
+    const int nv = K / 4;
+    for (int i = threadIdx.x; i < nv; i += kThreads)
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < a.M) v = reinterpret_cast<const float4*>(a.x + (size_t)m * K)[i];
+        reinterpret_cast<float4*>(xs + (size_t)m * K)[i] = v;
+      }
+  }
+  __syncthreads();
+  if constexpr (WT == SX_DTYPE_Q4_K) {
+    for (int g = threadIdx.x; g < K / 16; g += kThreads)
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float* p = xs + (size_t)m * K + g * 16;
+        float t = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; e++) t += p[e];
+        xsum16[(size_t)m * (K / 16) + g] = t;
+      }
+    __syncthreads();
+  }
+
+  // ---- main loop over the row ----
+  float acc[RPW][M];
+#pragma unroll
+  for (int r = 0; r < RPW; r++)
+#pragma unroll
+    for (int m = 0; m < M; m++) acc[r][m] = 0.f;
+
+  for (int base = 0; base < units; base += 32 * UNROLL) {
+    if (base > 0) {
+#pragma unroll
+      for (int u = 0; u < UNROLL; u++) {
+        const int unit = base + u * 32 + lane;
+        if (unit < units)
+#pragma unroll
+          for (int r = 0; r < RPW; r++) load_frag<WT>(a, prow[r], unit, fr[u][r]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; u++) {
+      const int unit = base + u * 32 + lane;
+      if (unit < units)
+#pragma unroll
+        for (int r = 0; r < RPW; r++) frag_dot<WT, M>(fr[u][r], xs, K, unit, xsum16, acc[r]);
+    }
+  }
+
+#pragma unroll
+  for (int r = 0; r < RPW; r++)
+#pragma unroll
+    for (int m = 0; m < M; m++) acc[r][m] = warp_sum(acc[r][m]);
+
+  // ---- epilogues ----
+  if constexpr (EPI == EPI_SWIGLU) {
+    // rows (row0 + 2p, row0 + 2p + 1) = (gate_j, up_j) with j = (row0 + 2p) / 2
+    if (lane == 0) {
+#pragma unroll
+      for (int p = 0; p < RPW / 2; p++) {
+        const int i = row0 + 2 * p;
+        if (i + 1 < n_logical) {
+          const int j = i >> 1;
+#pragma unroll
+          for (int m = 0; m < M; m++)
+            if (m < a.M) {
+              const float g = acc[2 * p][m], u = acc[2 * p + 1][m];
+              a.y[(size_t)m * a.ldy + j] = __fmul_rn(silu_f(g), u);
+            }
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_ARGMAX) {
+    __shared__ unsigned long long best[kWarps][kMaxTok];
+    unsigned long long bk[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) bk[m] = 0ull;
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < RPW; r++) {
+        const int i = row0 + r;
+        if (i < n_logical) {
+          const uint32_t pr = (uint32_t)prow[r];
+          const bool allowed = (pr >= a.allow_lo && pr <= a.allow_hi) || (pr >= a.stop_lo && pr < a.stop_hi);
+#pragma unroll
+          for (int m = 0; m < M; m++)
+            if (m < a.M) {
+              float v = acc[r][m];
+              if (a.bias) v = __fadd_rn(v, a.bias[pr]);
+              if (a.y) a.y[(size_t)m * a.ldy + pr] = v;
+              if (allowed) {
+                const unsigned long long key = argmax_key(v, pr);
+                bk[m] = key > bk[m] ? key : bk[m];
+              }
+            }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; m++) best[warp][m] = bk[m];
+    }
+    __syncthreads();
+    if (threadIdx.x < a.M && threadIdx.x < M) {
+      unsigned long long b = 0ull;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) b = best[w][threadIdx.x] > b ? best[w][threadIdx.x] : b;
+      if (b != 0ull) {
+        unsigned long long* dst = a.amax + threadIdx.x;
+        if (b > *(volatile unsigned long long*)dst) atomicMax(dst, b);
+      }
+    }
+  } else {
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < RPW; r++) {
+        const int i = row0 + r;
+        if (i < n_logical) {
+          const int pr = prow[r];
+#pragma unroll
+          for (int m = 0; m < M; m++)
+            if (m < a.M) {
+              float v = acc[r][m];
+              if (a.bias) v = __fadd_rn(v, a.bias[pr]);
+              float* dst = a.y + (size_t)m * a.ldy + pr;
+              if constexpr (EPI == EPI_ADD)
+                *dst = __fadd_rn(*dst, v);
+              else
+                *dst = v;
+            }
+        }
+      }
+    }
+  }
+}
+
+template <int WT, int M, int RPW, int UNROLL, int EPI>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
+  const int n_logical = a.n_range + a.n_extra;
+  const int rows_per_cta = kWarps * RPW;
+  const int K = (int)a.w.cols;
+  size_t smem = (size_t)M * K * sizeof(float);
+  if (WT == SX_DTYPE_Q4_K) smem += (size_t)M * (K / 16) * sizeof(float);
+  auto kern = k_gemv<WT, M, RPW, UNROLL, EPI>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((n_logical + rows_per_cta - 1) / rows_per_cta);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int WT, int M>
+cudaError_t dispatch_epi(const GemvArgs& a, Epi epi, cudaStream_t st) {
+  // Q8_0: 2 rows per warp, 4 chunks (2 KB of weights per warp) in flight.
+  constexpr int U = WT == SX_DTYPE_F32 ? 8 : (WT == SX_DTYPE_Q4_K ? 2 : 4);
+  switch (epi) {
+    case EPI_STORE: return launch_t<WT, M, 2, U, EPI_STORE>(a, st);
+    case EPI_ADD: return launch_t<WT, M, 2, U, EPI_ADD>(a, st);
+    case EPI_SWIGLU: return launch_t<WT, M, 2, U, EPI_SWIGLU>(a, st);
+    case EPI_ARGMAX: return launch_t<WT, M, 2, U, EPI_ARGMAX>(a, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int WT>
+cudaError_t dispatch_m(const GemvArgs& a, Epi epi, cudaStream_t st) {
+  if (a.M <= 1) return dispatch_epi<WT, 1>(a, epi, st);
+  if (a.M <= 2) return dispatch_epi<WT, 2>(a, epi, st);
+  if (a.M <= 4) return dispatch_epi<WT, 4>(a, epi, st);
+  return dispatch_epi<WT, 8>(a, epi, st);
+}
+
+}  // namespace
+
+cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
+  if (a.M < 1 || a.M > kMaxTok || a.n_range + a.n_extra < 1) return cudaErrorInvalidValue;
+  // x of all M tokens is staged in shared memory; split the tokens when it does not fit
+  const size_t K = (size_t)a.w.cols;
+  const size_t per_tok = K * 4 + (a.w.dtype == SX_DTYPE_Q4_K ? (K / 16) * 4 : 0);
+  const int max_m = (int)std::max<size_t>(1, std::min<size_t>(kMaxTok, (200 * 1024) / per_tok));
+  for (int m0 = 0; m0 < a.M; m0 += max_m) {
+    GemvArgs b = a;
+    b.M = std::min(max_m, a.M - m0);
+    b.x = a.x + (size_t)m0 * K;
+    if (a.y) b.y = a.y + (size_t)m0 * a.ldy;
+    if (a.amax) b.amax = a.amax + m0;
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (a.w.dtype) {
+      case SX_DTYPE_Q8_0: e = dispatch_m<SX_DTYPE_Q8_0>(b, epi, st); break;
+      case SX_DTYPE_Q4_K: e = dispatch_m<SX_DTYPE_Q4_K>(b, epi, st); break;
+      case SX_DTYPE_F32: e = dispatch_m<SX_DTYPE_F32>(b, epi, st); break;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace sx

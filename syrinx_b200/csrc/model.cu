@@ -1,0 +1,956 @@
+// model.cu — model upload/repack, sessions, and the decode orchestration on one GPU.
+//
+// The per-layer kernel sequence (5 launches, all programmatic-dependent):
+//   1 gemv  wqkv   prologue RMSNorm(attention_norm), + qkv bias        (s2/nn.rs:309-313)
+//   2 attn  QK-norm, RoPE, KV append, split-K GQA softmax(QK^T)V       (s2/nn.rs:315-352)
+//   3 gemv  wo     epilogue + bias, residual add                        (s2/slow_ar.rs:195)
+//   4 gemv  w1|w3  prologue RMSNorm(ffn_norm), epilogue SiLU(g)*u      (s2/nn.rs:452-456)
+//   5 gemv  w2     epilogue residual add                                (s2/slow_ar.rs:198)
+// A greedy frame (head -> semantic -> fast AR x C -> MCF embed -> slow stack -> advance)
+// is captured once into a CUDA graph and replayed per frame with no host round trip
+// (the driver loop of crates/syrinx-fish/src/common/dualar.rs:188-219 with top_k = 1).
+#include "model.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "sx_internal.hpp"
+
+namespace sx {
+
+size_t DevMat::bytes() const {
+  switch (dtype) {
+    case SX_DTYPE_Q8_0: return (size_t)rows * cols + (size_t)rows * (cols / 32) * 2;
+    case SX_DTYPE_Q4_K: return (size_t)rows * cols / 2 + (size_t)rows * (cols / 256) * 16;
+    case SX_DTYPE_F32: return (size_t)rows * cols * 4;
+  }
+  return 0;
+}
+
+namespace {
+
+#define SX_CU(expr)                                                                   \
+  do {                                                                                \
+    cudaError_t e_ = (expr);                                                          \
+    if (e_ != cudaSuccess) {                                                          \
+      set_error(std::string(#expr) + ": " + cudaGetErrorString(e_));                  \
+      return SX_E_CUDA;                                                               \
+    }                                                                                 \
+  } while (0)
+
+#define SX_RC(expr)        \
+  do {                     \
+    int rc_ = (expr);      \
+    if (rc_) return rc_;   \
+  } while (0)
+
+template <class T>
+int dalloc(std::vector<void*>& allocs, T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) count = 1;
+  cudaError_t e = cudaMalloc((void**)p, count * sizeof(T));
+  if (e != cudaSuccess) {
+    set_error(std::string("cudaMalloc(") + std::to_string(count * sizeof(T)) + "): " + cudaGetErrorString(e));
+    return SX_E_OOM;
+  }
+  allocs.push_back(*p);
+  return SX_OK;
+}
+
+int check_tdesc(const sx_transformer_desc& t, const char* what) {
+  if (t.dim <= 0 || t.n_layer < 0 || t.n_head <= 0 || t.n_local_heads <= 0 || t.intermediate_size <= 0) {
+    set_error(std::string(what) + ": non-positive dimension");
+    return SX_E_INVALID;
+  }
+  if (t.head_dim != 32 && t.head_dim != 64 && t.head_dim != 128) {
+    set_error(std::string(what) + ": head_dim must be 32, 64 or 128");
+    return SX_E_UNSUPPORTED;
+  }
+  if (t.n_head % t.n_local_heads || t.n_head / t.n_local_heads > kMaxGroup) {
+    set_error(std::string(what) + ": n_head must be a multiple (<= 8x) of n_local_heads");
+    return SX_E_UNSUPPORTED;
+  }
+  if (t.dim % 32 || t.intermediate_size % 32 || (t.n_head * t.head_dim) % 32) {
+    set_error(std::string(what) + ": dims must be multiples of 32");
+    return SX_E_UNSUPPORTED;
+  }
+  return SX_OK;
+}
+
+struct Loader {
+  sx_model* m;
+  BlobIndex idx;
+  uint8_t* staging = nullptr;
+  size_t staging_cap = 0;
+  ~Loader() {
+    if (staging) cudaFree(staging);
+  }
+
+  const BlobTensor* get(const std::string& name, int64_t rows, int64_t cols) {
+    auto it = idx.t.find(name);
+    if (it == idx.t.end()) {
+      set_error("weight blob: missing tensor " + name);
+      return nullptr;
+    }
+    if (it->second.rows != rows || it->second.cols != cols) {
+      set_error("weight blob: shape mismatch for " + name + " (expected " + std::to_string(rows) + "x" +
+                std::to_string(cols) + ")");
+      return nullptr;
+    }
+    return &it->second;
+  }
+
+  int vec(const std::string& name, int64_t n, float** out) {
+    const BlobTensor* t = get(name, 1, n);
+    if (!t) return SX_E_BLOB;
+    if (t->dtype != SX_DTYPE_F32) {
+      set_error("weight blob: " + name + " must be f32");
+      return SX_E_BLOB;
+    }
+    SX_RC(dalloc(m->allocs, out, (size_t)n));
+    SX_CU(cudaMemcpy(*out, t->data, (size_t)n * 4, cudaMemcpyHostToDevice));
+    m->weight_bytes += (size_t)n * 4;
+    return SX_OK;
+  }
+
+  // Upload `name` [rows x cols] into dst at destination rows r*row_mul + row_add;
+  // dst spans total_rows rows and is allocated on first use.
+  int mat(const std::string& name, int64_t rows, int64_t cols, DevMat* dst, int64_t total_rows,
+          int row_mul = 1, int row_add = 0) {
+    const BlobTensor* t = get(name, rows, cols);
+    if (!t) return SX_E_BLOB;
+    if (t->dtype != SX_DTYPE_Q8_0 && t->dtype != SX_DTYPE_Q4_K && t->dtype != SX_DTYPE_F32) {
+      set_error("weight blob: " + name + " has an unsupported dtype (Q8_0, Q4_K or F32)");
+      return SX_E_UNSUPPORTED;
+    }
+    if (dst->dtype < 0) {
+      dst->dtype = t->dtype;
+      dst->rows = total_rows;
+      dst->cols = cols;
+      if (t->dtype == SX_DTYPE_Q8_0) {
+        int8_t* q;
+        SX_RC(dalloc(m->allocs, &q, (size_t)total_rows * cols));
+        SX_RC(dalloc(m->allocs, &dst->s, (size_t)total_rows * (cols / 32)));
+        dst->q = q;
+      } else if (t->dtype == SX_DTYPE_Q4_K) {
+        uint8_t* q;
+        SX_RC(dalloc(m->allocs, &q, (size_t)total_rows * cols / 2));
+        SX_RC(dalloc(m->allocs, &dst->meta, (size_t)total_rows * (cols / 256) * 16));
+        dst->q = q;
+      } else {
+        float* q;
+        SX_RC(dalloc(m->allocs, &q, (size_t)total_rows * cols));
+        dst->q = q;
+      }
+      m->weight_bytes += dst->bytes();
+    } else if (dst->dtype != t->dtype) {
+      set_error("weight blob: " + name + " dtype differs from its fused partner");
+      return SX_E_BLOB;
+    }
+    if (t->dtype == SX_DTYPE_F32) {
+      SX_CU(cudaMemcpy2D((float*)dst->q + (size_t)row_add * cols, (size_t)row_mul * cols * 4, t->data,
+                         (size_t)cols * 4, (size_t)cols * 4, (size_t)rows, cudaMemcpyHostToDevice));
+      return SX_OK;
+    }
+    if (t->nbytes > staging_cap) {
+      if (staging) cudaFree(staging);
+      staging = nullptr;
+      SX_CU(cudaMalloc((void**)&staging, t->nbytes));
+      staging_cap = t->nbytes;
+    }
+    SX_CU(cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
+    if (t->dtype == SX_DTYPE_Q8_0)
+      SX_CU(repack_q8_0(staging, rows, cols, (int8_t*)dst->q, dst->s, row_mul, row_add, 0));
+    else
+      SX_CU(repack_q4_k(staging, rows, cols, (uint8_t*)dst->q, dst->meta, row_mul, row_add, 0));
+    SX_CU(cudaStreamSynchronize(0));
+    return SX_OK;
+  }
+
+  int layers(const sx_transformer_desc& td, const char* prefix, std::vector<DevLayer>* out) {
+    const int64_t qkv = (int64_t)(td.n_head + 2 * td.n_local_heads) * td.head_dim;
+    for (int l = 0; l < td.n_layer; l++) {
+      const std::string p = std::string(prefix) + "." + std::to_string(l) + ".";
+      DevLayer L;
+      SX_RC(vec(p + "attention_norm.weight", td.dim, &L.attn_norm));
+      SX_RC(mat(p + "attention.wqkv.weight", qkv, td.dim, &L.wqkv, qkv));
+      if (td.qkv_bias) SX_RC(vec(p + "attention.wqkv.bias", qkv, &L.bqkv));
+      if (td.qk_norm) {
+        SX_RC(vec(p + "attention.q_norm.weight", td.head_dim, &L.qn));
+        SX_RC(vec(p + "attention.k_norm.weight", td.head_dim, &L.kn));
+      }
+      SX_RC(mat(p + "attention.wo.weight", td.dim, (int64_t)td.n_head * td.head_dim, &L.wo, td.dim));
+      if (td.o_bias) SX_RC(vec(p + "attention.wo.bias", td.dim, &L.bo));
+      SX_RC(vec(p + "ffn_norm.weight", td.dim, &L.ffn_norm));
+      const int64_t F = td.intermediate_size;
+      SX_RC(mat(p + "feed_forward.w1.weight", F, td.dim, &L.w13, 2 * F, 2, 0));
+      SX_RC(mat(p + "feed_forward.w3.weight", F, td.dim, &L.w13, 2 * F, 2, 1));
+      SX_RC(mat(p + "feed_forward.w2.weight", td.dim, F, &L.w2, td.dim));
+      out->push_back(L);
+    }
+    return SX_OK;
+  }
+};
+
+// RoPE inverse frequencies 1 / base^(2i/hd) evaluated in f32 on the host, as the
+// reference tables are (s2/nn.rs:125-127, cv2/attention.rs:110-112).
+int upload_inv_freq(sx_model* m, const sx_transformer_desc& td, float** out) {
+  std::vector<float> f(td.head_dim / 2);
+  for (int i = 0; i < td.head_dim / 2; i++)
+    f[i] = 1.0f / std::pow(td.rope_base, (2.0f * (float)i) / (float)td.head_dim);
+  SX_RC(dalloc(m->allocs, out, f.size()));
+  SX_CU(cudaMemcpy(*out, f.data(), f.size() * 4, cudaMemcpyHostToDevice));
+  return SX_OK;
+}
+
+}  // namespace
+
+int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out) {
+  if (!desc || !blob || !out) {
+    set_error("sx_model_create: null argument");
+    return SX_E_INVALID;
+  }
+  const sx_model_desc& d = *desc;
+  SX_RC(check_tdesc(d.slow, "slow"));
+  if (d.fast.n_layer > 0) {
+    SX_RC(check_tdesc(d.fast, "fast"));
+    if (d.fast.dim != d.slow.dim) {
+      set_error("fast.dim != slow.dim needs fast_project_in, which this build does not load");
+      return SX_E_UNSUPPORTED;
+    }
+    if (d.num_codebooks < 2 || d.codebook_size <= 0) {
+      set_error("a fast AR needs num_codebooks >= 2 and codebook_size > 0");
+      return SX_E_INVALID;
+    }
+  }
+  if (d.num_codebooks < 0 || d.num_codebooks > 64 || d.vocab_size <= 0 || d.num_stop_tokens < 0 ||
+      d.num_stop_tokens > 4 || d.semantic_end_id < d.semantic_begin_id) {
+    set_error("sx_model_desc: bad vocab / codebook / stop configuration");
+    return SX_E_INVALID;
+  }
+  int ndev = 0;
+  SX_CU(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) {
+    set_error("sx_model_create: no such CUDA device");
+    return SX_E_INVALID;
+  }
+  SX_CU(cudaSetDevice(device));
+  auto m = new sx_model();
+  m->d = d;
+  m->device = device;
+  Loader L{m};
+  std::string err;
+  int rc = parse_blob(blob, size, &L.idx, &err);
+  if (rc) {
+    set_error(err);
+    delete m;
+    return rc;
+  }
+  auto fail = [&](int r) {
+    model_destroy(m);
+    return r;
+  };
+  if ((rc = L.layers(d.slow, "layers", &m->slow))) return fail(rc);
+  if ((rc = L.mat("embeddings.weight", d.vocab_size, d.slow.dim, &m->emb, d.vocab_size))) return fail(rc);
+  if ((rc = L.vec("norm.weight", d.slow.dim, &m->norm))) return fail(rc);
+  if (d.tie_word_embeddings) {
+    m->out_w = m->emb;
+  } else if ((rc = L.mat("output.weight", d.vocab_size, d.slow.dim, &m->out_w, d.vocab_size))) {
+    return fail(rc);
+  }
+  if (d.head_bias && (rc = L.vec("output.bias", d.vocab_size, &m->out_b))) return fail(rc);
+  if (d.num_codebooks > 0) {
+    const int64_t n = (int64_t)d.num_codebooks * d.codebook_size;
+    if ((rc = L.mat("codebook_embeddings.weight", n, d.slow.dim, &m->cb_emb, n))) return fail(rc);
+  }
+  if (d.fast.n_layer > 0) {
+    if ((rc = L.layers(d.fast, "fast_layers", &m->fast))) return fail(rc);
+    if ((rc = L.vec("fast_norm.weight", d.fast.dim, &m->fast_norm))) return fail(rc);
+    if ((rc = L.mat("fast_output.weight", d.codebook_size, d.fast.dim, &m->fast_out, d.codebook_size)))
+      return fail(rc);
+    if ((rc = L.mat("fast_embeddings.weight", d.codebook_size, d.fast.dim, &m->fast_emb, d.codebook_size)))
+      return fail(rc);
+  }
+  if ((rc = upload_inv_freq(m, d.slow, &m->inv_slow))) return fail(rc);
+  if (d.fast.n_layer > 0 && (rc = upload_inv_freq(m, d.fast, &m->inv_fast))) return fail(rc);
+  *out = m;
+  return SX_OK;
+}
+
+void model_destroy(sx_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+}
+
+// ---------------------------------------------------------------------------------------
+// sessions
+// ---------------------------------------------------------------------------------------
+int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out) {
+  if (!m || !out || max_batch < 1 || max_batch > kMaxTok || max_ctx < 1) {
+    set_error("sx_session_create: max_batch must be 1..8 and max_ctx >= 1");
+    return SX_E_INVALID;
+  }
+  SX_CU(cudaSetDevice(m->device));
+  const sx_model_desc& d = m->d;
+  auto s = new sx_session();
+  s->m = m;
+  s->max_batch = max_batch;
+  s->max_ctx = max_ctx;
+  s->len.assign(max_batch, 0);
+  auto fail = [&](int r) {
+    session_destroy(s);
+    return r;
+  };
+  if (cudaStreamCreateWithFlags(&s->own_st, cudaStreamNonBlocking) != cudaSuccess) {
+    set_error("cudaStreamCreate failed");
+    return fail(SX_E_CUDA);
+  }
+  s->st = s->own_st;
+  const auto& sl = d.slow;
+  s->pages_per_seq = (max_ctx + kPage - 1) / kPage;
+  s->n_pages = max_batch * s->pages_per_seq;
+  s->kv_layer_elems = (size_t)2 * s->n_pages * sl.n_local_heads * kPage * sl.head_dim;
+  int rc;
+  if ((rc = dalloc(s->allocs, &s->kv, s->kv_layer_elems * sl.n_layer))) return fail(rc);
+  if ((rc = dalloc(s->allocs, &s->page_table, (size_t)s->n_pages))) return fail(rc);
+  {
+    std::vector<int> pt(s->n_pages);
+    for (int i = 0; i < s->n_pages; i++) pt[i] = i;  // sequence b owns pages [b*pps, (b+1)*pps)
+    if (cudaMemcpy(s->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(SX_E_CUDA);
+  }
+  const int C = d.num_codebooks;
+  const bool has_fast = d.fast.n_layer > 0;
+  if (has_fast) {
+    const auto& f = d.fast;
+    s->fkv_layer_elems = (size_t)2 * max_batch * f.n_local_heads * kPage * f.head_dim;
+    if ((rc = dalloc(s->allocs, &s->fkv, s->fkv_layer_elems * f.n_layer))) return fail(rc);
+    if ((rc = dalloc(s->allocs, &s->fpage_table, (size_t)max_batch))) return fail(rc);
+    std::vector<int> pt(max_batch);
+    for (int i = 0; i < max_batch; i++) pt[i] = i;
+    if (cudaMemcpy(s->fpage_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(SX_E_CUDA);
+  }
+  const int width = 1 + C;
+  auto qkv_w = [](const sx_transformer_desc& t) { return (t.n_head + 2 * t.n_local_heads) * t.head_dim; };
+  const int max_qkv = std::max(qkv_w(sl), has_fast ? qkv_w(d.fast) : 0);
+  const int max_att = std::max(sl.n_head * sl.head_dim, has_fast ? d.fast.n_head * d.fast.head_dim : 0);
+  const int max_F = std::max(sl.intermediate_size, has_fast ? d.fast.intermediate_size : 0);
+  const int dim = sl.dim;
+  s->ring_frames = max_ctx;
+  const size_t part_slow = (size_t)kMaxTok * sl.n_local_heads * kMaxSplit * (sl.n_head / sl.n_local_heads) * (sl.head_dim + 2);
+  const size_t part_fast =
+      has_fast ? (size_t)kMaxTok * d.fast.n_local_heads * kMaxSplit * (d.fast.n_head / d.fast.n_local_heads) * (d.fast.head_dim + 2) : 0;
+  const int max_hkv = std::max(sl.n_local_heads, has_fast ? d.fast.n_local_heads : 0);
+  if ((rc = dalloc(s->allocs, &s->tok_seq, kMaxTok)) || (rc = dalloc(s->allocs, &s->tok_pos, kMaxTok)) ||
+      (rc = dalloc(s->allocs, &s->ptok_seq, kMaxTok)) || (rc = dalloc(s->allocs, &s->ptok_pos, kMaxTok)) ||
+      (rc = dalloc(s->allocs, &s->seq_len, max_batch)) || (rc = dalloc(s->allocs, &s->done, max_batch)) ||
+      (rc = dalloc(s->allocs, &s->frame_count, max_batch)) || (rc = dalloc(s->allocs, &s->err, 1)) ||
+      (rc = dalloc(s->allocs, &s->frames, (size_t)max_batch * width)) ||
+      (rc = dalloc(s->allocs, &s->ring, (size_t)s->ring_frames * max_batch * width)) ||
+      (rc = dalloc(s->allocs, &s->prompt, (size_t)width * max_ctx)) ||
+      (rc = dalloc(s->allocs, &s->h, (size_t)max_batch * dim)) ||
+      (rc = dalloc(s->allocs, &s->hp, (size_t)kMaxTok * dim)) ||
+      (rc = dalloc(s->allocs, &s->fx, (size_t)max_batch * dim)) ||
+      (rc = dalloc(s->allocs, &s->xqkv, (size_t)kMaxTok * max_qkv)) ||
+      (rc = dalloc(s->allocs, &s->attn, (size_t)kMaxTok * max_att)) ||
+      (rc = dalloc(s->allocs, &s->act, (size_t)kMaxTok * max_F)) ||
+      (rc = dalloc(s->allocs, &s->logits, (size_t)max_batch * d.vocab_size)) ||
+      (rc = dalloc(s->allocs, &s->fast_logits, (size_t)max_batch * std::max(1, d.codebook_size))) ||
+      (rc = dalloc(s->allocs, &s->hidden, (size_t)max_batch * dim)) ||
+      (rc = dalloc(s->allocs, &s->amax, (size_t)max_batch)) ||
+      (rc = dalloc(s->allocs, &s->part, std::max(part_slow, part_fast))) ||
+      (rc = dalloc(s->allocs, &s->counters, (size_t)kMaxTok * max_hkv)))
+    return fail(rc);
+  if (cudaMemset(s->counters, 0, (size_t)kMaxTok * max_hkv * 4) != cudaSuccess ||
+      cudaMemset(s->amax, 0, (size_t)max_batch * 8) != cudaSuccess ||
+      cudaMemset(s->err, 0, 4) != cudaSuccess || cudaMemset(s->frames, 0, (size_t)max_batch * width * 4) != cudaSuccess)
+    return fail(SX_E_CUDA);
+  *out = s;
+  return SX_OK;
+}
+
+void session_destroy(sx_session* s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  if (s->st) cudaStreamSynchronize(s->st);
+  if (s->own_st) cudaStreamSynchronize(s->own_st);
+  for (auto& g : s->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  for (void* p : s->allocs) cudaFree(p);
+  if (s->own_st) cudaStreamDestroy(s->own_st);
+  delete s;
+}
+
+int session_reset(sx_session* s) {
+  std::fill(s->len.begin(), s->len.end(), 0);
+  return SX_OK;
+}
+
+namespace {
+
+int n_split_for(const sx_session* s, int M, int Hkv) {
+  int S = std::max(1, (2 * 148) / std::max(1, M * Hkv));
+  S = std::min(S, kMaxSplit);
+  S = std::min(S, std::max(1, s->max_ctx / 32));
+  return S;
+}
+
+int gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
+  SX_CU(launch_gemv(a, epi, st));
+  return SX_OK;
+}
+
+// One transformer stack over M tokens. resid [M][dim] is updated in place.
+int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos,
+              int const_pos, bool append) {
+  sx_model* m = s->m;
+  const sx_transformer_desc& td = fast ? m->d.fast : m->d.slow;
+  const std::vector<DevLayer>& layers = fast ? m->fast : m->slow;
+  const int qkv_w = (td.n_head + 2 * td.n_local_heads) * td.head_dim;
+  const size_t layer_elems = fast ? s->fkv_layer_elems : s->kv_layer_elems;
+  const size_t half = layer_elems / 2;
+  for (size_t l = 0; l < layers.size(); l++) {
+    const DevLayer& L = layers[l];
+    GemvArgs g;
+    g.w = L.wqkv;
+    g.x = resid;
+    g.norm_w = L.attn_norm;
+    g.eps = td.norm_eps;
+    g.bias = L.bqkv;
+    g.y = s->xqkv;
+    g.ldy = qkv_w;
+    g.M = M;
+    g.n_range = qkv_w;
+    SX_RC(gemv(g, EPI_STORE, s->st));
+
+    AttnArgs a;
+    a.qkv = s->xqkv;
+    a.out = s->attn;
+    __nv_bfloat16* base = (fast ? s->fkv : s->kv) + l * layer_elems;
+    a.kbase = base;
+    a.vbase = base + half;
+    a.page_table = fast ? s->fpage_table : s->page_table;
+    a.pt_stride = fast ? 1 : s->pages_per_seq;
+    a.tok_seq = tok_seq;
+    a.tok_pos = tok_pos;
+    a.const_pos = const_pos;
+    a.qn = L.qn;
+    a.kn = L.kn;
+    a.eps = td.norm_eps;
+    a.inv_freq = fast ? m->inv_fast : m->inv_slow;
+    a.interleaved = td.rope_interleaved;
+    a.scale = (float)(1.0 / std::sqrt((double)td.head_dim));
+    a.H = td.n_head;
+    a.Hkv = td.n_local_heads;
+    a.hd = td.head_dim;
+    a.n_split = fast ? 1 : n_split_for(s, M, td.n_local_heads);
+    a.append = append ? 1 : 0;
+    a.part = s->part;
+    a.counters = s->counters;
+    a.M = M;
+    if (!append) SX_CU(launch_kv_append(a, s->st));
+    SX_CU(launch_attention(a, s->st));
+
+    GemvArgs o;
+    o.w = L.wo;
+    o.x = s->attn;
+    o.bias = L.bo;
+    o.y = resid;
+    o.ldy = td.dim;
+    o.M = M;
+    o.n_range = td.dim;
+    SX_RC(gemv(o, EPI_ADD, s->st));
+
+    GemvArgs f;
+    f.w = L.w13;
+    f.x = resid;
+    f.norm_w = L.ffn_norm;
+    f.eps = td.norm_eps;
+    f.y = s->act;
+    f.ldy = td.intermediate_size;
+    f.M = M;
+    f.n_range = 2 * td.intermediate_size;
+    SX_RC(gemv(f, EPI_SWIGLU, s->st));
+
+    GemvArgs w2;
+    w2.w = L.w2;
+    w2.x = s->act;
+    w2.y = resid;
+    w2.ldy = td.dim;
+    w2.M = M;
+    w2.n_range = td.dim;
+    SX_RC(gemv(w2, EPI_ADD, s->st));
+  }
+  return SX_OK;
+}
+
+int upload_tokens(sx_session* s, int* dseq, int* dpos, const std::vector<int>& seq, const std::vector<int>& pos) {
+  SX_CU(cudaMemcpyAsync(dseq, seq.data(), seq.size() * 4, cudaMemcpyHostToDevice, s->st));
+  SX_CU(cudaMemcpyAsync(dpos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, s->st));
+  return SX_OK;
+}
+
+int check_err(sx_session* s) {
+  int e = 0;
+  SX_CU(cudaMemcpyAsync(&e, s->err, 4, cudaMemcpyDeviceToHost, s->st));
+  SX_CU(cudaStreamSynchronize(s->st));
+  if (e) {
+    SX_CU(cudaMemsetAsync(s->err, 0, 4, s->st));
+    SX_CU(cudaStreamSynchronize(s->st));
+    set_error("token id or codebook code out of range");
+    return SX_E_INVALID;
+  }
+  return SX_OK;
+}
+
+EmbedArgs embed_args(sx_session* s) {
+  const sx_model_desc& d = s->m->d;
+  EmbedArgs e;
+  e.emb = s->m->emb;
+  e.cb_emb = s->m->cb_emb;
+  e.dim = d.slow.dim;
+  e.C = d.num_codebooks;
+  e.R = d.codebook_size;
+  e.vocab = d.vocab_size;
+  e.sem_lo = d.semantic_begin_id;
+  e.sem_hi = d.semantic_end_id;
+  e.scale_cb = d.scale_codebook_embeddings;
+  e.err = s->err;
+  return e;
+}
+
+}  // namespace
+
+int prefill_seq(sx_session* s, int seq, const uint32_t* prompt, int T) {
+  const sx_model_desc& d = s->m->d;
+  const int rows = 1 + d.num_codebooks;
+  if (T <= 0) {
+    set_error("prefill: empty prompt");
+    return SX_E_INVALID;
+  }
+  if (s->len[seq] + T > s->max_ctx) {
+    set_error("prefill: prompt exceeds the session's max_ctx");
+    return SX_E_RANGE;
+  }
+  SX_CU(cudaMemcpyAsync(s->prompt, prompt, (size_t)rows * T * 4, cudaMemcpyHostToDevice, s->st));
+  const int base = s->len[seq];
+  int last_M = 0;
+  for (int c0 = 0; c0 < T; c0 += kMaxTok) {
+    const int M = std::min(kMaxTok, T - c0);
+    std::vector<int> ts(M, seq), tp(M);
+    for (int i = 0; i < M; i++) tp[i] = base + c0 + i;
+    SX_RC(upload_tokens(s, s->ptok_seq, s->ptok_pos, ts, tp));
+    EmbedArgs e = embed_args(s);
+    e.ids = s->prompt;
+    e.T = T;
+    e.t0 = c0;
+    e.h = s->hp;
+    e.M = M;
+    SX_CU(launch_embed(e, s->st));
+    SX_RC(run_stack(s, false, M, s->hp, s->ptok_seq, s->ptok_pos, 0, false));
+    last_M = M;
+  }
+  SX_CU(cudaMemcpyAsync(s->h + (size_t)seq * d.slow.dim, s->hp + (size_t)(last_M - 1) * d.slow.dim,
+                        (size_t)d.slow.dim * 4, cudaMemcpyDeviceToDevice, s->st));
+  SX_RC(check_err(s));
+  s->len[seq] = base + T;
+  return SX_OK;
+}
+
+int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n) {
+  const sx_model_desc& d = s->m->d;
+  const int width = 1 + d.num_codebooks;
+  std::vector<int> ts(n), tp(n);
+  for (int i = 0; i < n; i++) {
+    if (seqs[i] != i) {
+      set_error("slow_step: token i must be sequence i");
+      return SX_E_INVALID;
+    }
+    if (s->len[i] <= 0) {
+      set_error("slow_step before prefill");
+      return SX_E_STATE;
+    }
+    if (s->len[i] + 1 > s->max_ctx) {
+      set_error("slow_step: context exceeds the session's max_ctx");
+      return SX_E_RANGE;
+    }
+    ts[i] = i;
+    tp[i] = s->len[i];
+  }
+  SX_CU(cudaMemcpyAsync(s->frames, frames, (size_t)n * width * 4, cudaMemcpyHostToDevice, s->st));
+  SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+  EmbedArgs e = embed_args(s);
+  e.tok_seq = s->tok_seq;
+  e.frames = s->frames;
+  e.frame_stride = width;
+  e.h = s->h;
+  e.M = n;
+  SX_CU(launch_embed(e, s->st));
+  SX_RC(run_stack(s, false, n, s->h, s->tok_seq, s->tok_pos, 0, true));
+  SX_RC(check_err(s));
+  for (int i = 0; i < n; i++) s->len[i] += 1;
+  return SX_OK;
+}
+
+int run_head(sx_session* s, int n, bool want_logits, bool want_argmax, bool mask_stop) {
+  sx_model* m = s->m;
+  const sx_model_desc& d = m->d;
+  GemvArgs g;
+  g.w = m->out_w;
+  g.x = s->h;
+  g.norm_w = m->norm;
+  g.eps = d.slow.norm_eps;
+  g.bias = m->out_b;
+  g.M = n;
+  const uint32_t sem_hi = std::min<uint32_t>(d.semantic_end_id, (uint32_t)d.vocab_size - 1);
+  if (want_logits) {
+    g.y = s->logits;
+    g.ldy = d.vocab_size;
+    g.n_range = d.vocab_size;
+  } else {
+    g.row_base = (int)d.semantic_begin_id;
+    g.n_range = (int)(sem_hi - d.semantic_begin_id + 1);
+    if (!mask_stop)
+      for (int i = 0; i < d.num_stop_tokens; i++) {
+        const uint32_t id = d.stop_token_id + i;
+        if ((id < d.semantic_begin_id || id > sem_hi) && id < (uint32_t)d.vocab_size) g.extra[g.n_extra++] = (int)id;
+      }
+  }
+  if (want_argmax) {
+    g.amax = s->amax;
+    g.allow_lo = d.semantic_begin_id;
+    g.allow_hi = sem_hi;
+    if (!mask_stop) {
+      g.stop_lo = d.stop_token_id;
+      g.stop_hi = d.stop_token_id + d.num_stop_tokens;
+    }
+    return gemv(g, EPI_ARGMAX, s->st);
+  }
+  return gemv(g, EPI_STORE, s->st);
+}
+
+int make_hidden(sx_session* s, int n) {
+  const sx_model_desc& d = s->m->d;
+  if (d.norm_fastlayer_input)
+    SX_CU(launch_final_norm(s->h, s->m->norm, d.slow.norm_eps, d.slow.dim, n, s->hidden, s->st));
+  else
+    SX_CU(cudaMemcpyAsync(s->hidden, s->h, (size_t)n * d.slow.dim * 4, cudaMemcpyDeviceToDevice, s->st));
+  return SX_OK;
+}
+
+namespace {
+
+FrameArgs frame_args(sx_session* s, int n) {
+  const sx_model_desc& d = s->m->d;
+  FrameArgs f;
+  f.M = n;
+  f.tok_seq = s->tok_seq;
+  f.frames = s->frames;
+  f.frame_stride = 1 + d.num_codebooks;
+  f.sem_begin = d.semantic_begin_id;
+  f.R = std::max(1, d.codebook_size);
+  f.dim = d.slow.dim;
+  return f;
+}
+
+int fast_head(sx_session* s, int n, Epi epi) {
+  sx_model* m = s->m;
+  GemvArgs g;
+  g.w = m->fast_out;
+  g.x = s->fx;
+  g.norm_w = m->fast_norm;
+  g.eps = m->d.fast.norm_eps;
+  g.M = n;
+  g.n_range = m->d.codebook_size;
+  if (epi == EPI_ARGMAX) {
+    g.amax = s->amax;
+    g.allow_lo = 0;
+    g.allow_hi = (uint32_t)m->d.codebook_size - 1;
+  } else {
+    g.y = s->fast_logits;
+    g.ldy = m->d.codebook_size;
+  }
+  return gemv(g, epi, s->st);
+}
+
+}  // namespace
+
+int fast_expand_rows(sx_session* s, int n, const int* /*seqs*/) {
+  sx_model* m = s->m;
+  const int C = m->d.num_codebooks;
+  SX_RC(run_stack(s, true, n, s->fx, s->tok_seq, nullptr, 0, true));
+  FrameArgs f = frame_args(s, n);
+  f.slot = 1;
+  f.emb = m->fast_emb;
+  f.x = s->fx;
+  SX_CU(launch_take_code(f, s->st));
+  for (int cb = 1; cb < C; cb++) {
+    SX_RC(run_stack(s, true, n, s->fx, s->tok_seq, nullptr, cb, true));
+    SX_RC(fast_head(s, n, EPI_ARGMAX));
+    FrameArgs t = frame_args(s, n);
+    t.amax = s->amax;
+    t.slot = 1 + cb;
+    if (cb < C - 1) {
+      t.emb = m->fast_emb;
+      t.x = s->fx;
+    }
+    SX_CU(launch_take_code(t, s->st));
+  }
+  return SX_OK;
+}
+
+int fast_expand_sampled(sx_session* s, uint32_t first_code, sx_sample_fn fn, void* user, uint32_t* codes_out) {
+  sx_model* m = s->m;
+  const sx_model_desc& d = m->d;
+  const int C = d.num_codebooks, R = d.codebook_size;
+  if (first_code >= (uint32_t)R) {
+    set_error("fast_expand: first_code out of range");
+    return SX_E_INVALID;
+  }
+  const std::vector<int> ts{0}, tp{s->len[0]};
+  SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+  SX_RC(make_hidden(s, 1));
+  SX_CU(cudaMemcpyAsync(s->fx, s->hidden, (size_t)d.slow.dim * 4, cudaMemcpyDeviceToDevice, s->st));
+  SX_CU(cudaMemcpyAsync(s->frames + 1, &first_code, 4, cudaMemcpyHostToDevice, s->st));
+  SX_RC(run_stack(s, true, 1, s->fx, s->tok_seq, nullptr, 0, true));
+  FrameArgs f = frame_args(s, 1);
+  f.slot = 1;
+  f.emb = m->fast_emb;
+  f.x = s->fx;
+  SX_CU(launch_take_code(f, s->st));
+  codes_out[0] = first_code;
+  std::vector<float> logits(R);
+  for (int cb = 1; cb < C; cb++) {
+    SX_RC(run_stack(s, true, 1, s->fx, s->tok_seq, nullptr, cb, true));
+    SX_RC(fast_head(s, 1, EPI_STORE));
+    SX_CU(cudaMemcpyAsync(logits.data(), s->fast_logits, (size_t)R * 4, cudaMemcpyDeviceToHost, s->st));
+    SX_CU(cudaStreamSynchronize(s->st));
+    const uint32_t code = fn(user, logits.data(), R);
+    if (code >= (uint32_t)R) {
+      set_error("fast_expand: sampler returned an out-of-range code");
+      return SX_E_INVALID;
+    }
+    codes_out[cb] = code;
+    if (cb < C - 1) {
+      SX_CU(cudaMemcpyAsync(s->frames + 1 + cb, &codes_out[cb], 4, cudaMemcpyHostToDevice, s->st));
+      FrameArgs t = frame_args(s, 1);
+      t.slot = 1 + cb;
+      t.emb = m->fast_emb;
+      t.x = s->fx;
+      SX_CU(launch_take_code(t, s->st));
+    }
+  }
+  SX_CU(cudaStreamSynchronize(s->st));
+  return SX_OK;
+}
+
+namespace {
+
+// head -> semantic -> (fast AR) for rows [0, n): leaves the frame in s->frames
+int greedy_frame_front(sx_session* s, int n, int mask_stop) {
+  sx_model* m = s->m;
+  const sx_model_desc& d = m->d;
+  SX_RC(run_head(s, n, false, true, mask_stop != 0));
+  FrameArgs f = frame_args(s, n);
+  f.amax = s->amax;
+  f.slot = 0;
+  f.write_first_code = d.num_codebooks > 0;
+  f.done = s->done;
+  f.stop_lo = d.stop_token_id;
+  f.stop_hi = d.stop_token_id + d.num_stop_tokens;
+  if (d.fast.n_layer > 0) {
+    f.x = s->fx;
+    f.h_last = s->h;
+    f.norm_w = d.norm_fastlayer_input ? m->norm : nullptr;
+    f.eps = d.slow.norm_eps;
+  }
+  SX_CU(launch_take_semantic(f, s->st));
+  if (d.fast.n_layer > 0) SX_RC(fast_expand_rows(s, n, nullptr));
+  return SX_OK;
+}
+
+int build_graph(sx_session* s, int n, int mask_stop, cudaGraphExec_t* exec) {
+  const sx_model_desc& d = s->m->d;
+  const int width = 1 + d.num_codebooks;
+  SX_CU(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+  auto body = [&]() -> int {
+    SX_RC(greedy_frame_front(s, n, mask_stop));
+    EmbedArgs e = embed_args(s);
+    e.tok_seq = s->tok_seq;
+    e.frames = s->frames;
+    e.frame_stride = width;
+    e.h = s->h;
+    e.M = n;
+    SX_CU(launch_embed(e, s->st));
+    SX_RC(run_stack(s, false, n, s->h, s->tok_seq, s->tok_pos, 0, true));
+    AdvanceArgs a;
+    a.M = n;
+    a.tok_seq = s->tok_seq;
+    a.tok_pos = s->tok_pos;
+    a.seq_len = s->seq_len;
+    a.done = s->done;
+    a.frames = s->frames;
+    a.frame_stride = width;
+    a.ring = s->ring;
+    a.ring_frames = s->ring_frames;
+    a.frame_count = s->frame_count;
+    a.batch = s->max_batch;
+    SX_CU(launch_advance(a, s->st));
+    return SX_OK;
+  };
+  int rc = body();
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s->st, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error(std::string("graph capture: ") + cudaGetErrorString(e));
+    return SX_E_CUDA;
+  }
+  e = cudaGraphInstantiateWithFlags(exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    set_error(std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return SX_E_CUDA;
+  }
+  return SX_OK;
+}
+
+}  // namespace
+
+int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* frames_out, int* n_frames_out) {
+  const sx_model_desc& d = s->m->d;
+  const int width = 1 + d.num_codebooks;
+  if (n < 1 || n > s->max_batch || n_frames < 0) {
+    set_error("decode_greedy: bad batch or frame count");
+    return SX_E_INVALID;
+  }
+  int max_len = 0;
+  for (int i = 0; i < n; i++) {
+    if (s->len[i] <= 0) {
+      set_error("decode_greedy before prefill");
+      return SX_E_STATE;
+    }
+    max_len = std::max(max_len, s->len[i]);
+  }
+  // each frame's trailing slow step writes position len + f
+  n_frames = std::min(n_frames, s->max_ctx - max_len);
+  n_frames = std::min(n_frames, s->ring_frames);
+  std::vector<int> ts(n), tp(n), zeros(n, 0);
+  for (int i = 0; i < n; i++) {
+    ts[i] = i;
+    tp[i] = s->len[i];
+  }
+  SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+  SX_CU(cudaMemcpyAsync(s->seq_len, tp.data(), n * 4, cudaMemcpyHostToDevice, s->st));
+  SX_CU(cudaMemcpyAsync(s->done, zeros.data(), n * 4, cudaMemcpyHostToDevice, s->st));
+  SX_CU(cudaMemcpyAsync(s->frame_count, zeros.data(), n * 4, cudaMemcpyHostToDevice, s->st));
+  GreedyGraph* gg = nullptr;
+  for (auto& g : s->graphs)
+    if (g.M == n && g.mask_stop == mask_stop) gg = &g;
+  if (!gg) {
+    GreedyGraph g;
+    g.M = n;
+    g.mask_stop = mask_stop;
+    SX_RC(build_graph(s, n, mask_stop, &g.exec));
+    s->graphs.push_back(g);
+    gg = &s->graphs.back();
+  }
+  for (int f = 0; f < n_frames; f++) SX_CU(cudaGraphLaunch(gg->exec, s->st));
+  std::vector<int> counts(n), lens(n);
+  SX_CU(cudaMemcpyAsync(counts.data(), s->frame_count, n * 4, cudaMemcpyDeviceToHost, s->st));
+  SX_CU(cudaMemcpyAsync(lens.data(), s->seq_len, n * 4, cudaMemcpyDeviceToHost, s->st));
+  std::vector<uint32_t> ring((size_t)std::max(1, n_frames) * s->max_batch * width);
+  if (n_frames > 0)
+    SX_CU(cudaMemcpyAsync(ring.data(), s->ring, (size_t)n_frames * s->max_batch * width * 4,
+                          cudaMemcpyDeviceToHost, s->st));
+  SX_CU(cudaStreamSynchronize(s->st));
+  for (int i = 0; i < n; i++) {
+    const int c = std::min(counts[i], n_frames);
+    if (n_frames_out) n_frames_out[i] = c;
+    s->len[i] = lens[i];
+    if (frames_out)
+      for (int f = 0; f < c; f++)
+        std::memcpy(frames_out + ((size_t)i * n_frames + f) * width, ring.data() + ((size_t)f * s->max_batch + i) * width,
+                    width * 4);
+  }
+  return SX_OK;
+}
+
+int profile_gemv(sx_session* s, int kind, int n_launches) {
+  sx_model* m = s->m;
+  const sx_transformer_desc& td = m->d.slow;
+  if (kind < 0 || kind > 3 || n_launches < 0 || m->slow.empty()) {
+    set_error("profile_gemv: kind must be 0..3");
+    return SX_E_INVALID;
+  }
+  for (int i = 0; i < n_launches; i++) {
+    const DevLayer& L = m->slow[i % m->slow.size()];
+    GemvArgs g;
+    g.M = 1;
+    Epi epi = EPI_STORE;
+    if (kind == 0) {
+      g.w = L.wqkv;
+      g.x = s->h;
+      g.norm_w = L.attn_norm;
+      g.eps = td.norm_eps;
+      g.bias = L.bqkv;
+      g.y = s->xqkv;
+      g.ldy = (int)L.wqkv.rows;
+      g.n_range = (int)L.wqkv.rows;
+    } else if (kind == 1) {
+      g.w = L.wo;
+      g.x = s->attn;
+      g.y = s->hp;
+      g.ldy = td.dim;
+      g.n_range = td.dim;
+    } else if (kind == 2) {
+      g.w = L.w13;
+      g.x = s->h;
+      g.norm_w = L.ffn_norm;
+      g.eps = td.norm_eps;
+      g.y = s->act;
+      g.ldy = td.intermediate_size;
+      g.n_range = 2 * td.intermediate_size;
+      epi = EPI_SWIGLU;
+    } else {
+      g.w = L.w2;
+      g.x = s->act;
+      g.y = s->hp;
+      g.ldy = td.dim;
+      g.n_range = td.dim;
+    }
+    SX_RC(gemv(g, epi, s->st));
+  }
+  return SX_OK;
+}
+
+int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, uint32_t* frame_out, int* stopped) {
+  const sx_model_desc& d = s->m->d;
+  const int width = 1 + d.num_codebooks;
+  if (s->len[0] <= 0) {
+    set_error("frame_step before prefill");
+    return SX_E_STATE;
+  }
+  if (frame_in) {
+    const int seq0 = 0;
+    SX_RC(slow_step_seqs(s, &seq0, frame_in, 1));
+  } else {
+    const std::vector<int> ts{0}, tp{s->len[0]};
+    SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+  }
+  SX_RC(greedy_frame_front(s, 1, mask_stop));
+  SX_CU(cudaMemcpyAsync(frame_out, s->frames, (size_t)width * 4, cudaMemcpyDeviceToHost, s->st));
+  SX_CU(cudaStreamSynchronize(s->st));
+  if (stopped)
+    *stopped = frame_out[0] >= d.stop_token_id && frame_out[0] < d.stop_token_id + (uint32_t)d.num_stop_tokens;
+  return SX_OK;
+}
+
+}  // namespace sx

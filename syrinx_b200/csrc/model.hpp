@@ -1,0 +1,100 @@
+// model.hpp — device model and decoding session of the B200 dual-AR path.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "blob.hpp"
+#include "sx_internal.hpp"
+
+struct sx_model {
+  sx_model_desc d{};
+  int device = 0;
+  std::vector<sx::DevLayer> slow, fast;
+  sx::DevMat emb, cb_emb, out_w, fast_out, fast_emb;
+  float* norm = nullptr;
+  float* out_b = nullptr;
+  float* fast_norm = nullptr;
+  float* inv_slow = nullptr;
+  float* inv_fast = nullptr;
+  std::vector<void*> allocs;
+  size_t weight_bytes = 0;
+};
+
+struct GreedyGraph {
+  cudaGraphExec_t exec = nullptr;
+  int M = 0;
+  int mask_stop = 0;
+};
+
+struct sx_session {
+  sx_model* m = nullptr;
+  int max_batch = 0, max_ctx = 0;
+  cudaStream_t st = nullptr;      // stream all work is enqueued on
+  cudaStream_t own_st = nullptr;  // the session's own stream (st unless a caller set one)
+  int pages_per_seq = 0, n_pages = 0;
+  __nv_bfloat16* kv = nullptr;   // slow: per layer [2][n_pages][Hkv][PAGE][hd]
+  __nv_bfloat16* fkv = nullptr;  // fast: per layer [2][max_batch][Hkv][PAGE][hd]
+  size_t kv_layer_elems = 0, fkv_layer_elems = 0;
+  int* page_table = nullptr;   // [max_batch][pages_per_seq]
+  int* fpage_table = nullptr;  // [max_batch][1]
+  // token lists: decode (graph state) and prefill chunks
+  int* tok_seq = nullptr;
+  int* tok_pos = nullptr;
+  int* ptok_seq = nullptr;
+  int* ptok_pos = nullptr;
+  int* seq_len = nullptr;
+  int* done = nullptr;
+  int* frame_count = nullptr;
+  int* err = nullptr;
+  uint32_t* frames = nullptr;  // [max_batch][1+C]
+  uint32_t* ring = nullptr;    // [ring_frames][max_batch][1+C]
+  int ring_frames = 0;
+  uint32_t* prompt = nullptr;  // [(1+C) * max_ctx]
+  // activations
+  float* h = nullptr;     // [max_batch][dim] decode residual (h_last after prefill)
+  float* hp = nullptr;    // [kMaxTok][dim] prefill residual
+  float* fx = nullptr;    // [max_batch][fast dim] fast residual
+  float* xqkv = nullptr;  // [kMaxTok][max qkv]
+  float* attn = nullptr;  // [kMaxTok][max H*hd]
+  float* act = nullptr;   // [kMaxTok][max F]
+  float* logits = nullptr;       // [max_batch][vocab]
+  float* fast_logits = nullptr;  // [max_batch][R]
+  float* hidden = nullptr;       // [max_batch][dim]
+  unsigned long long* amax = nullptr;  // [max_batch]
+  float* part = nullptr;
+  int* counters = nullptr;
+  std::vector<int> len;  // host mirror of per-sequence cache lengths
+  bool device_len_dirty = false;  // device seq_len advanced by a graph loop
+  std::vector<GreedyGraph> graphs;
+  std::vector<void*> allocs;
+};
+
+namespace sx {
+int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out);
+void model_destroy(sx_model* m);
+int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out);
+void session_destroy(sx_session* s);
+int session_reset(sx_session* s);
+int sync_lengths(sx_session* s);
+
+// prefill one sequence; leaves its last residual in s->h[seq]
+int prefill_seq(sx_session* s, int seq, const uint32_t* prompt, int T);
+// one slow step for n sequences (frames on the host, [n][1+C]); seqs[i] owns row i of s->h
+int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n);
+// head over h rows [0, n): full logits to s->logits (if want_logits) and/or the greedy
+// argmax over the semantic constraint into s->amax
+int run_head(sx_session* s, int n, bool want_logits, bool want_argmax, bool mask_stop);
+// fast-AR prefix hidden of rows [0, n) into s->hidden
+int make_hidden(sx_session* s, int n);
+// greedy fast AR for rows [0, n) with first codes already in frames[seq][1]
+int fast_expand_rows(sx_session* s, int n, const int* seqs);
+int fast_expand_sampled(sx_session* s, uint32_t first_code, sx_sample_fn fn, void* user,
+                        uint32_t* codes_out);
+int profile_gemv(sx_session* s, int kind, int n_launches);
+int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* frames_out,
+                  int* n_frames_out);
+int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, uint32_t* frame_out,
+                      int* stopped);
+}  // namespace sx

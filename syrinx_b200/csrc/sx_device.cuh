@@ -1,0 +1,102 @@
+// sx_device.cuh — device-side helpers shared by the sm_100a kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace sx {
+
+// ---- programmatic dependent launch (PDL) ---------------------------------------------
+// Every kernel of the decode chain is launched with programmatic stream serialization:
+// it may start while its predecessor drains, issue loads that do not depend on the
+// predecessor (weights), and must execute pdl_wait() before touching upstream data or
+// writing anything. Every CTA of every kernel executes pdl_wait() before it exits, which
+// keeps grid completion ordered along the stream.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- loads ------------------------------------------------------------------------------
+// Streaming 128-bit load of weights: read once per step, do not pollute L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// ---- packed f32x2 arithmetic (sm_100 FADD2/FFMA2: two lanes of IEEE f32 per issue) ------
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ unsigned long long pack2u(uint32_t lo, uint32_t hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                   unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// int8 x 4 (packed in a word) -> exact f32 values, two per f32x2 register.
+// Each byte b is biased to u = b ^ 0x80 = q + 128, placed in the low mantissa byte of
+// 2^23 (bit pattern 0x4B0000uu = 8388608 + u), and 8388736 = 2^23 + 128 is subtracted:
+// an exact integer conversion on the byte-permute and f32x2 pipes.
+__device__ __forceinline__ void i8x4_to_f32x2x2(uint32_t w, unsigned long long& lo,
+                                                unsigned long long& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const unsigned long long bias = 0xCB000080CB000080ull;  // {-8388736.f, -8388736.f}
+  lo = add2(pack2u(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541)), bias);
+  hi = add2(pack2u(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543)), bias);
+}
+
+// 4-bit values in bytes (each byte 0..15, packed in a word) -> exact f32, two per f32x2.
+__device__ __forceinline__ void u4x4_to_f32x2x2(uint32_t nib, unsigned long long& lo,
+                                                unsigned long long& hi) {
+  const unsigned long long bias = 0xCB000000CB000000ull;  // {-8388608.f, -8388608.f}
+  lo = add2(pack2u(__byte_perm(nib, 0x4B000000u, 0x7540), __byte_perm(nib, 0x4B000000u, 0x7541)), bias);
+  hi = add2(pack2u(__byte_perm(nib, 0x4B000000u, 0x7542), __byte_perm(nib, 0x4B000000u, 0x7543)), bias);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Total order on f32 as u32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t f32_order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+// Packed argmax key: max value first, then the LOWEST row on ties.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t row) {
+  return ((unsigned long long)f32_order_key(v) << 32) | (unsigned long long)(~row);
+}
+__device__ __forceinline__ uint32_t argmax_row(unsigned long long key) {
+  return ~(uint32_t)(key & 0xffffffffull);
+}
+
+__device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+}  // namespace sx

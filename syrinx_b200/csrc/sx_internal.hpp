@@ -1,0 +1,178 @@
+// sx_internal.hpp — device data layout and kernel launch interfaces of the B200 path.
+//
+// HBM layout (all device memory owned by the library):
+//   Q8_0 weight [N][K]  -> q : int8 [N][K] (row-major, one row = K bytes, 16-B aligned)
+//                          s : f16  [N][K/32] (block scales)
+//   Q4_K weight [N][K]  -> q : u8   [N][K/2] (GGML nibble order inside each 256 super-block)
+//                          meta : 16 B [N][K/256] = {f16 d, f16 dmin, u8 scales[12]}
+//   F32  weight [N][K]  -> f : f32 [N][K]
+//   The GGML array-of-blocks layout (34-B Q8_0 blocks are not 16-B aligned) is split into
+//   these structure-of-arrays forms at load, losslessly, so every GEMV lane issues 128-bit
+//   coalesced loads. w1/w3 are interleaved row by row (g0,u0,g1,u1,...) so one warp owns a
+//   gate/up pair and applies SiLU(g)*u in its epilogue.
+//   KV cache: bf16 pages of PAGE positions, per layer [2][n_pages][Hkv][PAGE][hd], with a
+//   per-sequence page table [max_batch][pages_per_seq] of int32 page ids.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/syrinx_dualar.h"
+
+namespace sx {
+
+constexpr int kPage = 64;         // KV positions per page
+constexpr int kMaxTok = 8;        // max tokens per GEMV launch (batched decode / prefill chunk)
+constexpr int kAttnThreads = 128;
+constexpr int kMaxSplit = 32;     // max split-K partitions of the attention sequence axis
+constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one CTA
+
+struct DevMat {
+  int dtype = -1;
+  int64_t rows = 0, cols = 0;
+  void* q = nullptr;     // Q8_0 int8 / Q4_K nibbles / F32 values
+  __half* s = nullptr;   // Q8_0 scales
+  uint8_t* meta = nullptr;  // Q4_K 16-B super-block headers
+  size_t bytes() const;
+};
+
+struct DevLayer {
+  float* attn_norm = nullptr;
+  float* bqkv = nullptr;
+  float* qn = nullptr;
+  float* kn = nullptr;
+  float* bo = nullptr;
+  float* ffn_norm = nullptr;
+  DevMat wqkv, wo, w13, w2;
+};
+
+// ---- kernel argument bundles --------------------------------------------------------
+
+enum Epi : int {
+  EPI_STORE = 0,   // y[m][row] = acc (+ bias[row])
+  EPI_ADD = 1,     // y[m][row] = y[m][row] + (acc (+ bias[row]))   (residual add)
+  EPI_SWIGLU = 2,  // rows (2j, 2j+1) = (gate_j, up_j): y[m][j] = silu(g) * u
+  EPI_ARGMAX = 3,  // logits (stored if y != null) + packed argmax over allowed rows
+};
+
+struct GemvArgs {
+  DevMat w;
+  const float* x = nullptr;  // [M][K] activations (row stride K)
+  const float* norm_w = nullptr;  // non-null: RMSNorm prologue with this gain over K
+  float eps = 0.f;
+  const float* bias = nullptr;  // [N] f32
+  float* y = nullptr;           // output (row stride ldy)
+  int ldy = 0;
+  int M = 1;
+  // logical -> physical row map (head over a row subset): i < n_range -> row_base + i,
+  // else extra[i - n_range]
+  int row_base = 0, n_range = 0, n_extra = 0;
+  int extra[4] = {0, 0, 0, 0};
+  // argmax epilogue: allowed = [allow_lo, allow_hi] U [stop_lo, stop_hi) (stops when !mask)
+  unsigned long long* amax = nullptr;  // [M] packed (orderable f32 << 32 | ~row)
+  uint32_t allow_lo = 0, allow_hi = 0, stop_lo = 0, stop_hi = 0;
+};
+
+struct AttnArgs {
+  const float* qkv = nullptr;  // [M][(H + 2 Hkv) hd]
+  float* out = nullptr;        // [M][H hd]
+  __nv_bfloat16* kbase = nullptr;  // this layer's K pages
+  __nv_bfloat16* vbase = nullptr;  // this layer's V pages
+  const int* page_table = nullptr;  // [batch][pt_stride]
+  int pt_stride = 0;
+  const int* tok_seq = nullptr;  // [M] sequence of each token
+  const int* tok_pos = nullptr;  // [M] absolute position of each token (null: const_pos)
+  int const_pos = 0;
+  const float* qn = nullptr;
+  const float* kn = nullptr;
+  float eps = 0.f;
+  const float* inv_freq = nullptr;
+  int interleaved = 1;
+  float scale = 1.f;  // f32(1/sqrt(hd)) computed in double on the host (s2/nn.rs:344)
+  int H = 0, Hkv = 0, hd = 0;
+  int n_split = 1;
+  int append = 1;  // 1: this launch appends each token's own K/V (decode)
+  float* part = nullptr;  // [M][Hkv][n_split][G][hd + 2]
+  int* counters = nullptr;  // [M][Hkv]
+  int M = 1;
+};
+
+// ---- launchers (stream-ordered, programmatic dependent launch enabled) ----------------
+cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st);
+
+struct EmbedArgs {
+  const int* tok_seq = nullptr;
+  const uint32_t* frames = nullptr;  // [batch][1+C] per-sequence current frame
+  int frame_stride = 0;
+  const uint32_t* ids = nullptr;  // prompt ids [(1+C) x T] when frames == null
+  int T = 0, t0 = 0;               // column offset into the prompt
+  DevMat emb, cb_emb;
+  int dim = 0, C = 0, R = 0, vocab = 0;
+  uint32_t sem_lo = 0, sem_hi = 0;
+  int scale_cb = 0;
+  float* h = nullptr;  // [M][dim]
+  int M = 1;
+  int* err = nullptr;  // device error flag (id out of range)
+};
+cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t st);
+
+// fast-AR / frame bookkeeping kernels (greedy device loop)
+struct FrameArgs {
+  int M = 1;
+  const int* tok_seq = nullptr;
+  unsigned long long* amax = nullptr;  // [M] packed argmax (null: code already in the frame)
+  uint32_t* frames = nullptr;          // [batch][1+C] current frame per sequence
+  int frame_stride = 0;
+  int slot = 0;                        // frame column written (0 semantic, 1+c code c)
+  uint32_t sem_begin = 0;
+  int R = 0;
+  DevMat emb;          // fast_embeddings (next fast input) — optional
+  float* x = nullptr;  // [M][dim] next fast input
+  int dim = 0;
+  const float* h_last = nullptr;  // slow residual (for the fast prefix)
+  const float* norm_w = nullptr;  // final norm gain (post-norm hidden) or null (pre-norm)
+  float eps = 0.f;
+  int write_first_code = 0;
+  int* done = nullptr;            // [batch] stop flags
+  uint32_t stop_lo = 0, stop_hi = 0;
+};
+cudaError_t launch_take_semantic(const FrameArgs& a, cudaStream_t st);
+cudaError_t launch_take_code(const FrameArgs& a, cudaStream_t st);
+cudaError_t launch_final_norm(const float* h, const float* w, float eps, int dim, int M, float* out,
+                              cudaStream_t st);
+
+struct AdvanceArgs {
+  int M = 1;
+  const int* tok_seq = nullptr;
+  int* tok_pos = nullptr;
+  int* seq_len = nullptr;
+  const int* done = nullptr;
+  const uint32_t* frames = nullptr;
+  int frame_stride = 0;
+  uint32_t* ring = nullptr;  // [max_frames][batch][1+C]
+  int ring_frames = 0;
+  int* frame_count = nullptr;  // [batch]
+  int batch = 0;
+};
+cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st);
+
+// repack / dequant
+// destination row of source row r is r * row_mul + row_add (w1/w3 interleave)
+cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
+                        int row_mul, int row_add, cudaStream_t st);
+cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* q, uint8_t* meta,
+                        int row_mul, int row_add, cudaStream_t st);
+cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out,
+                           cudaStream_t st);
+
+// host helpers
+void set_error(const std::string& msg);
+int ggml_row_bytes(int dtype, int64_t cols, size_t* out);
+
+}  // namespace sx
