@@ -164,7 +164,7 @@ def bench_device(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_all = float(t.item())
     mean_ctx = ctx_start + (K - 1) / 2.0
-    fb_sem = frame_bytes(cfg, SX_DTYPE_Q8_0, ctx=mean_ctx, semantic_head=True)
+    fb_sem = frame_bytes(cfg, SX_DTYPE_Q8_0, ctx=mean_ctx, semantic_head=True, kv_elem=4)
 
     # ---- roofline of the dominant kernel: the batch-1 Q8_0 GEMV, timed alone live ----
     peak, peak_kind = peaks()
@@ -261,7 +261,7 @@ def cpu_baseline(cfg, blob, budget_s: float, frames: int | None = None) -> dict:
     from syrinx_b200.workloads import dual_ar_prompt
 
     om = oc.OracleModel(cfg, blob)
-    sess = oc.OracleSession(om, max_ctx=256, kv_bf16=True)
+    sess = oc.OracleSession(om, max_ctx=256, kv_bf16=False)
     prompt = dual_ar_prompt(cfg, 16, 13, seed=SEED)
     logits, hidden = sess.prefill(prompt)
     n, t_total = 0, 0.0

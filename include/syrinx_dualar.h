@@ -126,10 +126,14 @@ int sx_model_destroy(sx_model* model);
 /* Device bytes held by the model's weights. */
 int sx_model_weight_bytes(const sx_model* model, size_t* bytes_out);
 
-/* A decoding session: paged bf16 KV cache for up to `max_batch` sequences of `max_ctx`
+/* A decoding session: paged KV cache for up to `max_batch` (<= 8) sequences of `max_ctx`
  * positions each, plus activation buffers. Replaces `KvCache` (s2/nn.rs:223-261;
- * cv2/mod.rs:117-170). */
+ * cv2/mod.rs:117-170). sx_session_create keeps K/V in f32, like the reference's CPU
+ * cache, so greedy output is token-exact; sx_session_create_ex also accepts
+ * SX_DTYPE_BF16 (half the KV bytes; logits within the 2e-2 parity tolerance). */
 int sx_session_create(sx_model* model, int32_t max_batch, int32_t max_ctx, sx_session** out);
+int sx_session_create_ex(sx_model* model, int32_t max_batch, int32_t max_ctx, int32_t kv_dtype,
+                         sx_session** out);
 /* Clear every sequence (the reference `reset`, dualar.rs:73). */
 int sx_session_reset(sx_session* s);
 int sx_session_destroy(sx_session* s);

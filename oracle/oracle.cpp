@@ -432,7 +432,7 @@ void run_layers(oc_session* s, bool fast, float* x, int M, int pos0) {
   const std::vector<float>& inv = fast ? m->inv_fast : m->inv_slow;
   std::vector<float>& kc = fast ? s->fk : s->k;
   std::vector<float>& vc = fast ? s->fv : s->v;
-  const bool round_kv = !fast && s->kv_bf16;
+  const bool round_kv = s->kv_bf16;  // mirrors the device cache element type (slow and fast)
   const float scale = (float)(1.0 / std::sqrt((double)hd));
 
   std::vector<float> hn((size_t)M * d), qkv((size_t)M * qkv_w), ctx((size_t)M * H * hd);

@@ -28,6 +28,7 @@ SIGNATURES = {
     "sx_model_destroy": (C.c_int, [C.c_void_p]),
     "sx_model_weight_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
     "sx_session_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "sx_session_create_ex": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "sx_session_reset": (C.c_int, [C.c_void_p]),
     "sx_session_destroy": (C.c_int, [C.c_void_p]),
     "sx_session_len": (C.c_int, [C.c_void_p, C.c_int32, _i32p]),

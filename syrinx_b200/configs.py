@@ -142,10 +142,12 @@ def bytes_per_weight(wtype: int) -> float:
     return {SX_DTYPE_Q8_0: 34 / 32, SX_DTYPE_Q4_K: 144 / 256, SX_DTYPE_F32: 4.0}[wtype]
 
 
-def frame_bytes(cfg: ModelConfig, wtype: int, ctx: float, semantic_head: bool = True) -> dict:
+def frame_bytes(cfg: ModelConfig, wtype: int, ctx: float, semantic_head: bool = True,
+                kv_elem: int = 2) -> dict:
     """Algorithmic HBM bytes streamed per frame (batch 1):
-    slow weights + head rows + C x fast layers + (C-1) x fast_output + bf16 KV read
-    (2 * L * Hkv * hd * 2 B per context position; the fast AR's local KV is negligible)."""
+    slow weights + head rows + C x fast layers + (C-1) x fast_output + KV read
+    (2 * L * Hkv * hd * kv_elem B per context position: 2 for bf16, 4 for f32; the fast AR's
+    local KV is negligible)."""
     bpw = bytes_per_weight(wtype)
     s = cfg.slow
     slow_w = s.n_layer * s.layer_params() * bpw
@@ -156,7 +158,7 @@ def frame_bytes(cfg: ModelConfig, wtype: int, ctx: float, semantic_head: bool = 
         f = cfg.fast
         fast_w = cfg.num_codebooks * f.n_layer * f.layer_params() * bpw
         fast_w += (cfg.num_codebooks - 1) * cfg.codebook_size * f.dim * bpw
-    kv = 2 * s.n_layer * s.n_local_heads * s.head_dim * 2 * ctx
+    kv = 2 * s.n_layer * s.n_local_heads * s.head_dim * kv_elem * ctx
     return {"slow": slow_w, "head": head_w, "fast": fast_w, "kv": kv,
             "total": slow_w + head_w + fast_w + kv}
 

@@ -1,4 +1,4 @@
-// attention.cu — GQA decode attention over the paged bf16 KV cache.
+// attention.cu — GQA decode attention over the paged KV cache (f32 or bf16 elements).
 //
 // Replaces the reference attention block after the wqkv projection
 // (`attention`, crates/syrinx-fish/src/s2/nn.rs:315-352; `attn_cached`,
@@ -61,23 +61,60 @@ __device__ __forceinline__ size_t kv_off(const AttnArgs& a, int seq, int t, int 
   return ((size_t)(page * a.Hkv + g) * kPage + (t % kPage)) * HD;
 }
 
-// Compute token m's K (normed, rotated) and V for kv head g and store them as bf16 at
-// position pos of its sequence. One warp; buf is HD floats of shared memory.
-template <int HD>
+// KV element type: f32 (exact, the reference CPU path's cache) or bf16 (half the bytes).
+__device__ __forceinline__ void kv_store(float* p, float v) { *p = v; }
+__device__ __forceinline__ void kv_store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ float kv_load(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ float kv_load(const __nv_bfloat16* p) { return __bfloat162float(__ldcg(p)); }
+
+// EPL consecutive elements of a K row starting at p, as f32 (one vector load).
+template <int EPL>
+__device__ __forceinline__ void kv_load_row(const float* p, float (&v)[EPL]) {
+  if constexpr (EPL == 4) {
+    const float4 r = __ldcg(reinterpret_cast<const float4*>(p));
+    v[0] = r.x; v[1] = r.y; v[2] = r.z; v[3] = r.w;
+  } else if constexpr (EPL == 2) {
+    const float2 r = __ldcg(reinterpret_cast<const float2*>(p));
+    v[0] = r.x; v[1] = r.y;
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; e++) v[e] = __ldcg(p + e);
+  }
+}
+template <int EPL>
+__device__ __forceinline__ void kv_load_row(const __nv_bfloat16* p, float (&v)[EPL]) {
+  if constexpr (EPL == 4) {
+    const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(p));
+    const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    v[0] = __low2float(p0); v[1] = __high2float(p0); v[2] = __low2float(p1); v[3] = __high2float(p1);
+  } else if constexpr (EPL == 2) {
+    const unsigned int raw = __ldcg(reinterpret_cast<const unsigned int*>(p));
+    const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw);
+    v[0] = __low2float(p0); v[1] = __high2float(p0);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; e++) v[e] = __bfloat162float(__ldcg(p + e));
+  }
+}
+
+// Compute token m's K (normed, rotated) and V for kv head g and store them at position
+// pos of its sequence. One warp; buf is HD floats of shared memory.
+template <int HD, typename KT>
 __device__ void append_kv(const AttnArgs& a, int m, int seq, int pos, int g, float* buf, int lane) {
   const float* kr = a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * HD + (size_t)(a.H + g) * HD;
   const float* vr = kr + (size_t)a.Hkv * HD;
-  for (int e = lane; e < HD; e += 32) buf[e] = kr[e];
+  for (int e = lane; e < HD; e += 32) buf[e] = ld_cg(kr + e);
   __syncwarp();
   norm_rope_head<HD>(buf, a.kn, a.eps, a.inv_freq, a.interleaved, pos, lane);
   const size_t off = kv_off(a, seq, pos, g, HD);
   for (int e = lane; e < HD; e += 32) {
-    a.kbase[off + e] = __float2bfloat16_rn(buf[e]);
-    a.vbase[off + e] = __float2bfloat16_rn(vr[e]);
+    kv_store(static_cast<KT*>(a.kbase) + off + e, buf[e]);
+    kv_store(static_cast<KT*>(a.vbase) + off + e, ld_cg(vr + e));
   }
 }
 
-template <int HD>
+template <int HD, typename KT>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   constexpr int EPL = HD / 32;           // key elements per lane in the score phase
   constexpr int NG = kAttnThreads / HD;  // token groups in the P.V phase
@@ -94,8 +131,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   const int m = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.H / a.Hkv;
-  const int seq = a.tok_seq ? a.tok_seq[m] : 0;
-  const int pos = a.tok_pos ? a.tok_pos[m] : a.const_pos;
+  const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
+  const int pos = a.tok_pos ? ld_cg(a.tok_pos + m) : a.const_pos;
   const int n_keys = pos + 1;
   const int chunk = (n_keys + a.n_split - 1) / a.n_split;
   const int t0 = min(n_keys, s * chunk);
@@ -106,12 +143,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   const float* qrow = a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * HD;
   for (int i = warp; i < G; i += kWarpsA) {
     const float* src = qrow + (size_t)(g * G + i) * HD;
-    for (int e = lane; e < HD; e += 32) qs[i][e] = src[e];
+    for (int e = lane; e < HD; e += 32) qs[i][e] = ld_cg(src + e);
     __syncwarp();
     norm_rope_head<HD>(qs[i], a.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
   }
   if (a.append && pos >= t0 && pos < t1 && warp == kWarpsA - 1)
-    append_kv<HD>(a, m, seq, pos, g, kbuf, lane);
+    append_kv<HD, KT>(a, m, seq, pos, g, kbuf, lane);
   if (threadIdx.x < kMaxGroup) {
     m_s[threadIdx.x] = -INFINITY;
     l_s[threadIdx.x] = 0.f;
@@ -127,24 +164,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
     const int n = min(kSub, t1 - tb);
     // scores: one key row per warp iteration, lanes split the head dimension
     for (int t = warp; t < n; t += kWarpsA) {
-      const __nv_bfloat16* kr = a.kbase + kv_off(a, seq, tb + t, g, HD) + lane * EPL;
+      const KT* kr = static_cast<const KT*>(a.kbase) + kv_off(a, seq, tb + t, g, HD) + lane * EPL;
       float kv[EPL];
-      if constexpr (EPL == 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(kr);
-        const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        kv[0] = __low2float(p0);
-        kv[1] = __high2float(p0);
-        kv[2] = __low2float(p1);
-        kv[3] = __high2float(p1);
-      } else if constexpr (EPL == 2) {
-        const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(kr);
-        kv[0] = __low2float(p0);
-        kv[1] = __high2float(p0);
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPL; e++) kv[e] = __bfloat162float(kr[e]);
-      }
+      kv_load_row<EPL>(kr, kv);
       for (int i = 0; i < G; i++) {
         float d = 0.f;
 #pragma unroll
@@ -180,7 +202,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
     for (int i = 0; i < G; i++) acc[i] *= alpha_s[i];
     // P.V: thread (e, grp) accumulates keys t == grp (mod NG)
     for (int t = grp; t < n; t += NG) {
-      const float v = __bfloat162float(a.vbase[kv_off(a, seq, tb + t, g, HD) + e_pv]);
+      const float v = kv_load(static_cast<const KT*>(a.vbase) + kv_off(a, seq, tb + t, g, HD) + e_pv);
       for (int i = 0; i < G; i++) acc[i] = fmaf(sc[i][t], v, acc[i]);
     }
     __syncthreads();
@@ -242,27 +264,19 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
 
 // Prefill: append the K/V of all M tokens first (tokens of one sequence attend to each
 // other, so appends and reads cannot share a launch).
-template <int HD>
+template <int HD, typename KT>
 __global__ void __launch_bounds__(32) k_kv_append(const AttnArgs a) {
   __shared__ float buf[HD];
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x, g = blockIdx.y;
-  const int seq = a.tok_seq ? a.tok_seq[m] : 0;
-  const int pos = a.tok_pos ? a.tok_pos[m] : a.const_pos;
-  append_kv<HD>(a, m, seq, pos, g, buf, threadIdx.x);
+  const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
+  const int pos = a.tok_pos ? ld_cg(a.tok_pos + m) : a.const_pos;
+  append_kv<HD, KT>(a, m, seq, pos, g, buf, threadIdx.x);
 }
 
 cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cfg;
+  return launch_cfg(grid, block, 0, st, attr);
 }
 
 }  // namespace
@@ -273,9 +287,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.M, a.Hkv, a.n_split), dim3(kAttnThreads), st, attr);
   switch (a.hd) {
-    case 32: return cudaLaunchKernelEx(&cfg, k_attention<32>, a);
-    case 64: return cudaLaunchKernelEx(&cfg, k_attention<64>, a);
-    case 128: return cudaLaunchKernelEx(&cfg, k_attention<128>, a);
+    case 32: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_attention<32, float>, a)
+                             : cudaLaunchKernelEx(&cfg, k_attention<32, __nv_bfloat16>, a);
+    case 64: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_attention<64, float>, a)
+                             : cudaLaunchKernelEx(&cfg, k_attention<64, __nv_bfloat16>, a);
+    case 128: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_attention<128, float>, a)
+                              : cudaLaunchKernelEx(&cfg, k_attention<128, __nv_bfloat16>, a);
   }
   return cudaErrorInvalidValue;
 }
@@ -284,9 +301,12 @@ cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.M, a.Hkv), dim3(32), st, attr);
   switch (a.hd) {
-    case 32: return cudaLaunchKernelEx(&cfg, k_kv_append<32>, a);
-    case 64: return cudaLaunchKernelEx(&cfg, k_kv_append<64>, a);
-    case 128: return cudaLaunchKernelEx(&cfg, k_kv_append<128>, a);
+    case 32: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_kv_append<32, float>, a)
+                             : cudaLaunchKernelEx(&cfg, k_kv_append<32, __nv_bfloat16>, a);
+    case 64: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_kv_append<64, float>, a)
+                             : cudaLaunchKernelEx(&cfg, k_kv_append<64, __nv_bfloat16>, a);
+    case 128: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_kv_append<128, float>, a)
+                              : cudaLaunchKernelEx(&cfg, k_kv_append<128, __nv_bfloat16>, a);
   }
   return cudaErrorInvalidValue;
 }

@@ -154,12 +154,19 @@ int sx_model_weight_bytes(const sx_model* model, size_t* bytes_out) {
 }
 
 int sx_session_create(sx_model* model, int32_t max_batch, int32_t max_ctx, sx_session** out) {
+  return sx_session_create_ex(model, max_batch, max_ctx, SX_DTYPE_F32, out);
+}
+
+int sx_session_create_ex(sx_model* model, int32_t max_batch, int32_t max_ctx, int32_t kv_dtype,
+                         sx_session** out) {
   SX_GUARD({
     if (!model) {
       set_error("null model");
       return SX_E_INVALID;
     }
-    return session_create(model, max_batch, max_ctx, out);
+    int rc = use_device(model);
+    if (rc) return rc;
+    return session_create(model, max_batch, max_ctx, kv_dtype, out);
   })
 }
 

@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
     for (int k = threadIdx.x; k < K; k += kThreads)
 #pragma unroll
       for (int m = 0; m < M; m++) {
-        const float v = (m < a.M) ? a.x[(size_t)m * K + k] : 0.f;
+        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
         ss[m] = fmaf(v, v, ss[m]);
       }
 #pragma unroll
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
       const float g = a.norm_w[k];
 #pragma unroll
       for (int m = 0; m < M; m++) {
-        const float v = (m < a.M) ? a.x[(size_t)m * K + k] : 0.f;
+        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
         xs[(size_t)m * K + k] = __fmul_rn(__fdiv_rn(v, den[m]), g);
       }
     }
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
 #pragma unroll
       for (int m = 0; m < M; m++) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < a.M) v = reinterpret_cast<const float4*>(a.x + (size_t)m * K)[i];
+        if (m < a.M) v = ld_cg4(a.x + (size_t)m * K + 4 * i);
         reinterpret_cast<float4*>(xs + (size_t)m * K)[i] = v;
       }
   }
@@ -337,8 +337,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
 #pragma unroll
       for (int w = 0; w < kWarps; w++) b = best[w][threadIdx.x] > b ? best[w][threadIdx.x] : b;
       if (b != 0ull) {
-        unsigned long long* dst = a.amax + threadIdx.x;
-        if (b > *(volatile unsigned long long*)dst) atomicMax(dst, b);
+        atomicMax(a.amax + threadIdx.x, b);
       }
     }
   } else {
@@ -355,7 +354,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
               if (a.bias) v = __fadd_rn(v, a.bias[pr]);
               float* dst = a.y + (size_t)m * a.ldy + pr;
               if constexpr (EPI == EPI_ADD)
-                *dst = __fadd_rn(*dst, v);
+                *dst = __fadd_rn(ld_cg(dst), v);
               else
                 *dst = v;
             }
@@ -377,16 +376,9 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((n_logical + rows_per_cta - 1) / rows_per_cta);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cudaLaunchConfig_t cfg =
+      launch_cfg(dim3((n_logical + rows_per_cta - 1) / rows_per_cta), dim3(kThreads), smem, st, attr);
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
@@ -415,10 +407,12 @@ cudaError_t dispatch_m(const GemvArgs& a, Epi epi, cudaStream_t st) {
 
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
   if (a.M < 1 || a.M > kMaxTok || a.n_range + a.n_extra < 1) return cudaErrorInvalidValue;
-  // x of all M tokens is staged in shared memory; split the tokens when it does not fit
+  // x of all M tokens is staged in shared memory, sized by the kernel's template M
+  // (1, 2, 4 or 8): split the tokens into launches whose template fits in 200 KB
   const size_t K = (size_t)a.w.cols;
   const size_t per_tok = K * 4 + (a.w.dtype == SX_DTYPE_Q4_K ? (K / 16) * 4 : 0);
-  const int max_m = (int)std::max<size_t>(1, std::min<size_t>(kMaxTok, (200 * 1024) / per_tok));
+  int max_m = kMaxTok;
+  while (max_m > 1 && (size_t)max_m * per_tok > 200 * 1024) max_m >>= 1;
   for (int m0 = 0; m0 < a.M; m0 += max_m) {
     GemvArgs b = a;
     b.M = std::min(max_m, a.M - m0);

@@ -14,6 +14,8 @@
 //                  (common/dualar.rs:198-218).
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "sx_device.cuh"
 #include "sx_internal.hpp"
 
@@ -21,15 +23,7 @@ namespace sx {
 namespace {
 
 cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cfg;
+  return launch_cfg(grid, block, 0, st, attr);
 }
 
 // Exact dequantized element (r, e) of a device matrix: the value ggml's dequantize_row_*
@@ -76,10 +70,10 @@ __global__ void __launch_bounds__(256) k_embed(const EmbedArgs a, float inv_scal
   if (threadIdx.x < rows) {
     uint32_t v;
     if (a.frames) {
-      const int seq = a.tok_seq ? a.tok_seq[m] : 0;
-      v = a.frames[(size_t)seq * a.frame_stride + threadIdx.x];
+      const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
+      v = ld_cg(a.frames + (size_t)seq * a.frame_stride + threadIdx.x);
     } else {
-      v = a.ids[(size_t)threadIdx.x * a.T + a.t0 + m];
+      v = ld_cg(a.ids + (size_t)threadIdx.x * a.T + a.t0 + m);
     }
     ids[threadIdx.x] = v;
     const bool ok = threadIdx.x == 0 ? v < (uint32_t)a.vocab : v < (uint32_t)a.R;
@@ -114,12 +108,11 @@ __global__ void __launch_bounds__(256) k_take_semantic(const FrameArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
-  const int seq = a.tok_seq ? a.tok_seq[m] : 0;
+  const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
   __shared__ float red[8];
   if (threadIdx.x == 0) {
-    const unsigned long long key = a.amax[m];
+    const unsigned long long key = atomicExch(a.amax + m, 0ull);  // read and re-arm
     const uint32_t tok = argmax_row(key);
-    a.amax[m] = 0ull;
     uint32_t* fr = a.frames + (size_t)seq * a.frame_stride;
     fr[0] = tok;
     if (a.write_first_code) {
@@ -134,7 +127,10 @@ __global__ void __launch_bounds__(256) k_take_semantic(const FrameArgs a) {
   float* x = a.x + (size_t)m * a.dim;
   if (a.norm_w) {
     float ss = 0.f;
-    for (int e = threadIdx.x; e < a.dim; e += blockDim.x) ss = fmaf(h[e], h[e], ss);
+    for (int e = threadIdx.x; e < a.dim; e += blockDim.x) {
+      const float v = ld_cg(h + e);
+      ss = fmaf(v, v, ss);
+    }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
@@ -142,9 +138,9 @@ __global__ void __launch_bounds__(256) k_take_semantic(const FrameArgs a) {
     for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
     const float den = sqrtf(__fadd_rn(__fdiv_rn(t, (float)a.dim), a.eps));
     for (int e = threadIdx.x; e < a.dim; e += blockDim.x)
-      x[e] = __fmul_rn(__fdiv_rn(h[e], den), a.norm_w[e]);
+      x[e] = __fmul_rn(__fdiv_rn(ld_cg(h + e), den), a.norm_w[e]);
   } else {
-    for (int e = threadIdx.x; e < a.dim; e += blockDim.x) x[e] = h[e];
+    for (int e = threadIdx.x; e < a.dim; e += blockDim.x) x[e] = ld_cg(h + e);
   }
 }
 
@@ -154,17 +150,16 @@ __global__ void __launch_bounds__(256) k_take_code(const FrameArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
-  const int seq = a.tok_seq ? a.tok_seq[m] : 0;
+  const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
   __shared__ uint32_t code_s;
   uint32_t* fr = a.frames + (size_t)seq * a.frame_stride;
   if (threadIdx.x == 0) {
     uint32_t code;
     if (a.amax) {
-      code = argmax_row(a.amax[m]);
-      a.amax[m] = 0ull;
+      code = argmax_row(atomicExch(a.amax + m, 0ull));  // read and re-arm
       fr[a.slot] = code;
     } else {
-      code = fr[a.slot];
+      code = ld_cg(fr + a.slot);
     }
     code_s = min(code, (uint32_t)(a.R - 1));
   }
@@ -182,7 +177,10 @@ __global__ void __launch_bounds__(256) k_final_norm(const float* h, const float*
   const int m = blockIdx.x;
   const float* hr = h + (size_t)m * dim;
   float ss = 0.f;
-  for (int e = threadIdx.x; e < dim; e += blockDim.x) ss = fmaf(hr[e], hr[e], ss);
+  for (int e = threadIdx.x; e < dim; e += blockDim.x) {
+    const float v = ld_cg(hr + e);
+    ss = fmaf(v, v, ss);
+  }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -190,7 +188,7 @@ __global__ void __launch_bounds__(256) k_final_norm(const float* h, const float*
   for (int k = 0; k < (int)(blockDim.x >> 5); k++) t += red[k];
   const float den = sqrtf(__fadd_rn(__fdiv_rn(t, (float)dim), eps));
   for (int e = threadIdx.x; e < dim; e += blockDim.x)
-    out[(size_t)m * dim + e] = __fmul_rn(__fdiv_rn(hr[e], den), w[e]);
+    out[(size_t)m * dim + e] = __fmul_rn(__fdiv_rn(ld_cg(hr + e), den), w[e]);
 }
 
 __global__ void k_advance(const AdvanceArgs a) {
@@ -198,16 +196,16 @@ __global__ void k_advance(const AdvanceArgs a) {
   pdl_wait();
   const int m = threadIdx.x;
   if (m >= a.M) return;
-  const int seq = a.tok_seq ? a.tok_seq[m] : m;
-  if (a.done && a.done[seq]) return;
-  const int f = a.frame_count[seq];
+  const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : m;
+  if (a.done && ld_cg(a.done + seq)) return;
+  const int f = ld_cg(a.frame_count + seq);
   const int width = a.frame_stride;
   if (f < a.ring_frames) {
     uint32_t* dst = a.ring + ((size_t)f * a.batch + seq) * width;
-    for (int i = 0; i < width; i++) dst[i] = a.frames[(size_t)seq * width + i];
+    for (int i = 0; i < width; i++) dst[i] = ld_cg(a.frames + (size_t)seq * width + i);
   }
   a.frame_count[seq] = f + 1;
-  const int len = a.seq_len[seq] + 1;
+  const int len = ld_cg(a.seq_len + seq) + 1;
   a.seq_len[seq] = len;
   a.tok_pos[m] = len;
 }
@@ -278,6 +276,27 @@ __global__ void k_dequant(int dtype, const uint8_t* blocks, int64_t n_blocks, fl
 
 }  // namespace
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SYRINX_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+cudaLaunchConfig_t launch_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cfg;
+}
+
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t st) {
   if (a.C > 64) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
@@ -314,12 +333,14 @@ cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st) {
 
 cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
                         int row_mul, int row_add, cudaStream_t st) {
+  (void)cudaGetLastError();  // report this launch's status, not an earlier one
   k_repack_q8_0<<<1184, 256, 0, st>>>(blocks, rows, cols, q, s, row_mul, row_add);
   return cudaGetLastError();
 }
 
 cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* q, uint8_t* meta,
                         int row_mul, int row_add, cudaStream_t st) {
+  (void)cudaGetLastError();  // report this launch's status, not an earlier one
   k_repack_q4_k<<<1184, 256, 0, st>>>(blocks, rows, cols, q, meta, row_mul, row_add);
   return cudaGetLastError();
 }
@@ -327,6 +348,7 @@ cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8
 cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out,
                            cudaStream_t st) {
   if (dtype != SX_DTYPE_Q8_0 && dtype != SX_DTYPE_Q4_K) return cudaErrorInvalidValue;
+  (void)cudaGetLastError();  // report this launch's status, not an earlier one
   k_dequant<<<1184, 256, 0, st>>>(dtype, blocks, n_blocks, out);
   return cudaGetLastError();
 }

@@ -288,10 +288,14 @@ void model_destroy(sx_model* m) {
 // ---------------------------------------------------------------------------------------
 // sessions
 // ---------------------------------------------------------------------------------------
-int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out) {
+int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_session** out) {
   if (!m || !out || max_batch < 1 || max_batch > kMaxTok || max_ctx < 1) {
     set_error("sx_session_create: max_batch must be 1..8 and max_ctx >= 1");
     return SX_E_INVALID;
+  }
+  if (kv_dtype != SX_DTYPE_F32 && kv_dtype != SX_DTYPE_BF16) {
+    set_error("sx_session_create: kv_dtype must be SX_DTYPE_F32 or SX_DTYPE_BF16");
+    return SX_E_UNSUPPORTED;
   }
   SX_CU(cudaSetDevice(m->device));
   const sx_model_desc& d = m->d;
@@ -299,6 +303,8 @@ int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out) {
   s->m = m;
   s->max_batch = max_batch;
   s->max_ctx = max_ctx;
+  s->kv_f32 = kv_dtype == SX_DTYPE_F32;
+  s->kv_elem = s->kv_f32 ? 4 : 2;
   s->len.assign(max_batch, 0);
   auto fail = [&](int r) {
     session_destroy(s);
@@ -314,7 +320,7 @@ int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out) {
   s->n_pages = max_batch * s->pages_per_seq;
   s->kv_layer_elems = (size_t)2 * s->n_pages * sl.n_local_heads * kPage * sl.head_dim;
   int rc;
-  if ((rc = dalloc(s->allocs, &s->kv, s->kv_layer_elems * sl.n_layer))) return fail(rc);
+  if ((rc = dalloc(s->allocs, &s->kv, s->kv_layer_elems * sl.n_layer * s->kv_elem))) return fail(rc);
   if ((rc = dalloc(s->allocs, &s->page_table, (size_t)s->n_pages))) return fail(rc);
   {
     std::vector<int> pt(s->n_pages);
@@ -327,7 +333,7 @@ int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out) {
   if (has_fast) {
     const auto& f = d.fast;
     s->fkv_layer_elems = (size_t)2 * max_batch * f.n_local_heads * kPage * f.head_dim;
-    if ((rc = dalloc(s->allocs, &s->fkv, s->fkv_layer_elems * f.n_layer))) return fail(rc);
+    if ((rc = dalloc(s->allocs, &s->fkv, s->fkv_layer_elems * f.n_layer * s->kv_elem))) return fail(rc);
     if ((rc = dalloc(s->allocs, &s->fpage_table, (size_t)max_batch))) return fail(rc);
     std::vector<int> pt(max_batch);
     for (int i = 0; i < max_batch; i++) pt[i] = i;
@@ -430,9 +436,10 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     AttnArgs a;
     a.qkv = s->xqkv;
     a.out = s->attn;
-    __nv_bfloat16* base = (fast ? s->fkv : s->kv) + l * layer_elems;
+    uint8_t* base = (fast ? s->fkv : s->kv) + l * layer_elems * s->kv_elem;
     a.kbase = base;
-    a.vbase = base + half;
+    a.vbase = base + half * s->kv_elem;
+    a.kv_f32 = s->kv_f32;
     a.page_table = fast ? s->fpage_table : s->page_table;
     a.pt_stride = fast ? 1 : s->pages_per_seq;
     a.tok_seq = tok_seq;

@@ -34,8 +34,10 @@ struct sx_session {
   cudaStream_t st = nullptr;      // stream all work is enqueued on
   cudaStream_t own_st = nullptr;  // the session's own stream (st unless a caller set one)
   int pages_per_seq = 0, n_pages = 0;
-  __nv_bfloat16* kv = nullptr;   // slow: per layer [2][n_pages][Hkv][PAGE][hd]
-  __nv_bfloat16* fkv = nullptr;  // fast: per layer [2][max_batch][Hkv][PAGE][hd]
+  int kv_f32 = 1;                // KV element type: 1 f32 (exact), 0 bf16
+  size_t kv_elem = 4;            // bytes per KV element
+  uint8_t* kv = nullptr;         // slow: per layer [2][n_pages][Hkv][PAGE][hd]
+  uint8_t* fkv = nullptr;        // fast: per layer [2][max_batch][Hkv][PAGE][hd]
   size_t kv_layer_elems = 0, fkv_layer_elems = 0;
   int* page_table = nullptr;   // [max_batch][pages_per_seq]
   int* fpage_table = nullptr;  // [max_batch][1]
@@ -74,7 +76,7 @@ struct sx_session {
 namespace sx {
 int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out);
 void model_destroy(sx_model* m);
-int session_create(sx_model* m, int max_batch, int max_ctx, sx_session** out);
+int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_session** out);
 void session_destroy(sx_session* s);
 int session_reset(sx_session* s);
 int sync_lengths(sx_session* s);

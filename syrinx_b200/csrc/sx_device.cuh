@@ -73,6 +73,15 @@ __device__ __forceinline__ void u4x4_to_f32x2x2(uint32_t nib, unsigned long long
   hi = add2(pack2u(__byte_perm(nib, 0x4B000000u, 0x7542), __byte_perm(nib, 0x4B000000u, 0x7543)), bias);
 }
 
+// Reads of data produced by earlier kernels of the decode chain (activations, frames,
+// positions, argmax slots) go through L2 only (ld.global.cg): with programmatic dependent
+// launch a CTA can be resident on an SM before its producer finishes, so an L1 line that
+// SM cached earlier must never serve such a read.
+__device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ float4 ld_cg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ int ld_cg(const int* p) { return __ldcg(p); }
+__device__ __forceinline__ uint32_t ld_cg(const uint32_t* p) { return __ldcg(reinterpret_cast<const unsigned int*>(p)); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -80,8 +80,9 @@ struct GemvArgs {
 struct AttnArgs {
   const float* qkv = nullptr;  // [M][(H + 2 Hkv) hd]
   float* out = nullptr;        // [M][H hd]
-  __nv_bfloat16* kbase = nullptr;  // this layer's K pages
-  __nv_bfloat16* vbase = nullptr;  // this layer's V pages
+  void* kbase = nullptr;       // this layer's K pages (f32 or bf16 elements)
+  void* vbase = nullptr;       // this layer's V pages
+  int kv_f32 = 1;              // element type of the cache: 1 f32, 0 bf16
   const int* page_table = nullptr;  // [batch][pt_stride]
   int pt_stride = 0;
   const int* tok_seq = nullptr;  // [M] sequence of each token
@@ -173,6 +174,10 @@ cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, f
 
 // host helpers
 void set_error(const std::string& msg);
+// Programmatic dependent launch is on unless SYRINX_PDL=0 (plain stream ordering).
+bool pdl_enabled();
+// Launch config with the programmatic-stream-serialization attribute when enabled.
+cudaLaunchConfig_t launch_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr);
 int ggml_row_bytes(int dtype, int64_t cols, size_t* out);
 
 }  // namespace sx

@@ -17,7 +17,7 @@ import math
 import numpy as np
 
 from . import _lib
-from .configs import SX_DTYPE_Q8_0, ModelConfig, SxSamplingParams
+from .configs import SX_DTYPE_F32, SX_DTYPE_Q8_0, ModelConfig, SxSamplingParams
 
 
 def _p(a: np.ndarray, ct):
@@ -72,13 +72,17 @@ class SlowStep:
 class B200DualAr:
     """`DualArBackend` over the B200 kernels, one session of up to `max_batch` sequences."""
 
-    def __init__(self, model: Model, max_ctx: int, max_batch: int = 1):
+    def __init__(self, model: Model, max_ctx: int, max_batch: int = 1, kv_dtype: int = SX_DTYPE_F32):
+        """kv_dtype SX_DTYPE_F32 (default, the reference CPU cache: token-exact greedy output)
+        or SX_DTYPE_BF16 (half the KV bytes, for long contexts and batched decode)."""
         self.model = model
         self.cfg = model.cfg
         self.max_ctx = max_ctx
         self.max_batch = max_batch
+        self.kv_dtype = kv_dtype
         self.handle = C.c_void_p()
-        _lib.check(_lib.lib().sx_session_create(model.handle, max_batch, max_ctx, C.byref(self.handle)))
+        _lib.check(_lib.lib().sx_session_create_ex(model.handle, max_batch, max_ctx, kv_dtype,
+                                                   C.byref(self.handle)))
 
     # -- DualArBackend ------------------------------------------------------------------
     def config(self) -> ModelConfig:
