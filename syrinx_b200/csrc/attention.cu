@@ -8,12 +8,15 @@
 //   -> scores * 1/sqrt(hd) -> softmax -> P.V, per kv head for its whole query group, so
 //   the repeat_kv copy (nn.rs:194-202) never exists.
 //
-// One CTA per (token, kv head, split of the key axis): the CTA streams its slice of the
-// bf16 K/V pages once for all G query heads of the group, keeps an online softmax in f32,
-// and the last CTA of a (token, kv head) to finish merges the split partials (flash-decoding).
+// One CTA per (token, kv head, split of the key axis). Each warp walks chunks of KC keys:
+// it issues the K and V row loads of the whole chunk at once (lanes split the head
+// dimension, so every row load is coalesced), reduces the KC x G dot products across lanes
+// in independent shuffle chains, and folds the chunk into an online softmax held in
+// registers. The warps are merged through shared memory, and the last CTA of a
+// (token, kv head) to finish merges the split partials (flash-decoding).
 // In decode (append = 1) the CTA whose slice contains the new position computes that
-// token's normed, rotated K and V, writes them into the cache and uses them directly, so
-// no other CTA reads a slot written in the same launch.
+// token's normed, rotated K and V and writes them into the cache before its warps read the
+// slice, so no CTA reads a slot written by another CTA of the same launch.
 #include <cuda_runtime.h>
 
 #include "sx_device.cuh"
@@ -23,7 +26,6 @@ namespace sx {
 namespace {
 
 constexpr int kWarpsA = kAttnThreads / 32;
-constexpr int kSub = 128;  // keys per shared-memory score tile
 
 // RMSNorm (optional) + RoPE of one head held in shared memory by one warp, in place.
 template <int HD>
@@ -64,10 +66,8 @@ __device__ __forceinline__ size_t kv_off(const AttnArgs& a, int seq, int t, int 
 // KV element type: f32 (exact, the reference CPU path's cache) or bf16 (half the bytes).
 __device__ __forceinline__ void kv_store(float* p, float v) { *p = v; }
 __device__ __forceinline__ void kv_store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
-__device__ __forceinline__ float kv_load(const float* p) { return __ldcg(p); }
-__device__ __forceinline__ float kv_load(const __nv_bfloat16* p) { return __bfloat162float(__ldcg(p)); }
 
-// EPL consecutive elements of a K row starting at p, as f32 (one vector load).
+// EPL consecutive elements of a K/V row starting at p, as f32 (one vector load, L2 only).
 template <int EPL>
 __device__ __forceinline__ void kv_load_row(const float* p, float (&v)[EPL]) {
   if constexpr (EPL == 4) {
@@ -114,15 +114,17 @@ __device__ void append_kv(const AttnArgs& a, int m, int seq, int pos, int g, flo
   }
 }
 
-template <int HD, typename KT>
+// GM: compile-time bound on the query heads per kv head (the loops over heads unroll and
+// predicate on the runtime G <= GM).
+template <int HD, typename KT, int GM>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
-  constexpr int EPL = HD / 32;           // key elements per lane in the score phase
-  constexpr int NG = kAttnThreads / HD;  // token groups in the P.V phase
-  __shared__ __align__(16) float qs[kMaxGroup][HD];
-  __shared__ float sc[kMaxGroup][kSub];
-  __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
-  __shared__ float accx[NG][kMaxGroup][HD];
+  constexpr int EPL = HD / 32;          // head elements per lane
+  constexpr int KC = GM <= 4 ? 8 : 4;   // keys per warp chunk
+  __shared__ __align__(16) float qs[GM][HD];
+  __shared__ __align__(16) float wacc[kWarpsA][GM][HD];
+  __shared__ float wm[kWarpsA][GM], wl[kWarpsA][GM];
   __shared__ float kbuf[HD];
+  __shared__ float wq[kMaxSplit][GM], lq[kMaxSplit][GM], inv_l[GM];
   __shared__ int is_last;
 
   pdl_launch_dependents();
@@ -137,7 +139,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   const int chunk = (n_keys + a.n_split - 1) / a.n_split;
   const int t0 = min(n_keys, s * chunk);
   const int t1 = min(n_keys, t0 + chunk);
-  const float scale = a.scale;
 
   // q heads of this group: norm + rope into shared memory
   const float* qrow = a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * HD;
@@ -149,92 +150,134 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   }
   if (a.append && pos >= t0 && pos < t1 && warp == kWarpsA - 1)
     append_kv<HD, KT>(a, m, seq, pos, g, kbuf, lane);
-  if (threadIdx.x < kMaxGroup) {
-    m_s[threadIdx.x] = -INFINITY;
-    l_s[threadIdx.x] = 0.f;
-  }
   __syncthreads();
 
-  float acc[kMaxGroup];
+  float qv[GM][EPL];
 #pragma unroll
-  for (int i = 0; i < kMaxGroup; i++) acc[i] = 0.f;
-  const int e_pv = threadIdx.x % HD, grp = threadIdx.x / HD;
-
-  for (int tb = t0; tb < t1; tb += kSub) {
-    const int n = min(kSub, t1 - tb);
-    // scores: one key row per warp iteration, lanes split the head dimension
-    for (int t = warp; t < n; t += kWarpsA) {
-      const KT* kr = static_cast<const KT*>(a.kbase) + kv_off(a, seq, tb + t, g, HD) + lane * EPL;
-      float kv[EPL];
-      kv_load_row<EPL>(kr, kv);
-      for (int i = 0; i < G; i++) {
-        float d = 0.f;
+  for (int i = 0; i < GM; i++)
 #pragma unroll
-        for (int e = 0; e < EPL; e++) d = fmaf(qs[i][lane * EPL + e], kv[e], d);
-        d = warp_sum(d);
-        if (lane == 0) sc[i][t] = __fmul_rn(d, scale);
-      }
-    }
-    __syncthreads();
-    // online softmax statistics: one warp per head
-    for (int i = warp; i < G; i += kWarpsA) {
-      float mx = -INFINITY;
-      for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[i][t]);
-      mx = warp_max(mx);
-      const float m_old = m_s[i];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.f;
-      for (int t = lane; t < n; t += 32) {
-        const float p = expf(sc[i][t] - m_new);
-        sc[i][t] = p;
-        sum += p;
-      }
-      sum = warp_sum(sum);
-      __syncwarp();
-      if (lane == 0) {
-        const float al = expf(m_old - m_new);
-        alpha_s[i] = al;
-        l_s[i] = l_s[i] * al + sum;
-        m_s[i] = m_new;
-      }
-    }
-    __syncthreads();
-    for (int i = 0; i < G; i++) acc[i] *= alpha_s[i];
-    // P.V: thread (e, grp) accumulates keys t == grp (mod NG)
-    for (int t = grp; t < n; t += NG) {
-      const float v = kv_load(static_cast<const KT*>(a.vbase) + kv_off(a, seq, tb + t, g, HD) + e_pv);
-      for (int i = 0; i < G; i++) acc[i] = fmaf(sc[i][t], v, acc[i]);
-    }
-    __syncthreads();
+    for (int e = 0; e < EPL; e++) qv[i][e] = i < G ? qs[i][lane * EPL + e] : 0.f;
+  float m_w[GM], l_w[GM], acc[GM][EPL];
+#pragma unroll
+  for (int i = 0; i < GM; i++) {
+    m_w[i] = -INFINITY;
+    l_w[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; e++) acc[i][e] = 0.f;
   }
 
-  if constexpr (NG > 1) {
-    for (int i = 0; i < G; i++) accx[grp][i][e_pv] = acc[i];
-    __syncthreads();
-    if (grp == 0)
-      for (int i = 0; i < G; i++) {
-        float t = 0.f;
-        for (int q = 0; q < NG; q++) t += accx[q][i][e_pv];
-        acc[i] = t;
+  const KT* kb = static_cast<const KT*>(a.kbase);
+  const KT* vb = static_cast<const KT*>(a.vbase);
+  const int n_chunks = (t1 - t0 + KC - 1) / KC;
+  for (int c = warp; c < n_chunks; c += kWarpsA) {
+    const int base = t0 + c * KC;
+    float kv[KC][EPL], vv[KC][EPL];
+#pragma unroll
+    for (int j = 0; j < KC; j++) {
+      if (base + j < t1) {
+        const size_t off = kv_off(a, seq, base + j, g, HD) + lane * EPL;
+        kv_load_row<EPL>(kb + off, kv[j]);
+        kv_load_row<EPL>(vb + off, vv[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; e++) kv[j][e] = vv[j][e] = 0.f;
       }
+    }
+    float sc[KC][GM];
+#pragma unroll
+    for (int j = 0; j < KC; j++)
+#pragma unroll
+      for (int i = 0; i < GM; i++) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) d = fmaf(qv[i][e], kv[j][e], d);
+        sc[j][i] = d;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < KC; j++)
+#pragma unroll
+        for (int i = 0; i < GM; i++) sc[j][i] += __shfl_xor_sync(0xffffffffu, sc[j][i], o);
+#pragma unroll
+    for (int i = 0; i < GM; i++) {
+      float cmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < KC; j++) {
+        sc[j][i] = base + j < t1 ? __fmul_rn(sc[j][i], a.scale) : -INFINITY;
+        cmax = fmaxf(cmax, sc[j][i]);
+      }
+      const float m_new = fmaxf(m_w[i], cmax);
+      const float alpha = expf(m_w[i] - m_new);
+      float lsum = l_w[i] * alpha;
+#pragma unroll
+      for (int e = 0; e < EPL; e++) acc[i][e] *= alpha;
+#pragma unroll
+      for (int j = 0; j < KC; j++) {
+        const float p = base + j < t1 ? expf(sc[j][i] - m_new) : 0.f;
+        lsum += p;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) acc[i][e] = fmaf(p, vv[j][e], acc[i][e]);
+      }
+      l_w[i] = lsum;
+      m_w[i] = m_new;
+    }
+  }
+
+  // merge the warps of this CTA
+#pragma unroll
+  for (int i = 0; i < GM; i++) {
+    if (lane == 0) {
+      wm[warp][i] = m_w[i];
+      wl[warp][i] = l_w[i];
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; e++) wacc[warp][i][lane * EPL + e] = acc[i][e];
+  }
+  __syncthreads();
+  const int e_t = threadIdx.x % HD;   // element handled by this thread in the merges
+  const int i_t0 = threadIdx.x / HD;  // first head handled by this thread
+  constexpr int HSTEP = kAttnThreads / HD;
+  float cta_m[GM], cta_l[GM], cta_o[GM];
+#pragma unroll
+  for (int i = 0; i < GM; i++) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarpsA; w++) M = fmaxf(M, wm[w][i]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarpsA; w++) {
+        const float f = expf(wm[w][i] - M);
+        L = fmaf(wl[w][i], f, L);
+        O = fmaf(wacc[w][i][e_t], f, O);
+      }
+    }
+    cta_m[i] = M;
+    cta_l[i] = L;
+    cta_o[i] = O;
   }
 
   float* out = a.out + (size_t)m * a.H * HD + (size_t)g * G * HD;
   if (a.n_split == 1) {
-    if (grp == 0)
-      for (int i = 0; i < G; i++) out[(size_t)i * HD + e_pv] = __fdiv_rn(acc[i], l_s[i]);
+#pragma unroll
+    for (int i = 0; i < GM; i++)
+      if (i < G && (i % HSTEP) == i_t0) out[(size_t)i * HD + e_t] = __fdiv_rn(cta_o[i], cta_l[i]);
     return;
   }
 
   // split partial: per head [m, l, acc[HD]]
   const size_t stride_h = HD + 2;
   float* part = a.part + (((size_t)m * a.Hkv + g) * a.n_split + s) * G * stride_h;
-  if (threadIdx.x < G) {
-    part[threadIdx.x * stride_h + 0] = m_s[threadIdx.x];
-    part[threadIdx.x * stride_h + 1] = l_s[threadIdx.x];
-  }
-  if (grp == 0)
-    for (int i = 0; i < G; i++) part[i * stride_h + 2 + e_pv] = acc[i];
+#pragma unroll
+  for (int i = 0; i < GM; i++)
+    if (i < G && (i % HSTEP) == i_t0) {
+      if (e_t == 0) {
+        part[i * stride_h + 0] = cta_m[i];
+        part[i * stride_h + 1] = cta_l[i];
+      }
+      part[i * stride_h + 2 + e_t] = cta_o[i];
+    }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -244,21 +287,36 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  const float* base = a.part + ((size_t)m * a.Hkv + g) * a.n_split * G * stride_h;
-  if (grp == 0) {
-    for (int i = 0; i < G; i++) {
-      float M = -INFINITY;
-      for (int q = 0; q < a.n_split; q++) M = fmaxf(M, __ldcg(base + ((size_t)q * G + i) * stride_h));
-      float L = 0.f, O = 0.f;
-      for (int q = 0; q < a.n_split; q++) {
-        const float* p = base + ((size_t)q * G + i) * stride_h;
-        const float w = expf(__ldcg(p) - M);
-        L = fmaf(__ldcg(p + 1), w, L);
-        O = fmaf(__ldcg(p + 2 + e_pv), w, O);
-      }
-      out[(size_t)i * HD + e_pv] = __fdiv_rn(O, L);
-    }
+  // merge the splits: stage every split's (m, l), turn them into weights per head, then
+  // each thread sums its element over the splits with independent loads
+  const float* pbase = a.part + ((size_t)m * a.Hkv + g) * a.n_split * G * stride_h;
+  for (int t = threadIdx.x; t < a.n_split * G; t += kAttnThreads) {
+    const int q = t / G, i = t % G;
+    wq[q][i] = __ldcg(pbase + ((size_t)q * G + i) * stride_h);
+    lq[q][i] = __ldcg(pbase + ((size_t)q * G + i) * stride_h + 1);
   }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int i = threadIdx.x;
+    float M = -INFINITY;
+    for (int q = 0; q < a.n_split; q++) M = fmaxf(M, wq[q][i]);
+    float L = 0.f;
+    for (int q = 0; q < a.n_split; q++) {
+      const float w = expf(wq[q][i] - M);
+      wq[q][i] = w;
+      L = fmaf(lq[q][i], w, L);
+    }
+    inv_l[i] = L;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < GM; i++)
+    if (i < G && (i % HSTEP) == i_t0) {
+      float O = 0.f;
+#pragma unroll 8
+      for (int q = 0; q < a.n_split; q++) O = fmaf(__ldcg(pbase + ((size_t)q * G + i) * stride_h + 2 + e_t), wq[q][i], O);
+      out[(size_t)i * HD + e_t] = __fdiv_rn(O, inv_l[i]);
+    }
   if (threadIdx.x == 0) a.counters[(size_t)m * a.Hkv + g] = 0;
 }
 
@@ -275,8 +333,13 @@ __global__ void __launch_bounds__(32) k_kv_append(const AttnArgs a) {
   append_kv<HD, KT>(a, m, seq, pos, g, buf, threadIdx.x);
 }
 
-cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
-  return launch_cfg(grid, block, 0, st, attr);
+template <int HD, typename KT>
+cudaError_t launch_attention_hd(const AttnArgs& a, cudaLaunchConfig_t& cfg) {
+  const int G = a.H / a.Hkv;
+  if (G <= 1) return cudaLaunchKernelEx(&cfg, k_attention<HD, KT, 1>, a);
+  if (G <= 2) return cudaLaunchKernelEx(&cfg, k_attention<HD, KT, 2>, a);
+  if (G <= 4) return cudaLaunchKernelEx(&cfg, k_attention<HD, KT, 4>, a);
+  return cudaLaunchKernelEx(&cfg, k_attention<HD, KT, 8>, a);
 }
 
 }  // namespace
@@ -285,21 +348,19 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
   if (a.H % a.Hkv || a.H / a.Hkv > kMaxGroup || a.n_split < 1 || a.n_split > kMaxSplit)
     return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.M, a.Hkv, a.n_split), dim3(kAttnThreads), st, attr);
+  cudaLaunchConfig_t cfg = launch_cfg(dim3(a.M, a.Hkv, a.n_split), dim3(kAttnThreads), 0, st, attr);
   switch (a.hd) {
-    case 32: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_attention<32, float>, a)
-                             : cudaLaunchKernelEx(&cfg, k_attention<32, __nv_bfloat16>, a);
-    case 64: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_attention<64, float>, a)
-                             : cudaLaunchKernelEx(&cfg, k_attention<64, __nv_bfloat16>, a);
-    case 128: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_attention<128, float>, a)
-                              : cudaLaunchKernelEx(&cfg, k_attention<128, __nv_bfloat16>, a);
+    case 32: return a.kv_f32 ? launch_attention_hd<32, float>(a, cfg) : launch_attention_hd<32, __nv_bfloat16>(a, cfg);
+    case 64: return a.kv_f32 ? launch_attention_hd<64, float>(a, cfg) : launch_attention_hd<64, __nv_bfloat16>(a, cfg);
+    case 128:
+      return a.kv_f32 ? launch_attention_hd<128, float>(a, cfg) : launch_attention_hd<128, __nv_bfloat16>(a, cfg);
   }
   return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3(a.M, a.Hkv), dim3(32), st, attr);
+  cudaLaunchConfig_t cfg = launch_cfg(dim3(a.M, a.Hkv), dim3(32), 0, st, attr);
   switch (a.hd) {
     case 32: return a.kv_f32 ? cudaLaunchKernelEx(&cfg, k_kv_append<32, float>, a)
                              : cudaLaunchKernelEx(&cfg, k_kv_append<32, __nv_bfloat16>, a);

@@ -8,16 +8,20 @@
 //   epilogue  + bias, residual add (s2/slow_ar.rs:195,198), SiLU(g)*u (s2/nn.rs:452-457),
 //             or the greedy argmax of the head (sampling.rs:189-245 with top_k = 1).
 //
-// Memory-bound design (one pass over the weights, HBM roofline):
-//   * a warp owns RPW weight rows; each lane streams 128-bit chunks of those rows with
-//     ld.global.nc.L1::no_allocate, UNROLL chunks per row in flight;
+// Memory-bound design (one pass over the weights at the HBM roofline):
+//   * persistent grid: 1-2 CTAs of 8 warps per SM, each CTA owning a contiguous,
+//     balanced range of row groups (RPW rows), so x is staged (and RMS-normalised) once per
+//     CTA and every SM streams the same number of bytes;
+//   * the CTA's work is split into items (row group, 512-element k-chunk); each warp takes a
+//     contiguous run of items and streams them with 128-bit ld.global.nc.L1::no_allocate
+//     loads, ping-ponging two register buffers so the next item's weights are in flight
+//     while the current one is multiplied;
 //   * Q8_0 / Q4_K values are unpacked in registers (byte-permute into the 2^23 mantissa,
-//     exact) and multiplied on the packed f32x2 FMA pipe against x held in shared memory;
-//   * per-block scales are applied to 16/32-element partial dots; fp32 accumulation;
-//   * the cross-lane reduction is a warp shuffle butterfly;
-//   * the first weight chunks are requested before griddepcontrol.wait, so with
-//     programmatic dependent launch the weight stream of this kernel overlaps the tail of
-//     the kernel that produces x.
+//     exact) and multiplied on the packed f32x2 FMA pipe against x in shared memory;
+//   * a warp-shuffle reduction per run of items, partial sums per (row, k-chunk) in shared
+//     memory, then a fixed-order sum in the epilogue (deterministic for a given grid);
+//   * the first weight items are requested before griddepcontrol.wait, so under
+//     programmatic dependent launch they stream while the producer of x drains.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -28,7 +32,7 @@
 namespace sx {
 namespace {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
 // Elements covered by one lane-chunk (16 bytes of packed weights).
@@ -163,50 +167,117 @@ __device__ __forceinline__ void frag_dot(const Frag<WT>& f, const float* xs, int
   }
 }
 
-template <int WT, int M, int RPW, int UNROLL, int EPI>
+// Per-CTA work geometry shared by the loader, the compute loop and the epilogue.
+struct Geo {
+  int K, units, n_kc, n_logical, rg0, rg1, it0, it1;
+};
+
+template <int WT, int RPW>
+__device__ __forceinline__ void item_rows(const GemvArgs& a, const Geo& g, int item, int lane, int (&prow)[RPW],
+                                          int& unit, int& rg, int& kc) {
+  rg = g.rg0 + item / g.n_kc;
+  kc = item % g.n_kc;
+  unit = kc * 32 + lane;
+#pragma unroll
+  for (int r = 0; r < RPW; r++) {
+    const int i = rg * RPW + r;
+    prow[r] = phys_row(a, i < g.n_logical ? i : g.n_logical - 1);
+  }
+}
+
+template <int WT, int RPW, int B>
+__device__ __forceinline__ void load_group(const GemvArgs& a, const Geo& g, int base, int lane,
+                                           Frag<WT> (&f)[B][RPW]) {
+#pragma unroll
+  for (int b = 0; b < B; b++) {
+    const int item = base + b;
+    if (item < g.it1) {
+      int prow[RPW], unit, rg, kc;
+      item_rows<WT, RPW>(a, g, item, lane, prow, unit, rg, kc);
+      if (unit < g.units)
+#pragma unroll
+        for (int r = 0; r < RPW; r++) load_frag<WT>(a, prow[r], unit, f[b][r]);
+    }
+  }
+}
+
+// Flush a run of items of row group rg (started at k-chunk kc0) into the partial sums.
+template <int RPW, int M>
+__device__ __forceinline__ void flush(float (&acc)[RPW][M], float* part, const Geo& g, int rg, int kc0, int lane) {
+#pragma unroll
+  for (int r = 0; r < RPW; r++)
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const float v = warp_sum(acc[r][m]);
+      if (lane == 0) part[(((rg - g.rg0) * RPW + r) * g.n_kc + kc0) * M + m] = v;
+      acc[r][m] = 0.f;
+    }
+}
+
+template <int WT, int M, int RPW, int B>
+__device__ __forceinline__ void compute_group(const GemvArgs& a, const Geo& g, int base, int lane,
+                                              const Frag<WT> (&f)[B][RPW], const float* xs, const float* xsum16,
+                                              float* part, float (&acc)[RPW][M], int& cur_rg, int& run_kc0) {
+#pragma unroll
+  for (int b = 0; b < B; b++) {
+    const int item = base + b;
+    if (item < g.it1) {
+      int prow[RPW], unit, rg, kc;
+      item_rows<WT, RPW>(a, g, item, lane, prow, unit, rg, kc);
+      if (rg != cur_rg) {
+        if (cur_rg >= 0) flush<RPW, M>(acc, part, g, cur_rg, run_kc0, lane);
+        cur_rg = rg;
+        run_kc0 = kc;
+      }
+      if (unit < g.units)
+#pragma unroll
+        for (int r = 0; r < RPW; r++) frag_dot<WT, M>(f[b][r], xs, g.K, unit, xsum16, acc[r]);
+    }
+  }
+}
+
+template <int WT, int M, int RPW, int B, int EPI>
 __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
   constexpr int UE = Unit<WT>::elems;
-  const int K = (int)a.w.cols;
-  const int units = K / UE;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_logical = a.n_range + a.n_extra;
-  const int row0 = (blockIdx.x * kWarps + warp) * RPW;
+  Geo g;
+  g.K = (int)a.w.cols;
+  g.units = g.K / UE;
+  g.n_kc = (g.units + 31) / 32;
+  g.n_logical = a.n_range + a.n_extra;
+  const int n_rg = (g.n_logical + RPW - 1) / RPW;
+  g.rg0 = (int)((long long)blockIdx.x * n_rg / gridDim.x);
+  g.rg1 = (int)((long long)(blockIdx.x + 1) * n_rg / gridDim.x);
+  const int n_items = (g.rg1 - g.rg0) * g.n_kc;
+  g.it0 = (int)((long long)warp * n_items / kWarps);
+  g.it1 = (int)((long long)(warp + 1) * n_items / kWarps);
 
   pdl_launch_dependents();
 
-  int prow[RPW];
-#pragma unroll
-  for (int r = 0; r < RPW; r++) {
-    const int i = row0 + r;
-    prow[r] = phys_row(a, i < n_logical ? i : n_logical - 1);
-  }
-
-  // First weight chunks do not depend on the previous kernel: request them now.
-  Frag<WT> fr[UNROLL][RPW];
-#pragma unroll
-  for (int u = 0; u < UNROLL; u++) {
-    const int unit = u * 32 + lane;
-    if (unit < units)
-#pragma unroll
-      for (int r = 0; r < RPW; r++) load_frag<WT>(a, prow[r], unit, fr[u][r]);
-  }
+  // The first weight items do not depend on the previous kernel: request them now.
+  Frag<WT> fa[B][RPW], fb[B][RPW];
+  load_group<WT, RPW, B>(a, g, g.it0, lane, fa);
 
   pdl_wait();
 
-  // ---- stage x (optionally RMS-normalised) into shared memory ----
-  float* xs = smem;                       // [M][K]
-  float* xsum16 = smem + (size_t)M * K;   // [M][K/16] (Q4_K only)
+  // ---- shared memory: x [M][K] | xsum16 [M][K/16] (Q4_K) | partials [rows][n_kc][M] ----
+  float* xs = smem;
+  float* xsum16 = xs + (size_t)M * g.K;
+  float* part = xsum16 + (WT == SX_DTYPE_Q4_K ? (size_t)M * (g.K / 16) : 0);
+  const int rows_cta = (g.rg1 - g.rg0) * RPW;
   __shared__ float red[kWarps][kMaxTok];
   __shared__ float den[kMaxTok];
+  for (int i = threadIdx.x; i < rows_cta * g.n_kc * M; i += kThreads) part[i] = 0.f;
   if (a.norm_w) {
     float ss[M];
 #pragma unroll
     for (int m = 0; m < M; m++) ss[m] = 0.f;
-    for (int k = threadIdx.x; k < K; k += kThreads)
+    for (int k = threadIdx.x; k < g.K; k += kThreads)
 #pragma unroll
       for (int m = 0; m < M; m++) {
-        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
+        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
+        xs[(size_t)m * g.K + k] = v;
         ss[m] = fmaf(v, v, ss[m]);
       }
 #pragma unroll
@@ -219,88 +290,75 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
       float t = 0.f;
 #pragma unroll
       for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
-      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)K), a.eps));
+      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)g.K), a.eps));
     }
     __syncthreads();
-    for (int k = threadIdx.x; k < K; k += kThreads) {
-      const float g = a.norm_w[k];
+    for (int k = threadIdx.x; k < g.K; k += kThreads) {
+      const float gk = a.norm_w[k];
 #pragma unroll
       for (int m = 0; m < M; m++) {
-        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
-        xs[(size_t)m * K + k] = __fmul_rn(__fdiv_rn(v, den[m]), g);
+        float* p = xs + (size_t)m * g.K + k;
+        *p = __fmul_rn(__fdiv_rn(*p, den[m]), gk);
       }
     }
   } else {
-    const int nv = K / 4;
+    const int nv = g.K / 4;
     for (int i = threadIdx.x; i < nv; i += kThreads)
 #pragma unroll
       for (int m = 0; m < M; m++) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < a.M) v = ld_cg4(a.x + (size_t)m * K + 4 * i);
-        reinterpret_cast<float4*>(xs + (size_t)m * K)[i] = v;
+        if (m < a.M) v = ld_cg4(a.x + (size_t)m * g.K + 4 * i);
+        reinterpret_cast<float4*>(xs + (size_t)m * g.K)[i] = v;
       }
   }
   __syncthreads();
   if constexpr (WT == SX_DTYPE_Q4_K) {
-    for (int g = threadIdx.x; g < K / 16; g += kThreads)
+    for (int q = threadIdx.x; q < g.K / 16; q += kThreads)
 #pragma unroll
       for (int m = 0; m < M; m++) {
-        const float* p = xs + (size_t)m * K + g * 16;
+        const float* p = xs + (size_t)m * g.K + q * 16;
         float t = 0.f;
 #pragma unroll
         for (int e = 0; e < 16; e++) t += p[e];
-        xsum16[(size_t)m * (K / 16) + g] = t;
+        xsum16[(size_t)m * (g.K / 16) + q] = t;
       }
     __syncthreads();
   }
 
-  // ---- main loop over the row ----
+  // ---- stream this warp's items, two register buffers in ping-pong ----
   float acc[RPW][M];
 #pragma unroll
   for (int r = 0; r < RPW; r++)
 #pragma unroll
     for (int m = 0; m < M; m++) acc[r][m] = 0.f;
-
-  for (int base = 0; base < units; base += 32 * UNROLL) {
-    if (base > 0) {
-#pragma unroll
-      for (int u = 0; u < UNROLL; u++) {
-        const int unit = base + u * 32 + lane;
-        if (unit < units)
-#pragma unroll
-          for (int r = 0; r < RPW; r++) load_frag<WT>(a, prow[r], unit, fr[u][r]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < UNROLL; u++) {
-      const int unit = base + u * 32 + lane;
-      if (unit < units)
-#pragma unroll
-        for (int r = 0; r < RPW; r++) frag_dot<WT, M>(fr[u][r], xs, K, unit, xsum16, acc[r]);
+  int cur_rg = -1, run_kc0 = 0;
+  for (int base = g.it0; base < g.it1; base += 2 * B) {
+    if (base + B < g.it1) load_group<WT, RPW, B>(a, g, base + B, lane, fb);
+    compute_group<WT, M, RPW, B>(a, g, base, lane, fa, xs, xsum16, part, acc, cur_rg, run_kc0);
+    if (base + B < g.it1) {
+      if (base + 2 * B < g.it1) load_group<WT, RPW, B>(a, g, base + 2 * B, lane, fa);
+      compute_group<WT, M, RPW, B>(a, g, base + B, lane, fb, xs, xsum16, part, acc, cur_rg, run_kc0);
     }
   }
+  if (cur_rg >= 0) flush<RPW, M>(acc, part, g, cur_rg, run_kc0, lane);
+  __syncthreads();
 
-#pragma unroll
-  for (int r = 0; r < RPW; r++)
-#pragma unroll
-    for (int m = 0; m < M; m++) acc[r][m] = warp_sum(acc[r][m]);
-
-  // ---- epilogues ----
+  // ---- epilogue: fixed-order sum of the k-chunk partials of each row ----
+  const int row_lo = g.rg0 * RPW;
+  auto row_sum = [&](int rl, int m) {
+    float v = 0.f;
+    for (int kc = 0; kc < g.n_kc; kc++) v += part[(rl * g.n_kc + kc) * M + m];
+    return v;
+  };
   if constexpr (EPI == EPI_SWIGLU) {
-    // rows (row0 + 2p, row0 + 2p + 1) = (gate_j, up_j) with j = (row0 + 2p) / 2
-    if (lane == 0) {
-#pragma unroll
-      for (int p = 0; p < RPW / 2; p++) {
-        const int i = row0 + 2 * p;
-        if (i + 1 < n_logical) {
-          const int j = i >> 1;
-#pragma unroll
-          for (int m = 0; m < M; m++)
-            if (m < a.M) {
-              const float g = acc[2 * p][m], u = acc[2 * p + 1][m];
-              a.y[(size_t)m * a.ldy + j] = __fmul_rn(silu_f(g), u);
-            }
-        }
+    // logical rows (2j, 2j+1) = (gate_j, up_j)
+    const int pairs = rows_cta / 2;
+    for (int t = threadIdx.x; t < pairs * M; t += kThreads) {
+      const int p = t / M, m = t % M;
+      const int i = row_lo + 2 * p;
+      if (m < a.M && i + 1 < g.n_logical) {
+        const float gv = row_sum(2 * p, m), uv = row_sum(2 * p + 1, m);
+        a.y[(size_t)m * a.ldy + (i >> 1)] = __fmul_rn(silu_f(gv), uv);
       }
     }
   } else if constexpr (EPI == EPI_ARGMAX) {
@@ -308,89 +366,105 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
     unsigned long long bk[M];
 #pragma unroll
     for (int m = 0; m < M; m++) bk[m] = 0ull;
-    if (lane == 0) {
+    for (int rl = threadIdx.x; rl < rows_cta; rl += kThreads) {
+      const int i = row_lo + rl;
+      if (i >= g.n_logical) continue;
+      const uint32_t pr = (uint32_t)phys_row(a, i);
+      const bool allowed = (pr >= a.allow_lo && pr <= a.allow_hi) || (pr >= a.stop_lo && pr < a.stop_hi);
 #pragma unroll
-      for (int r = 0; r < RPW; r++) {
-        const int i = row0 + r;
-        if (i < n_logical) {
-          const uint32_t pr = (uint32_t)prow[r];
-          const bool allowed = (pr >= a.allow_lo && pr <= a.allow_hi) || (pr >= a.stop_lo && pr < a.stop_hi);
-#pragma unroll
-          for (int m = 0; m < M; m++)
-            if (m < a.M) {
-              float v = acc[r][m];
-              if (a.bias) v = __fadd_rn(v, a.bias[pr]);
-              if (a.y) a.y[(size_t)m * a.ldy + pr] = v;
-              if (allowed) {
-                const unsigned long long key = argmax_key(v, pr);
-                bk[m] = key > bk[m] ? key : bk[m];
-              }
-            }
+      for (int m = 0; m < M; m++)
+        if (m < a.M) {
+          float v = row_sum(rl, m);
+          if (a.bias) v = __fadd_rn(v, a.bias[pr]);
+          if (a.y) a.y[(size_t)m * a.ldy + pr] = v;
+          if (allowed) {
+            const unsigned long long key = argmax_key(v, pr);
+            bk[m] = key > bk[m] ? key : bk[m];
+          }
         }
-      }
+    }
 #pragma unroll
-      for (int m = 0; m < M; m++) best[warp][m] = bk[m];
+    for (int m = 0; m < M; m++) {
+      unsigned long long b = bk[m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+        b = other > b ? other : b;
+      }
+      if (lane == 0) best[warp][m] = b;
     }
     __syncthreads();
     if (threadIdx.x < a.M && threadIdx.x < M) {
       unsigned long long b = 0ull;
 #pragma unroll
       for (int w = 0; w < kWarps; w++) b = best[w][threadIdx.x] > b ? best[w][threadIdx.x] : b;
-      if (b != 0ull) {
-        atomicMax(a.amax + threadIdx.x, b);
-      }
+      if (b != 0ull) atomicMax(a.amax + threadIdx.x, b);
     }
   } else {
-    if (lane == 0) {
-#pragma unroll
-      for (int r = 0; r < RPW; r++) {
-        const int i = row0 + r;
-        if (i < n_logical) {
-          const int pr = prow[r];
-#pragma unroll
-          for (int m = 0; m < M; m++)
-            if (m < a.M) {
-              float v = acc[r][m];
-              if (a.bias) v = __fadd_rn(v, a.bias[pr]);
-              float* dst = a.y + (size_t)m * a.ldy + pr;
-              if constexpr (EPI == EPI_ADD)
-                *dst = __fadd_rn(ld_cg(dst), v);
-              else
-                *dst = v;
-            }
-        }
+    for (int t = threadIdx.x; t < rows_cta * M; t += kThreads) {
+      const int rl = t / M, m = t % M;
+      const int i = row_lo + rl;
+      if (m < a.M && i < g.n_logical) {
+        const int pr = phys_row(a, i);
+        float v = row_sum(rl, m);
+        if (a.bias) v = __fadd_rn(v, a.bias[pr]);
+        float* dst = a.y + (size_t)m * a.ldy + pr;
+        if constexpr (EPI == EPI_ADD)
+          *dst = __fadd_rn(ld_cg(dst), v);
+        else
+          *dst = v;
       }
     }
   }
 }
 
-template <int WT, int M, int RPW, int UNROLL, int EPI>
+int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int WT, int M, int RPW, int B, int EPI>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
+  constexpr int UE = Unit<WT>::elems;
   const int n_logical = a.n_range + a.n_extra;
-  const int rows_per_cta = kWarps * RPW;
   const int K = (int)a.w.cols;
-  size_t smem = (size_t)M * K * sizeof(float);
-  if (WT == SX_DTYPE_Q4_K) smem += (size_t)M * (K / 16) * sizeof(float);
-  auto kern = k_gemv<WT, M, RPW, UNROLL, EPI>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int n_kc = (K / UE + 31) / 32;
+  const int n_rg = (n_logical + RPW - 1) / RPW;
+  const size_t x_bytes = (size_t)M * K * sizeof(float) + (WT == SX_DTYPE_Q4_K ? (size_t)M * (K / 16) * sizeof(float) : 0);
+  // persistent grid: as many CTAs as are co-resident (registers and shared memory),
+  // at most two per SM, so every CTA streams an equal share in a single wave
+  static const int sms = num_sms();
+  auto kern = k_gemv<WT, M, RPW, B, EPI>;
+  int grid = std::min(n_rg, 2 * sms);
+  size_t smem = 0;
+  for (int attempt = 0; attempt < 2; attempt++) {
+    smem = x_bytes + (size_t)((n_rg + grid - 1) / grid) * RPW * n_kc * M * sizeof(float);
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    int occ = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
     if (e != cudaSuccess) return e;
+    if (occ >= 2 || grid <= sms) break;
+    grid = std::min(n_rg, sms);  // one CTA per SM: re-size the partial buffer for it
   }
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg =
-      launch_cfg(dim3((n_logical + rows_per_cta - 1) / rows_per_cta), dim3(kThreads), smem, st, attr);
+  cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kThreads), smem, st, attr);
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 template <int WT, int M>
 cudaError_t dispatch_epi(const GemvArgs& a, Epi epi, cudaStream_t st) {
-  // Q8_0: 2 rows per warp, 4 chunks (2 KB of weights per warp) in flight.
-  constexpr int U = WT == SX_DTYPE_F32 ? 8 : (WT == SX_DTYPE_Q4_K ? 2 : 4);
+  // items in flight per register buffer: 4 for batch-1 Q8_0 / F32, else 2
+  constexpr int B = (M == 1 && WT != SX_DTYPE_Q4_K) ? 4 : 2;
   switch (epi) {
-    case EPI_STORE: return launch_t<WT, M, 2, U, EPI_STORE>(a, st);
-    case EPI_ADD: return launch_t<WT, M, 2, U, EPI_ADD>(a, st);
-    case EPI_SWIGLU: return launch_t<WT, M, 2, U, EPI_SWIGLU>(a, st);
-    case EPI_ARGMAX: return launch_t<WT, M, 2, U, EPI_ARGMAX>(a, st);
+    case EPI_STORE: return launch_t<WT, M, 2, B, EPI_STORE>(a, st);
+    case EPI_ADD: return launch_t<WT, M, 2, B, EPI_ADD>(a, st);
+    case EPI_SWIGLU: return launch_t<WT, M, 2, B, EPI_SWIGLU>(a, st);
+    case EPI_ARGMAX: return launch_t<WT, M, 2, B, EPI_ARGMAX>(a, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -407,10 +481,15 @@ cudaError_t dispatch_m(const GemvArgs& a, Epi epi, cudaStream_t st) {
 
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
   if (a.M < 1 || a.M > kMaxTok || a.n_range + a.n_extra < 1) return cudaErrorInvalidValue;
-  // x of all M tokens is staged in shared memory, sized by the kernel's template M
-  // (1, 2, 4 or 8): split the tokens into launches whose template fits in 200 KB
+  // x and the row partial sums of all M tokens live in shared memory, sized by the
+  // kernel's template M (1, 2, 4 or 8): split the tokens into launches that fit
   const size_t K = (size_t)a.w.cols;
-  const size_t per_tok = K * 4 + (a.w.dtype == SX_DTYPE_Q4_K ? (K / 16) * 4 : 0);
+  const int ue = a.w.dtype == SX_DTYPE_Q8_0 ? 16 : (a.w.dtype == SX_DTYPE_Q4_K ? 32 : 4);
+  const size_t n_kc = (K / ue + 31) / 32;
+  const size_t n_rg = (size_t)(a.n_range + a.n_extra + 1) / 2;
+  static const int sms = num_sms();
+  const size_t per_tok = K * 4 + (a.w.dtype == SX_DTYPE_Q4_K ? (K / 16) * 4 : 0) +
+                         ((n_rg + sms - 1) / sms) * 2 * n_kc * 4;
   int max_m = kMaxTok;
   while (max_m > 1 && (size_t)max_m * per_tok > 200 * 1024) max_m >>= 1;
   for (int m0 = 0; m0 < a.M; m0 += max_m) {

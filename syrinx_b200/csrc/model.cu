@@ -398,11 +398,11 @@ int session_reset(sx_session* s) {
 
 namespace {
 
-int n_split_for(const sx_session* s, int M, int Hkv) {
-  int S = std::max(1, (2 * 148) / std::max(1, M * Hkv));
-  S = std::min(S, kMaxSplit);
-  S = std::min(S, std::max(1, s->max_ctx / 32));
-  return S;
+// Splits of the key axis: about 64 keys per CTA at the session's longest context, i.e.
+// two 8-key chunks per warp, so each CTA pays about two memory latencies; long contexts
+// get up to kMaxSplit CTAs per (token, kv head).
+int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
+  return std::max(1, std::min(kMaxSplit, (s->max_ctx + 63) / 64));
 }
 
 int gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {

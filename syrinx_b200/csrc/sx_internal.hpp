@@ -28,7 +28,7 @@ namespace sx {
 constexpr int kPage = 64;         // KV positions per page
 constexpr int kMaxTok = 8;        // max tokens per GEMV launch (batched decode / prefill chunk)
 constexpr int kAttnThreads = 128;
-constexpr int kMaxSplit = 32;     // max split-K partitions of the attention sequence axis
+constexpr int kMaxSplit = 64;     // max split-K partitions of the attention sequence axis
 constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one CTA
 
 struct DevMat {

@@ -1,0 +1,41 @@
+"""Profiling driver: runs the batch-1 decode GEMV (or a few greedy frames) of the
+Qwen3-4B-shaped model with fewer layers, so an `ncu --set full` capture stays small
+(the weights still exceed L2, so DRAM counters are meaningful).
+
+  python -m syrinx_b200.profile --what gemv --kind 2 --layers 8 --launches 16
+  python -m syrinx_b200.profile --what frames --layers 8 --frames 4
+"""
+from __future__ import annotations
+
+import argparse
+
+from . import QWEN3_4B, B200DualAr, Model, shrink, synth_blob
+from .configs import SX_DTYPE_Q4_K, SX_DTYPE_Q8_0
+from .workloads import dual_ar_prompt
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--what", choices=["gemv", "frames"], default="gemv")
+    ap.add_argument("--kind", type=int, default=2, help="0 wqkv, 1 wo, 2 w1|w3, 3 w2")
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--launches", type=int, default=16)
+    ap.add_argument("--frames", type=int, default=4)
+    ap.add_argument("--q4k", action="store_true")
+    args = ap.parse_args()
+    cfg = shrink(QWEN3_4B, args.layers, min(4, args.layers))
+    wtype = SX_DTYPE_Q4_K if args.q4k else SX_DTYPE_Q8_0
+    model = Model(cfg, synth_blob(cfg, wtype, seed=2))
+    be = B200DualAr(model, max_ctx=64 + args.frames)
+    be.prefill(dual_ar_prompt(cfg, 8, 6, seed=2))
+    if args.what == "gemv":
+        be.profile_gemv(args.kind, args.launches)  # close() below synchronizes the stream
+    else:
+        be.decode_greedy(args.frames, mask_stop=True)
+    be.close()
+    model.close()
+    print("profile run ok")
+
+
+if __name__ == "__main__":
+    main()
