@@ -222,7 +222,7 @@ def bench_device(args):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "q8_0 weights, f32 activations/accumulation, bf16 KV",
+        "dtype": "q8_0 weights, f32 activations/accumulation, f32 KV",
         "data": "synthetic (seeded N(0,0.02)-like weights quantized to Q8_0; random prompt ids)",
         "config": {"workload": "config3 qwen3-4b-shaped dual-AR Q8_0 b1: prompt 512 (430 semantic), "
                                "greedy frames, stop masked", "global_batch": world, "seq_len": PROMPT_T,

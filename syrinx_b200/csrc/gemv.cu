@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "sx_device.cuh"
 #include "sx_internal.hpp"
@@ -64,7 +65,7 @@ __device__ __forceinline__ void load_frag(const GemvArgs& a, int prow, int unit,
   if constexpr (WT == SX_DTYPE_Q8_0) {
     const int8_t* q = (const int8_t*)a.w.q + (size_t)prow * K + (size_t)unit * 16;
     f.q = ldg_stream(q);
-    f.d = __half2float(a.w.s[(size_t)prow * (K / 32) + (unit >> 1)]);
+    f.d = __half2float(a.w.s[(size_t)prow * a.w.s_stride + (unit >> 1)]);
   } else if constexpr (WT == SX_DTYPE_Q4_K) {
     const uint8_t* q = (const uint8_t*)a.w.q + (size_t)prow * (K / 2) + (size_t)unit * 16;
     f.q = ldg_stream(q);
@@ -89,10 +90,54 @@ __device__ __forceinline__ void q4k_sm(const uint8_t* sc12, int j, float& sc, fl
   m = (float)mm;
 }
 
-// Dot of one fragment with M token vectors held in shared memory.
+// x fragment of one lane-unit for M tokens (read from shared memory once, shared by the
+// RPW rows of a row group).
+template <int WT, int M> struct XFrag;
+template <int M> struct XFrag<SX_DTYPE_Q8_0, M> {
+  ulonglong2 v[M][4];  // 16 f32 as 8 f32x2
+};
+template <int M> struct XFrag<SX_DTYPE_Q4_K, M> {
+  ulonglong2 lo[M][4], hi[M][4];  // the low- and high-nibble runs of 16 elements
+  float slo[M], shi[M];           // their sums (for the sub-block minimum term)
+};
+template <int M> struct XFrag<SX_DTYPE_F32, M> {
+  ulonglong2 v[M];  // 4 f32 as 2 f32x2
+};
+
+// Q4_K unit u: super-block u/8, 16-byte chunk c = u%8 -> 64-group c/2, offset 16*(c%2)
+__device__ __forceinline__ int q4k_elem_lo(int unit) {
+  const int c = unit & 7;
+  return (unit >> 3) * 256 + (c >> 1) * 64 + (c & 1) * 16;
+}
+
 template <int WT, int M>
-__device__ __forceinline__ void frag_dot(const Frag<WT>& f, const float* xs, int K, int unit,
-                                         const float* xsum16, float (&acc)[M]) {
+__device__ __forceinline__ void load_x(const float* xs, int K, int unit, const float* xsum16, XFrag<WT, M>& x) {
+#pragma unroll
+  for (int m = 0; m < M; m++) {
+    if constexpr (WT == SX_DTYPE_Q8_0) {
+      const ulonglong2* p = (const ulonglong2*)(xs + (size_t)m * K + unit * 16);
+#pragma unroll
+      for (int j = 0; j < 4; j++) x.v[m][j] = p[j];
+    } else if constexpr (WT == SX_DTYPE_Q4_K) {
+      const int e = q4k_elem_lo(unit);
+      const ulonglong2* pl = (const ulonglong2*)(xs + (size_t)m * K + e);
+      const ulonglong2* ph = (const ulonglong2*)(xs + (size_t)m * K + e + 32);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        x.lo[m][j] = pl[j];
+        x.hi[m][j] = ph[j];
+      }
+      x.slo[m] = xsum16[(size_t)m * (K / 16) + (e >> 4)];
+      x.shi[m] = xsum16[(size_t)m * (K / 16) + ((e + 32) >> 4)];
+    } else {
+      x.v[m] = *(const ulonglong2*)(xs + (size_t)m * K + unit * 4);
+    }
+  }
+}
+
+// Dot of one weight fragment with the x fragment of M tokens, accumulated into acc.
+template <int WT, int M>
+__device__ __forceinline__ void frag_dot(const Frag<WT>& f, const XFrag<WT, M>& x, int unit, float (&acc)[M]) {
   if constexpr (WT == SX_DTYPE_Q8_0) {
     unsigned long long w[8];
     const uint32_t words[4] = {f.q.x, f.q.y, f.q.z, f.q.w};
@@ -100,24 +145,20 @@ __device__ __forceinline__ void frag_dot(const Frag<WT>& f, const float* xs, int
     for (int j = 0; j < 4; j++) i8x4_to_f32x2x2(words[j], w[2 * j], w[2 * j + 1]);
 #pragma unroll
     for (int m = 0; m < M; m++) {
-      const ulonglong2* xv = (const ulonglong2*)(xs + (size_t)m * K + unit * 16);
       unsigned long long s0 = 0, s1 = 0;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const ulonglong2 x2 = xv[j];
-        s0 = fma2(w[2 * j], x2.x, s0);
-        s1 = fma2(w[2 * j + 1], x2.y, s1);
+        s0 = fma2(w[2 * j], x.v[m][j].x, s0);
+        s1 = fma2(w[2 * j + 1], x.v[m][j].y, s1);
       }
       float a0, a1, b0, b1;
-      unpack2(s0, a0, a1);
-      unpack2(s1, b0, b1);
-      acc[m] = fmaf(f.d, (a0 + a1) + (b0 + b1), acc[m]);
+      unpack2(add2(s0, s1), a0, a1);
+      (void)b0;
+      (void)b1;
+      acc[m] = fmaf(f.d, a0 + a1, acc[m]);
     }
   } else if constexpr (WT == SX_DTYPE_Q4_K) {
-    // unit u: super-block sb = u/8, chunk c = u%8 -> 64-group j = c/2, offset l0 = 16*(c%2)
-    const int c = unit & 7;
-    const int jj = c >> 1;
-    const int e_lo = (unit >> 3) * 256 + jj * 64 + (c & 1) * 16;  // first low-nibble element
+    const int jj = (unit & 7) >> 1;
     const __half2 dd = *reinterpret_cast<const __half2*>(&f.meta.x);
     const float d = __low2float(dd), dmin = __high2float(dd);
     const uint8_t* sc12 = reinterpret_cast<const uint8_t*>(&f.meta) + 4;
@@ -134,32 +175,27 @@ __device__ __forceinline__ void frag_dot(const Frag<WT>& f, const float* xs, int
     }
 #pragma unroll
     for (int m = 0; m < M; m++) {
-      const ulonglong2* xl = (const ulonglong2*)(xs + (size_t)m * K + e_lo);
-      const ulonglong2* xh = (const ulonglong2*)(xs + (size_t)m * K + e_lo + 32);
       unsigned long long sl = 0, sh = 0;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const ulonglong2 a2 = xl[j], b2 = xh[j];
-        sl = fma2(wl[2 * j], a2.x, sl);
-        sl = fma2(wl[2 * j + 1], a2.y, sl);
-        sh = fma2(wh[2 * j], b2.x, sh);
-        sh = fma2(wh[2 * j + 1], b2.y, sh);
+        sl = fma2(wl[2 * j], x.lo[m][j].x, sl);
+        sl = fma2(wl[2 * j + 1], x.lo[m][j].y, sl);
+        sh = fma2(wh[2 * j], x.hi[m][j].x, sh);
+        sh = fma2(wh[2 * j + 1], x.hi[m][j].y, sh);
       }
       float a0, a1, b0, b1;
       unpack2(sl, a0, a1);
       unpack2(sh, b0, b1);
-      const float* xsm = xsum16 + (size_t)m * (K / 16);
-      float r = dl * (a0 + a1) - ml * xsm[e_lo >> 4];
-      r += dh * (b0 + b1) - mh * xsm[(e_lo + 32) >> 4];
+      float r = dl * (a0 + a1) - ml * x.slo[m];
+      r += dh * (b0 + b1) - mh * x.shi[m];
       acc[m] += r;
     }
   } else {
     const unsigned long long w0 = pack2u(f.q.x, f.q.y), w1 = pack2u(f.q.z, f.q.w);
 #pragma unroll
     for (int m = 0; m < M; m++) {
-      const ulonglong2 x2 = *(const ulonglong2*)(xs + (size_t)m * K + unit * 4);
-      unsigned long long s = fma2(w0, x2.x, 0ull);
-      s = fma2(w1, x2.y, s);
+      unsigned long long s = fma2(w0, x.v[m].x, 0ull);
+      s = fma2(w1, x.v[m].y, s);
       float a0, a1;
       unpack2(s, a0, a1);
       acc[m] += a0 + a1;
@@ -172,12 +208,13 @@ struct Geo {
   int K, units, n_kc, n_logical, rg0, rg1, it0, it1;
 };
 
+// Walk of a warp's items: (row group, k-chunk) advanced without divisions.
+struct Cursor {
+  int rg, kc, left;
+};
+
 template <int WT, int RPW>
-__device__ __forceinline__ void item_rows(const GemvArgs& a, const Geo& g, int item, int lane, int (&prow)[RPW],
-                                          int& unit, int& rg, int& kc) {
-  rg = g.rg0 + item / g.n_kc;
-  kc = item % g.n_kc;
-  unit = kc * 32 + lane;
+__device__ __forceinline__ void row_ptrs(const GemvArgs& a, const Geo& g, int rg, int (&prow)[RPW]) {
 #pragma unroll
   for (int r = 0; r < RPW; r++) {
     const int i = rg * RPW + r;
@@ -185,18 +222,26 @@ __device__ __forceinline__ void item_rows(const GemvArgs& a, const Geo& g, int i
   }
 }
 
+// Issue the loads of the next B items of the warp (those still to load).
 template <int WT, int RPW, int B>
-__device__ __forceinline__ void load_group(const GemvArgs& a, const Geo& g, int base, int lane,
-                                           Frag<WT> (&f)[B][RPW]) {
+__device__ __forceinline__ void load_group(const GemvArgs& a, const Geo& g, Cursor& c, int (&prow)[RPW], int& prow_rg,
+                                           int lane, Frag<WT> (&f)[B][RPW]) {
 #pragma unroll
   for (int b = 0; b < B; b++) {
-    const int item = base + b;
-    if (item < g.it1) {
-      int prow[RPW], unit, rg, kc;
-      item_rows<WT, RPW>(a, g, item, lane, prow, unit, rg, kc);
+    if (c.left > 0) {
+      if (c.rg != prow_rg) {
+        row_ptrs<WT, RPW>(a, g, c.rg, prow);
+        prow_rg = c.rg;
+      }
+      const int unit = c.kc * 32 + lane;
       if (unit < g.units)
 #pragma unroll
         for (int r = 0; r < RPW; r++) load_frag<WT>(a, prow[r], unit, f[b][r]);
+      if (++c.kc == g.n_kc) {
+        c.kc = 0;
+        c.rg++;
+      }
+      c.left--;
     }
   }
 }
@@ -215,27 +260,32 @@ __device__ __forceinline__ void flush(float (&acc)[RPW][M], float* part, const G
 }
 
 template <int WT, int M, int RPW, int B>
-__device__ __forceinline__ void compute_group(const GemvArgs& a, const Geo& g, int base, int lane,
-                                              const Frag<WT> (&f)[B][RPW], const float* xs, const float* xsum16,
-                                              float* part, float (&acc)[RPW][M], int& cur_rg, int& run_kc0) {
+__device__ __forceinline__ void compute_group(const Geo& g, Cursor& c, int lane, const Frag<WT> (&f)[B][RPW],
+                                              const float* xs, const float* xsum16, float* part,
+                                              float (&acc)[RPW][M], int& cur_rg, int& run_kc0) {
 #pragma unroll
   for (int b = 0; b < B; b++) {
-    const int item = base + b;
-    if (item < g.it1) {
-      int prow[RPW], unit, rg, kc;
-      item_rows<WT, RPW>(a, g, item, lane, prow, unit, rg, kc);
-      if (rg != cur_rg) {
+    if (c.left > 0) {
+      if (c.rg != cur_rg) {
         if (cur_rg >= 0) flush<RPW, M>(acc, part, g, cur_rg, run_kc0, lane);
-        cur_rg = rg;
-        run_kc0 = kc;
+        cur_rg = c.rg;
+        run_kc0 = c.kc;
       }
-      if (unit < g.units)
+      const int unit = c.kc * 32 + lane;
+      if (unit < g.units) {
+        XFrag<WT, M> x;
+        load_x<WT, M>(xs, g.K, unit, xsum16, x);
 #pragma unroll
-        for (int r = 0; r < RPW; r++) frag_dot<WT, M>(f[b][r], xs, g.K, unit, xsum16, acc[r]);
+        for (int r = 0; r < RPW; r++) frag_dot<WT, M>(f[b][r], x, unit, acc[r]);
+      }
+      if (++c.kc == g.n_kc) {
+        c.kc = 0;
+        c.rg++;
+      }
+      c.left--;
     }
   }
 }
-
 template <int WT, int M, int RPW, int B, int EPI>
 __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
@@ -256,8 +306,11 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
   pdl_launch_dependents();
 
   // The first weight items do not depend on the previous kernel: request them now.
+  Cursor lc{g.rg0 + g.it0 / g.n_kc, g.it0 % g.n_kc, g.it1 - g.it0};
+  Cursor cc = lc;
+  int prow[RPW], prow_rg = -1;
   Frag<WT> fa[B][RPW], fb[B][RPW];
-  load_group<WT, RPW, B>(a, g, g.it0, lane, fa);
+  load_group<WT, RPW, B>(a, g, lc, prow, prow_rg, lane, fa);
 
   pdl_wait();
 
@@ -332,12 +385,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a) {
 #pragma unroll
     for (int m = 0; m < M; m++) acc[r][m] = 0.f;
   int cur_rg = -1, run_kc0 = 0;
-  for (int base = g.it0; base < g.it1; base += 2 * B) {
-    if (base + B < g.it1) load_group<WT, RPW, B>(a, g, base + B, lane, fb);
-    compute_group<WT, M, RPW, B>(a, g, base, lane, fa, xs, xsum16, part, acc, cur_rg, run_kc0);
-    if (base + B < g.it1) {
-      if (base + 2 * B < g.it1) load_group<WT, RPW, B>(a, g, base + 2 * B, lane, fa);
-      compute_group<WT, M, RPW, B>(a, g, base + B, lane, fb, xs, xsum16, part, acc, cur_rg, run_kc0);
+  while (cc.left > 0) {
+    load_group<WT, RPW, B>(a, g, lc, prow, prow_rg, lane, fb);
+    compute_group<WT, M, RPW, B>(g, cc, lane, fa, xs, xsum16, part, acc, cur_rg, run_kc0);
+    if (cc.left > 0) {
+      load_group<WT, RPW, B>(a, g, lc, prow, prow_rg, lane, fa);
+      compute_group<WT, M, RPW, B>(g, cc, lane, fb, xs, xsum16, part, acc, cur_rg, run_kc0);
     }
   }
   if (cur_rg >= 0) flush<RPW, M>(acc, part, g, cur_rg, run_kc0, lane);
@@ -432,13 +485,14 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
   const int n_kc = (K / UE + 31) / 32;
   const int n_rg = (n_logical + RPW - 1) / RPW;
   const size_t x_bytes = (size_t)M * K * sizeof(float) + (WT == SX_DTYPE_Q4_K ? (size_t)M * (K / 16) * sizeof(float) : 0);
-  // persistent grid: as many CTAs as are co-resident (registers and shared memory),
-  // at most two per SM, so every CTA streams an equal share in a single wave
+  // persistent grid: as many CTAs as are co-resident (registers and shared memory, at
+  // most three per SM), so every CTA streams an equal share of the rows in a single wave
   static const int sms = num_sms();
   auto kern = k_gemv<WT, M, RPW, B, EPI>;
-  int grid = std::min(n_rg, 2 * sms);
+  int per_sm = 3, grid = 0;
   size_t smem = 0;
-  for (int attempt = 0; attempt < 2; attempt++) {
+  for (;;) {
+    grid = std::min(n_rg, per_sm * sms);
     smem = x_bytes + (size_t)((n_rg + grid - 1) / grid) * RPW * n_kc * M * sizeof(float);
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
@@ -448,8 +502,10 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
     int occ = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
     if (e != cudaSuccess) return e;
-    if (occ >= 2 || grid <= sms) break;
-    grid = std::min(n_rg, sms);  // one CTA per SM: re-size the partial buffer for it
+    if (occ >= per_sm || per_sm == 1 || grid < n_rg) {
+      if (occ >= per_sm || per_sm == 1) break;
+    }
+    per_sm = std::max(1, std::min(per_sm - 1, occ));
   }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kThreads), smem, st, attr);
@@ -458,13 +514,15 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
 
 template <int WT, int M>
 cudaError_t dispatch_epi(const GemvArgs& a, Epi epi, cudaStream_t st) {
-  // items in flight per register buffer: 4 for batch-1 Q8_0 / F32, else 2
-  constexpr int B = (M == 1 && WT != SX_DTYPE_Q4_K) ? 4 : 2;
+  // RPW = 4 rows share each x fragment; items per register buffer: 2 for batch-1 Q8_0 /
+  // F32 (2 x 2 x 4 x 512 B = 8 KB of weights in flight per warp), else 1
+  constexpr int RPW = 4;
+  constexpr int B = 1;
   switch (epi) {
-    case EPI_STORE: return launch_t<WT, M, 2, B, EPI_STORE>(a, st);
-    case EPI_ADD: return launch_t<WT, M, 2, B, EPI_ADD>(a, st);
-    case EPI_SWIGLU: return launch_t<WT, M, 2, B, EPI_SWIGLU>(a, st);
-    case EPI_ARGMAX: return launch_t<WT, M, 2, B, EPI_ARGMAX>(a, st);
+    case EPI_STORE: return launch_t<WT, M, RPW, B, EPI_STORE>(a, st);
+    case EPI_ADD: return launch_t<WT, M, RPW, B, EPI_ADD>(a, st);
+    case EPI_SWIGLU: return launch_t<WT, M, RPW, B, EPI_SWIGLU>(a, st);
+    case EPI_ARGMAX: return launch_t<WT, M, RPW, B, EPI_ARGMAX>(a, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -481,15 +539,20 @@ cudaError_t dispatch_m(const GemvArgs& a, Epi epi, cudaStream_t st) {
 
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
   if (a.M < 1 || a.M > kMaxTok || a.n_range + a.n_extra < 1) return cudaErrorInvalidValue;
+  static const bool tma = [] {
+    const char* v = getenv("SYRINX_GEMV_TMA");
+    return v && v[0] == '1';
+  }();
+  if (tma && gemv_tma_eligible(a)) return launch_gemv_tma(a, epi, st);
   // x and the row partial sums of all M tokens live in shared memory, sized by the
   // kernel's template M (1, 2, 4 or 8): split the tokens into launches that fit
   const size_t K = (size_t)a.w.cols;
   const int ue = a.w.dtype == SX_DTYPE_Q8_0 ? 16 : (a.w.dtype == SX_DTYPE_Q4_K ? 32 : 4);
   const size_t n_kc = (K / ue + 31) / 32;
-  const size_t n_rg = (size_t)(a.n_range + a.n_extra + 1) / 2;
+  const size_t n_rg = (size_t)(a.n_range + a.n_extra + 3) / 4;  // row groups of 4
   static const int sms = num_sms();
   const size_t per_tok = K * 4 + (a.w.dtype == SX_DTYPE_Q4_K ? (K / 16) * 4 : 0) +
-                         ((n_rg + sms - 1) / sms) * 2 * n_kc * 4;
+                         ((n_rg + sms - 1) / sms) * 4 * n_kc * 4;
   int max_m = kMaxTok;
   while (max_m > 1 && (size_t)max_m * per_tok > 200 * 1024) max_m >>= 1;
   for (int m0 = 0; m0 < a.M; m0 += max_m) {

@@ -31,7 +31,7 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAtt
 __device__ __forceinline__ float deq_elem(const DevMat& w, int64_t r, int64_t e) {
   const int64_t K = w.cols;
   if (w.dtype == SX_DTYPE_Q8_0) {
-    const float d = __half2float(w.s[r * (K / 32) + e / 32]);
+    const float d = __half2float(w.s[r * w.s_stride + e / 32]);
     return __fmul_rn((float)((const int8_t*)w.q)[r * K + e], d);
   } else if (w.dtype == SX_DTYPE_Q4_K) {
     const uint8_t* meta = w.meta + (r * (K / 256) + e / 256) * 16;
@@ -211,7 +211,7 @@ __global__ void k_advance(const AdvanceArgs a) {
 }
 
 __global__ void k_repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
-                              int row_mul, int row_add) {
+                              int64_t s_stride, int row_mul, int row_add) {
   const int64_t nb = cols / 32;
   const int64_t total = rows * nb;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -219,7 +219,7 @@ __global__ void k_repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols,
     const int64_t r = i / nb, b = i % nb;
     const uint8_t* src = blocks + i * 34;
     const int64_t dr = r * row_mul + row_add;
-    s[dr * nb + b] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
+    s[dr * s_stride + b] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
     int8_t* dq = q + dr * cols + b * 32;
     for (int j = 0; j < 32; j++) dq[j] = (int8_t)src[2 + j];
   }
@@ -332,9 +332,9 @@ cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st) {
 }
 
 cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
-                        int row_mul, int row_add, cudaStream_t st) {
+                        int64_t s_stride, int row_mul, int row_add, cudaStream_t st) {
   (void)cudaGetLastError();  // report this launch's status, not an earlier one
-  k_repack_q8_0<<<1184, 256, 0, st>>>(blocks, rows, cols, q, s, row_mul, row_add);
+  k_repack_q8_0<<<1184, 256, 0, st>>>(blocks, rows, cols, q, s, s_stride, row_mul, row_add);
   return cudaGetLastError();
 }
 

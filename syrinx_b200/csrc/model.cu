@@ -21,7 +21,7 @@ namespace sx {
 
 size_t DevMat::bytes() const {
   switch (dtype) {
-    case SX_DTYPE_Q8_0: return (size_t)rows * cols + (size_t)rows * (cols / 32) * 2;
+    case SX_DTYPE_Q8_0: return (size_t)rows * cols + (size_t)rows * s_stride * 2;
     case SX_DTYPE_Q4_K: return (size_t)rows * cols / 2 + (size_t)rows * (cols / 256) * 16;
     case SX_DTYPE_F32: return (size_t)rows * cols * 4;
   }
@@ -131,7 +131,8 @@ struct Loader {
       if (t->dtype == SX_DTYPE_Q8_0) {
         int8_t* q;
         SX_RC(dalloc(m->allocs, &q, (size_t)total_rows * cols));
-        SX_RC(dalloc(m->allocs, &dst->s, (size_t)total_rows * (cols / 32)));
+        dst->s_stride = q8_scale_stride(cols);
+        SX_RC(dalloc(m->allocs, &dst->s, (size_t)total_rows * dst->s_stride));
         dst->q = q;
       } else if (t->dtype == SX_DTYPE_Q4_K) {
         uint8_t* q;
@@ -161,7 +162,7 @@ struct Loader {
     }
     SX_CU(cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
     if (t->dtype == SX_DTYPE_Q8_0)
-      SX_CU(repack_q8_0(staging, rows, cols, (int8_t*)dst->q, dst->s, row_mul, row_add, 0));
+      SX_CU(repack_q8_0(staging, rows, cols, (int8_t*)dst->q, dst->s, dst->s_stride, row_mul, row_add, 0));
     else
       SX_CU(repack_q4_k(staging, rows, cols, (uint8_t*)dst->q, dst->meta, row_mul, row_add, 0));
     SX_CU(cudaStreamSynchronize(0));
@@ -405,8 +406,10 @@ int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
   return std::max(1, std::min(kMaxSplit, (s->max_ctx + 63) / 64));
 }
 
-int gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
-  SX_CU(launch_gemv(a, epi, st));
+// Every GEMV reports bounded-wait timeouts through the session's device error flag.
+int gemv(GemvArgs a, Epi epi, sx_session* s) {
+  a.err = s->err;
+  SX_CU(launch_gemv(a, epi, s->st));
   return SX_OK;
 }
 
@@ -431,7 +434,7 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     g.ldy = qkv_w;
     g.M = M;
     g.n_range = qkv_w;
-    SX_RC(gemv(g, EPI_STORE, s->st));
+    SX_RC(gemv(g, EPI_STORE, s));
 
     AttnArgs a;
     a.qkv = s->xqkv;
@@ -470,7 +473,7 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     o.ldy = td.dim;
     o.M = M;
     o.n_range = td.dim;
-    SX_RC(gemv(o, EPI_ADD, s->st));
+    SX_RC(gemv(o, EPI_ADD, s));
 
     GemvArgs f;
     f.w = L.w13;
@@ -481,7 +484,7 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     f.ldy = td.intermediate_size;
     f.M = M;
     f.n_range = 2 * td.intermediate_size;
-    SX_RC(gemv(f, EPI_SWIGLU, s->st));
+    SX_RC(gemv(f, EPI_SWIGLU, s));
 
     GemvArgs w2;
     w2.w = L.w2;
@@ -490,7 +493,7 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     w2.ldy = td.dim;
     w2.M = M;
     w2.n_range = td.dim;
-    SX_RC(gemv(w2, EPI_ADD, s->st));
+    SX_RC(gemv(w2, EPI_ADD, s));
   }
   return SX_OK;
 }
@@ -508,6 +511,10 @@ int check_err(sx_session* s) {
   if (e) {
     SX_CU(cudaMemsetAsync(s->err, 0, 4, s->st));
     SX_CU(cudaStreamSynchronize(s->st));
+    if (e == 2) {
+      set_error("a kernel's bounded pipeline wait timed out (device error flag)");
+      return SX_E_DEVICE;
+    }
     set_error("token id or codebook code out of range");
     return SX_E_INVALID;
   }
@@ -635,9 +642,9 @@ int run_head(sx_session* s, int n, bool want_logits, bool want_argmax, bool mask
       g.stop_lo = d.stop_token_id;
       g.stop_hi = d.stop_token_id + d.num_stop_tokens;
     }
-    return gemv(g, EPI_ARGMAX, s->st);
+    return gemv(g, EPI_ARGMAX, s);
   }
-  return gemv(g, EPI_STORE, s->st);
+  return gemv(g, EPI_STORE, s);
 }
 
 int make_hidden(sx_session* s, int n) {
@@ -681,7 +688,7 @@ int fast_head(sx_session* s, int n, Epi epi) {
     g.y = s->fast_logits;
     g.ldy = m->d.codebook_size;
   }
-  return gemv(g, epi, s->st);
+  return gemv(g, epi, s);
 }
 
 }  // namespace
@@ -887,7 +894,7 @@ int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* f
         std::memcpy(frames_out + ((size_t)i * n_frames + f) * width, ring.data() + ((size_t)f * s->max_batch + i) * width,
                     width * 4);
   }
-  return SX_OK;
+  return check_err(s);
 }
 
 int profile_gemv(sx_session* s, int kind, int n_launches) {
@@ -933,7 +940,7 @@ int profile_gemv(sx_session* s, int kind, int n_launches) {
       g.ldy = td.dim;
       g.n_range = td.dim;
     }
-    SX_RC(gemv(g, epi, s->st));
+    SX_RC(gemv(g, epi, s));
   }
   return SX_OK;
 }

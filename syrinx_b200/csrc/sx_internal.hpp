@@ -2,7 +2,9 @@
 //
 // HBM layout (all device memory owned by the library):
 //   Q8_0 weight [N][K]  -> q : int8 [N][K] (row-major, one row = K bytes, 16-B aligned)
-//                          s : f16  [N][K/32] (block scales)
+//                          s : f16  [N][s_stride] block scales, s_stride = K/32 rounded up
+//                              to 8 so every row's scales start on a 16-byte boundary (a
+//                              legal bulk-copy source for any row chunk)
 //   Q4_K weight [N][K]  -> q : u8   [N][K/2] (GGML nibble order inside each 256 super-block)
 //                          meta : 16 B [N][K/256] = {f16 d, f16 dmin, u8 scales[12]}
 //   F32  weight [N][K]  -> f : f32 [N][K]
@@ -36,9 +38,11 @@ struct DevMat {
   int64_t rows = 0, cols = 0;
   void* q = nullptr;     // Q8_0 int8 / Q4_K nibbles / F32 values
   __half* s = nullptr;   // Q8_0 scales
+  int64_t s_stride = 0;  // Q8_0 scales per row in memory (K/32 rounded up to 8)
   uint8_t* meta = nullptr;  // Q4_K 16-B super-block headers
   size_t bytes() const;
 };
+inline int64_t q8_scale_stride(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
 
 struct DevLayer {
   float* attn_norm = nullptr;
@@ -75,6 +79,7 @@ struct GemvArgs {
   // argmax epilogue: allowed = [allow_lo, allow_hi] U [stop_lo, stop_hi) (stops when !mask)
   unsigned long long* amax = nullptr;  // [M] packed (orderable f32 << 32 | ~row)
   uint32_t allow_lo = 0, allow_hi = 0, stop_lo = 0, stop_hi = 0;
+  int* err = nullptr;  // device error flag (2 = a bounded pipeline wait timed out)
 };
 
 struct AttnArgs {
@@ -103,7 +108,11 @@ struct AttnArgs {
 };
 
 // ---- launchers (stream-ordered, programmatic dependent launch enabled) ----------------
+// launch_gemv runs the register-streaming kernel; with SYRINX_GEMV_TMA=1 it runs the
+// TMA-fed batch-1 Q8_0 kernel for the shapes that kernel accepts.
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st);
+bool gemv_tma_eligible(const GemvArgs& a);
+cudaError_t launch_gemv_tma(const GemvArgs& a, Epi epi, cudaStream_t st);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st);
 
@@ -166,7 +175,7 @@ cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st);
 // repack / dequant
 // destination row of source row r is r * row_mul + row_add (w1/w3 interleave)
 cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
-                        int row_mul, int row_add, cudaStream_t st);
+                        int64_t s_stride, int row_mul, int row_add, cudaStream_t st);
 cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* q, uint8_t* meta,
                         int row_mul, int row_add, cudaStream_t st);
 cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out,
