@@ -257,6 +257,17 @@ int sx_profile_gemv(sx_session* s, int32_t kind, int32_t n_launches);
  * ggml's dequantize_row_* and gguf-py; host in / host out. */
 int sx_dequantize(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device);
 
+/* No reference counterpart (the reference dequantizes on the CPU while loading weights).
+ * sx_dequantize without any device allocation: blocks and values are staged through static
+ * device scratch sized for SX_DEQUANTIZE_NOALLOC_MAX_BLOCKS blocks (144 KB in, 1 MB out per
+ * device) instead of a cudaMalloc/cudaFree per call; same kernel, bit-identical values.
+ * n_blocks above the maximum returns SX_E_RANGE. The first call on a device resolves the
+ * scratch address (cudaGetSymbolAddress) and should come before any stream capture on that
+ * device. Nothing in the scratch has to start at zero. Calls that overlap on one device
+ * (several host threads) race on the shared scratch: serialize them. */
+#define SX_DEQUANTIZE_NOALLOC_MAX_BLOCKS 1024
+int sx_dequantize_noalloc(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device);
+
 #ifdef __cplusplus
 }
 #endif

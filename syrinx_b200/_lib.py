@@ -49,6 +49,7 @@ SIGNATURES = {
     "sx_decode_greedy_batch": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, _u32p, _i32p]),
     "sx_lm_step_tokens": (C.c_int, [C.c_void_p, _u32p, C.c_int32, _f32p]),
     "sx_dequantize": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, _f32p, C.c_int32]),
+    "sx_dequantize_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, _f32p, C.c_int32]),
 }
 
 _LIB = None

@@ -608,4 +608,8 @@ int sx_dequantize(int32_t dtype, const void* blocks, int64_t n_blocks, float* ou
   })
 }
 
+int sx_dequantize_noalloc(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device) {
+  SX_GUARD({ return dequantize_noalloc(dtype, blocks, n_blocks, out, device); })
+}
+
 }  // extern "C"

@@ -180,6 +180,8 @@ cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8
                         int row_mul, int row_add, cudaStream_t st);
 cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out,
                            cudaStream_t st);
+// sx_dequantize through static device scratch (noalloc.cu): returns an SX_* status
+int dequantize_noalloc(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device);
 
 // host helpers
 void set_error(const std::string& msg);
