@@ -34,6 +34,10 @@ PROMPT_T = 512
 PROMPT_SEMANTIC = 430
 SEED = 2
 METRIC = "semantic frames/s/GPU, 4B-shape Q8_0 dual-AR decode b1/b8; % of HBM roofline"
+# DRAM bytes (read + write) of one launch of the dominant kernel, the batch-1 w1|w3 GEMV,
+# from one `ncu --set full` capture (python -m syrinx_b200.profile --what gemv --kind 2
+# --layers 8 --launches 16): 52.99 MB read + 0.15 MB written against 52.92 MB algorithmic.
+W13_DRAM_BYTES = 53137664
 
 
 def peaks():
@@ -233,7 +237,9 @@ def bench_device(args):
             "note": "semantic-only head (4097 rows) counted, as streamed"},
         "roofline": {"bound": "hbm", "kernel": "k_gemv Q8_0 M=1 w1|w3 (+RMSNorm prologue, SwiGLU epilogue)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4), "traffic": W13_DRAM_BYTES,
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                     "algorithmic_bytes": int(bytes_w13),
                      "per_kind_ms": {k: round(v[1], 5) for k, v in gemv.items()},
                      "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
         "e2e": {"value": round(K_e2e * world / (ms_e2e * 1e-3), 2), "unit": "frames/s",

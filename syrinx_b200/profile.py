@@ -3,7 +3,7 @@ Qwen3-4B-shaped model with fewer layers, so an `ncu --set full` capture stays sm
 (the weights still exceed L2, so DRAM counters are meaningful).
 
   python -m syrinx_b200.profile --what gemv --kind 2 --layers 8 --launches 16
-  python -m syrinx_b200.profile --what frames --layers 8 --frames 4
+  python -m syrinx_b200.profile --what frames --layers 8 --frames 4 --prompt 512
 """
 from __future__ import annotations
 
@@ -22,12 +22,13 @@ def main():
     ap.add_argument("--launches", type=int, default=16)
     ap.add_argument("--frames", type=int, default=4)
     ap.add_argument("--q4k", action="store_true")
+    ap.add_argument("--prompt", type=int, default=8, help="prompt positions prefilled before the run")
     args = ap.parse_args()
     cfg = shrink(QWEN3_4B, args.layers, min(4, args.layers))
     wtype = SX_DTYPE_Q4_K if args.q4k else SX_DTYPE_Q8_0
     model = Model(cfg, synth_blob(cfg, wtype, seed=2))
-    be = B200DualAr(model, max_ctx=64 + args.frames)
-    be.prefill(dual_ar_prompt(cfg, 8, 6, seed=2))
+    be = B200DualAr(model, max_ctx=args.prompt + 64 + args.frames)
+    be.prefill(dual_ar_prompt(cfg, args.prompt, max(1, args.prompt * 3 // 4), seed=2))
     if args.what == "gemv":
         be.profile_gemv(args.kind, args.launches)  # close() below synchronizes the stream
     else:
