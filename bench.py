@@ -116,6 +116,7 @@ def kernels_per_frame(cfg) -> int:
 def bench_device(args):
     import torch
     import syrinx_b200 as sx
+    from syrinx_b200 import dp
     from syrinx_b200.configs import SX_DTYPE_Q8_0, frame_bytes
     from syrinx_b200.workloads import dual_ar_prompt
 
@@ -140,7 +141,7 @@ def bench_device(args):
     stream = torch.cuda.Stream()
     be.set_stream(stream.cuda_stream)
     # each rank decodes its own utterance (independent prompts: seed + rank)
-    prompt = dual_ar_prompt(cfg, PROMPT_T, PROMPT_SEMANTIC, seed=SEED + rank)
+    prompt = dual_ar_prompt(cfg, PROMPT_T, PROMPT_SEMANTIC, seed=dp.rank_seed(SEED, rank))
     be.prefill(prompt)
 
     def barrier():
@@ -162,11 +163,7 @@ def bench_device(args):
     barrier()
     ms = start.elapsed_time(end)
     assert frames.shape[0] == K, frames.shape
-    ms_all = ms
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_all = float(t.item())
+    ms_all = dp.max_over_ranks(ms, dist, device="cuda")
     mean_ctx = ctx_start + (K - 1) / 2.0
     fb_sem = frame_bytes(cfg, SX_DTYPE_Q8_0, ctx=mean_ctx, semantic_head=True, kv_elem=4)
 
@@ -186,7 +183,7 @@ def bench_device(args):
         torch.cuda.synchronize()
         per = s2.elapsed_time(e2) / n_prof
         gemv[kind] = (nw * 34 / 32, per)
-    # the largest per-layer matrix (w1|w3, 105 MB) is the dominant kernel of the step
+    # the largest per-layer matrix (w1|w3, 52.9 MB) is the dominant kernel of the step
     bytes_w13, ms_w13 = gemv[2]
     achieved = bytes_w13 / (ms_w13 * 1e-3) / 1e9
 
@@ -207,11 +204,7 @@ def bench_device(args):
         pin_in[:] = pin_out
     e3.record(stream)
     torch.cuda.synchronize()
-    ms_e2e = s3.elapsed_time(e3)
-    if dist:
-        t = torch.tensor([ms_e2e], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
+    ms_e2e = dp.max_over_ranks(s3.elapsed_time(e3), dist, device="cuda")
 
     frames_total = K * world
     value = frames_total / (ms_all * 1e-3)
@@ -231,7 +224,7 @@ def bench_device(args):
         "config": {"workload": "config3 qwen3-4b-shaped dual-AR Q8_0 b1: prompt 512 (430 semantic), "
                                "greedy frames, stop masked", "global_batch": world, "seq_len": PROMPT_T,
                    "ctx_mean": mean_ctx, "parallelism": f"dp{world} (independent utterances, no collective)",
-                   "l2": "inputs larger than L2 (4.8 GB of weights streamed per frame)"},
+                   "l2": "inputs larger than L2 (4.8 GB of weights; 8.4 GB streamed per frame)"},
         "hbm_roofline": {"bytes_per_frame": fb_sem["total"], "frac_of_peak": round(
             fb_sem["total"] * value / world / (peak * 1e9), 4), "peak_gbs": peak, "peak_kind": peak_kind,
             "note": "semantic-only head (4097 rows) counted, as streamed"},
