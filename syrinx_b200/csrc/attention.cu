@@ -8,19 +8,25 @@
 //   -> scores * 1/sqrt(hd) -> softmax -> P.V, per kv head for its whole query group, so
 //   the repeat_kv copy (nn.rs:194-202) never exists.
 //
-// One CTA per (token, kv head, split of the key axis). Each warp walks chunks of KC keys:
-// it issues the K and V row loads of the whole chunk at once (lanes split the head
-// dimension, so every row load is coalesced), reduces the KC x G dot products across lanes
-// in independent shuffle chains, and folds the chunk into an online softmax held in
-// registers. The warps are merged through shared memory, and the last CTA of a
-// (token, kv head) to finish merges the split partials (flash-decoding).
+// One CTA of 8 warps per (token, kv head, split of the key axis); the splits of one
+// (token, kv head) form a thread-block cluster. Each warp walks chunks of KC keys inside one
+// KV page: one page-table lookup, then the K and V row loads of the whole chunk at once
+// (lanes split the head dimension, so every row load is coalesced); the first chunk's loads
+// go out before the query work. The KC x G dot products are reduced across lanes in
+// independent shuffle chains and folded into an online softmax held in registers. The warps
+// are merged through shared memory; the splits are merged by cluster rank 0 reading the
+// other CTAs' partials through distributed shared memory after a cluster barrier
+// (flash-decoding without a global round trip, atomics or a second pass).
 // In decode (append = 1) the CTA whose slice contains the new position computes that
-// token's normed, rotated K and V and writes them into the cache before its warps read the
-// slice, so no CTA reads a slot written by another CTA of the same launch.
+// token's normed, rotated K and V, writes them into the cache for later steps and keeps
+// them in shared memory for its own warps, so no CTA reads a slot written in this launch.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "sx_device.cuh"
 #include "sx_internal.hpp"
+
+namespace cg = cooperative_groups;
 
 namespace sx {
 namespace {
@@ -66,6 +72,11 @@ __device__ __forceinline__ size_t kv_off(const AttnArgs& a, int seq, int t, int 
 // KV element type: f32 (exact, the reference CPU path's cache) or bf16 (half the bytes).
 __device__ __forceinline__ void kv_store(float* p, float v) { *p = v; }
 __device__ __forceinline__ void kv_store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+// The value a read of the cache element returns after kv_store(p, v).
+__device__ __forceinline__ float kv_round(float v, const float*) { return v; }
+__device__ __forceinline__ float kv_round(float v, const __nv_bfloat16*) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
 
 // EPL consecutive elements of a K/V row starting at p, as f32 (one vector load, L2 only).
 template <int EPL>
@@ -99,9 +110,12 @@ __device__ __forceinline__ void kv_load_row(const __nv_bfloat16* p, float (&v)[E
 }
 
 // Compute token m's K (normed, rotated) and V for kv head g and store them at position
-// pos of its sequence. One warp; buf is HD floats of shared memory.
+// pos of its sequence. One warp; buf is HD floats of shared memory. When vbuf is non-null
+// the stored values (rounded to KT, as a later read of the cache returns them) are also
+// left in buf / vbuf for the CTA's own readers.
 template <int HD, typename KT>
-__device__ void append_kv(const AttnArgs& a, int m, int seq, int pos, int g, float* buf, int lane) {
+__device__ void append_kv(const AttnArgs& a, int m, int seq, int pos, int g, float* buf, int lane,
+                          float* vbuf = nullptr) {
   const float* kr = a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * HD + (size_t)(a.H + g) * HD;
   const float* vr = kr + (size_t)a.Hkv * HD;
   for (int e = lane; e < HD; e += 32) buf[e] = ld_cg(kr + e);
@@ -109,8 +123,15 @@ __device__ void append_kv(const AttnArgs& a, int m, int seq, int pos, int g, flo
   norm_rope_head<HD>(buf, a.kn, a.eps, a.inv_freq, a.interleaved, pos, lane);
   const size_t off = kv_off(a, seq, pos, g, HD);
   for (int e = lane; e < HD; e += 32) {
-    kv_store(static_cast<KT*>(a.kbase) + off + e, buf[e]);
-    kv_store(static_cast<KT*>(a.vbase) + off + e, ld_cg(vr + e));
+    KT* kd = static_cast<KT*>(a.kbase) + off + e;
+    KT* vd = static_cast<KT*>(a.vbase) + off + e;
+    const float v = ld_cg(vr + e);
+    kv_store(kd, buf[e]);
+    kv_store(vd, v);
+    if (vbuf) {
+      buf[e] = kv_round(buf[e], kd);
+      vbuf[e] = kv_round(v, vd);
+    }
   }
 }
 
@@ -123,22 +144,49 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   __shared__ __align__(16) float qs[GM][HD];
   __shared__ __align__(16) float wacc[kWarpsA][GM][HD];
   __shared__ float wm[kWarpsA][GM], wl[kWarpsA][GM];
-  __shared__ float kbuf[HD];
-  __shared__ float wq[kMaxSplit][GM], lq[kMaxSplit][GM], inv_l[GM];
-  __shared__ int is_last;
+  __shared__ float kbuf[HD], vbuf[HD];
+  __shared__ __align__(16) float co[GM][HD];  // this split's partial, read by cluster rank 0
+  __shared__ float cm[GM], cl[GM];
 
   pdl_launch_dependents();
   pdl_wait();
 
   const int m = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+  const int n_split = gridDim.z;  // the splits of (m, g) are one cluster along z
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.H / a.Hkv;
   const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
   const int pos = a.tok_pos ? ld_cg(a.tok_pos + m) : a.const_pos;
   const int n_keys = pos + 1;
-  const int chunk = (n_keys + a.n_split - 1) / a.n_split;
+  // split lengths are whole chunks, so a chunk never straddles a KV page (kPage % KC == 0)
+  const int chunk = ((n_keys + n_split - 1) / n_split + KC - 1) / KC * KC;
   const int t0 = min(n_keys, s * chunk);
   const int t1 = min(n_keys, t0 + chunk);
+  const int n_chunks = (t1 - t0 + KC - 1) / KC;
+  // in decode the new key is read back from shared memory (the append below), not the cache
+  const bool own_new = a.append && pos >= t0 && pos < t1;
+
+  const KT* kb = static_cast<const KT*>(a.kbase);
+  const KT* vb = static_cast<const KT*>(a.vbase);
+  float kv[KC][EPL], vv[KC][EPL];
+  // K/V rows of chunk c: one page-table lookup, KC coalesced row loads each for K and V
+  auto load_chunk = [&](int c) {
+    const int base = t0 + c * KC;
+    const int page = ld_cg(a.page_table + (size_t)seq * a.pt_stride + base / kPage);
+    const size_t row0 = ((size_t)(page * a.Hkv + g) * kPage + (base % kPage)) * HD + lane * EPL;
+#pragma unroll
+    for (int j = 0; j < KC; j++) {
+      if (base + j < t1 && !(own_new && base + j == pos)) {
+        kv_load_row<EPL>(kb + row0 + (size_t)j * HD, kv[j]);
+        kv_load_row<EPL>(vb + row0 + (size_t)j * HD, vv[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; e++) kv[j][e] = vv[j][e] = 0.f;
+      }
+    }
+  };
+  // the first chunk's loads go out before the query work, so their latency overlaps it
+  if (warp < n_chunks) load_chunk(warp);
 
   // q heads of this group: norm + rope into shared memory
   const float* qrow = a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * HD;
@@ -148,8 +196,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
     __syncwarp();
     norm_rope_head<HD>(qs[i], a.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
   }
-  if (a.append && pos >= t0 && pos < t1 && warp == kWarpsA - 1)
-    append_kv<HD, KT>(a, m, seq, pos, g, kbuf, lane);
+  if (own_new && warp == kWarpsA - 1) append_kv<HD, KT>(a, m, seq, pos, g, kbuf, lane, vbuf);
   __syncthreads();
 
   float qv[GM][EPL];
@@ -166,22 +213,18 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
     for (int e = 0; e < EPL; e++) acc[i][e] = 0.f;
   }
 
-  const KT* kb = static_cast<const KT*>(a.kbase);
-  const KT* vb = static_cast<const KT*>(a.vbase);
-  const int n_chunks = (t1 - t0 + KC - 1) / KC;
   for (int c = warp; c < n_chunks; c += kWarpsA) {
     const int base = t0 + c * KC;
-    float kv[KC][EPL], vv[KC][EPL];
+    if (c != warp) load_chunk(c);
+    if (own_new) {
 #pragma unroll
-    for (int j = 0; j < KC; j++) {
-      if (base + j < t1) {
-        const size_t off = kv_off(a, seq, base + j, g, HD) + lane * EPL;
-        kv_load_row<EPL>(kb + off, kv[j]);
-        kv_load_row<EPL>(vb + off, vv[j]);
-      } else {
+      for (int j = 0; j < KC; j++)
+        if (base + j == pos)
 #pragma unroll
-        for (int e = 0; e < EPL; e++) kv[j][e] = vv[j][e] = 0.f;
-      }
+          for (int e = 0; e < EPL; e++) {
+            kv[j][e] = kbuf[lane * EPL + e];
+            vv[j][e] = vbuf[lane * EPL + e];
+          }
     }
     float sc[KC][GM];
 #pragma unroll
@@ -259,65 +302,42 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   }
 
   float* out = a.out + (size_t)m * a.H * HD + (size_t)g * G * HD;
-  if (a.n_split == 1) {
+  if (n_split == 1) {
 #pragma unroll
     for (int i = 0; i < GM; i++)
       if (i < G && (i % HSTEP) == i_t0) out[(size_t)i * HD + e_t] = __fdiv_rn(cta_o[i], cta_l[i]);
     return;
   }
 
-  // split partial: per head [m, l, acc[HD]]
-  const size_t stride_h = HD + 2;
-  float* part = a.part + (((size_t)m * a.Hkv + g) * a.n_split + s) * G * stride_h;
+  // this split's partial per head (m, l, acc[HD]) stays in shared memory; cluster rank 0
+  // merges the splits in rank order through distributed shared memory
 #pragma unroll
   for (int i = 0; i < GM; i++)
     if (i < G && (i % HSTEP) == i_t0) {
       if (e_t == 0) {
-        part[i * stride_h + 0] = cta_m[i];
-        part[i * stride_h + 1] = cta_l[i];
+        cm[i] = cta_m[i];
+        cl[i] = cta_l[i];
       }
-      part[i * stride_h + 2 + e_t] = cta_o[i];
+      co[i][e_t] = cta_o[i];
     }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd(&a.counters[(size_t)m * a.Hkv + g], 1);
-    is_last = (old == a.n_split - 1);
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  // merge the splits: stage every split's (m, l), turn them into weights per head, then
-  // each thread sums its element over the splits with independent loads
-  const float* pbase = a.part + ((size_t)m * a.Hkv + g) * a.n_split * G * stride_h;
-  for (int t = threadIdx.x; t < a.n_split * G; t += kAttnThreads) {
-    const int q = t / G, i = t % G;
-    wq[q][i] = __ldcg(pbase + ((size_t)q * G + i) * stride_h);
-    lq[q][i] = __ldcg(pbase + ((size_t)q * G + i) * stride_h + 1);
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    const int i = threadIdx.x;
-    float M = -INFINITY;
-    for (int q = 0; q < a.n_split; q++) M = fmaxf(M, wq[q][i]);
-    float L = 0.f;
-    for (int q = 0; q < a.n_split; q++) {
-      const float w = expf(wq[q][i] - M);
-      wq[q][i] = w;
-      L = fmaf(lq[q][i], w, L);
-    }
-    inv_l[i] = L;
-  }
-  __syncthreads();
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();  // every split's partial is visible to the cluster
+  if (cluster.block_rank() == 0) {
 #pragma unroll
-  for (int i = 0; i < GM; i++)
-    if (i < G && (i % HSTEP) == i_t0) {
-      float O = 0.f;
-#pragma unroll 8
-      for (int q = 0; q < a.n_split; q++) O = fmaf(__ldcg(pbase + ((size_t)q * G + i) * stride_h + 2 + e_t), wq[q][i], O);
-      out[(size_t)i * HD + e_t] = __fdiv_rn(O, inv_l[i]);
-    }
-  if (threadIdx.x == 0) a.counters[(size_t)m * a.Hkv + g] = 0;
+    for (int i = 0; i < GM; i++)
+      if (i < G && (i % HSTEP) == i_t0) {
+        float M = -INFINITY;
+        for (int r = 0; r < n_split; r++) M = fmaxf(M, *cluster.map_shared_rank(&cm[i], r));
+        float L = 0.f, O = 0.f;
+        for (int r = 0; r < n_split; r++) {
+          const float w = expf(*cluster.map_shared_rank(&cm[i], r) - M);
+          L = fmaf(*cluster.map_shared_rank(&cl[i], r), w, L);
+          O = fmaf(*cluster.map_shared_rank(&co[i][e_t], r), w, O);
+        }
+        out[(size_t)i * HD + e_t] = __fdiv_rn(O, L);
+      }
+  }
+  cluster.sync();  // no CTA leaves while rank 0 still reads its shared memory
 }
 
 // Prefill: append the K/V of all M tokens first (tokens of one sequence attend to each
@@ -345,10 +365,17 @@ cudaError_t launch_attention_hd(const AttnArgs& a, cudaLaunchConfig_t& cfg) {
 }  // namespace
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
-  if (a.H % a.Hkv || a.H / a.Hkv > kMaxGroup || a.n_split < 1 || a.n_split > kMaxSplit)
+  if (a.H % a.Hkv || a.H / a.Hkv > kMaxGroup || a.n_split < 1 || a.n_split > kMaxCluster)
     return cudaErrorInvalidValue;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_cfg(dim3(a.M, a.Hkv, a.n_split), dim3(kAttnThreads), 0, st, attr);
+  if (a.n_split > 1) {  // the splits of one (token, kv head) form a cluster
+    cudaLaunchAttribute& c = attr[cfg.numAttrs++];
+    c.id = cudaLaunchAttributeClusterDimension;
+    c.val.clusterDim.x = 1;
+    c.val.clusterDim.y = 1;
+    c.val.clusterDim.z = (unsigned)a.n_split;
+  }
   switch (a.hd) {
     case 32: return a.kv_f32 ? launch_attention_hd<32, float>(a, cfg) : launch_attention_hd<32, __nv_bfloat16>(a, cfg);
     case 64: return a.kv_f32 ? launch_attention_hd<64, float>(a, cfg) : launch_attention_hd<64, __nv_bfloat16>(a, cfg);

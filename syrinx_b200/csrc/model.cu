@@ -348,10 +348,6 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
   const int max_F = std::max(sl.intermediate_size, has_fast ? d.fast.intermediate_size : 0);
   const int dim = sl.dim;
   s->ring_frames = max_ctx;
-  const size_t part_slow = (size_t)kMaxTok * sl.n_local_heads * kMaxSplit * (sl.n_head / sl.n_local_heads) * (sl.head_dim + 2);
-  const size_t part_fast =
-      has_fast ? (size_t)kMaxTok * d.fast.n_local_heads * kMaxSplit * (d.fast.n_head / d.fast.n_local_heads) * (d.fast.head_dim + 2) : 0;
-  const int max_hkv = std::max(sl.n_local_heads, has_fast ? d.fast.n_local_heads : 0);
   if ((rc = dalloc(s->allocs, &s->tok_seq, kMaxTok)) || (rc = dalloc(s->allocs, &s->tok_pos, kMaxTok)) ||
       (rc = dalloc(s->allocs, &s->ptok_seq, kMaxTok)) || (rc = dalloc(s->allocs, &s->ptok_pos, kMaxTok)) ||
       (rc = dalloc(s->allocs, &s->seq_len, max_batch)) || (rc = dalloc(s->allocs, &s->done, max_batch)) ||
@@ -368,12 +364,9 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
       (rc = dalloc(s->allocs, &s->logits, (size_t)max_batch * d.vocab_size)) ||
       (rc = dalloc(s->allocs, &s->fast_logits, (size_t)max_batch * std::max(1, d.codebook_size))) ||
       (rc = dalloc(s->allocs, &s->hidden, (size_t)max_batch * dim)) ||
-      (rc = dalloc(s->allocs, &s->amax, (size_t)max_batch)) ||
-      (rc = dalloc(s->allocs, &s->part, std::max(part_slow, part_fast))) ||
-      (rc = dalloc(s->allocs, &s->counters, (size_t)kMaxTok * max_hkv)))
+      (rc = dalloc(s->allocs, &s->amax, (size_t)max_batch)))
     return fail(rc);
-  if (cudaMemset(s->counters, 0, (size_t)kMaxTok * max_hkv * 4) != cudaSuccess ||
-      cudaMemset(s->amax, 0, (size_t)max_batch * 8) != cudaSuccess ||
+  if (cudaMemset(s->amax, 0, (size_t)max_batch * 8) != cudaSuccess ||
       cudaMemset(s->err, 0, 4) != cudaSuccess || cudaMemset(s->frames, 0, (size_t)max_batch * width * 4) != cudaSuccess)
     return fail(SX_E_CUDA);
   *out = s;
@@ -399,11 +392,11 @@ int session_reset(sx_session* s) {
 
 namespace {
 
-// Splits of the key axis: about 64 keys per CTA at the session's longest context, i.e.
-// two 8-key chunks per warp, so each CTA pays about two memory latencies; long contexts
-// get up to kMaxSplit CTAs per (token, kv head).
+// Splits of the key axis (a cluster per token and kv head): about 64 keys per CTA of 8
+// warps at the session's longest context, i.e. one 8-key chunk per warp whose loads go out
+// before the query work; long contexts get up to kMaxCluster CTAs per (token, kv head).
 int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
-  return std::max(1, std::min(kMaxSplit, (s->max_ctx + 63) / 64));
+  return std::max(1, std::min(kMaxCluster, (s->max_ctx + 63) / 64));
 }
 
 // Every GEMV reports bounded-wait timeouts through the session's device error flag.
@@ -459,8 +452,6 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     a.hd = td.head_dim;
     a.n_split = fast ? 1 : n_split_for(s, M, td.n_local_heads);
     a.append = append ? 1 : 0;
-    a.part = s->part;
-    a.counters = s->counters;
     a.M = M;
     if (!append) SX_CU(launch_kv_append(a, s->st));
     SX_CU(launch_attention(a, s->st));

@@ -65,8 +65,6 @@ struct sx_session {
   float* fast_logits = nullptr;  // [max_batch][R]
   float* hidden = nullptr;       // [max_batch][dim]
   unsigned long long* amax = nullptr;  // [max_batch]
-  float* part = nullptr;
-  int* counters = nullptr;
   std::vector<int> len;  // host mirror of per-sequence cache lengths
   bool device_len_dirty = false;  // device seq_len advanced by a graph loop
   std::vector<GreedyGraph> graphs;

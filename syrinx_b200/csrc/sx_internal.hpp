@@ -12,8 +12,9 @@
 //   these structure-of-arrays forms at load, losslessly, so every GEMV lane issues 128-bit
 //   coalesced loads. w1/w3 are interleaved row by row (g0,u0,g1,u1,...) so one warp owns a
 //   gate/up pair and applies SiLU(g)*u in its epilogue.
-//   KV cache: bf16 pages of PAGE positions, per layer [2][n_pages][Hkv][PAGE][hd], with a
-//   per-sequence page table [max_batch][pages_per_seq] of int32 page ids.
+//   KV cache: f32 (default) or bf16 pages of PAGE positions, per layer
+//   [2][n_pages][Hkv][PAGE][hd], with a per-sequence page table [max_batch][pages_per_seq]
+//   of int32 page ids.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -29,8 +30,8 @@ namespace sx {
 
 constexpr int kPage = 64;         // KV positions per page
 constexpr int kMaxTok = 8;        // max tokens per GEMV launch (batched decode / prefill chunk)
-constexpr int kAttnThreads = 128;
-constexpr int kMaxSplit = 64;     // max split-K partitions of the attention sequence axis
+constexpr int kAttnThreads = 256;  // 8 warps per attention CTA
+constexpr int kMaxCluster = 8;     // max splits of the attention key axis (one portable cluster)
 constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one CTA
 
 struct DevMat {
@@ -100,10 +101,8 @@ struct AttnArgs {
   int interleaved = 1;
   float scale = 1.f;  // f32(1/sqrt(hd)) computed in double on the host (s2/nn.rs:344)
   int H = 0, Hkv = 0, hd = 0;
-  int n_split = 1;
+  int n_split = 1;  // splits of the key axis = cluster size (<= kMaxCluster)
   int append = 1;  // 1: this launch appends each token's own K/V (decode)
-  float* part = nullptr;  // [M][Hkv][n_split][G][hd + 2]
-  int* counters = nullptr;  // [M][Hkv]
   int M = 1;
 };
 
