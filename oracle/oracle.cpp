@@ -216,10 +216,63 @@ float dot(const float* a, const float* b, int64_t n) {
   return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
 }
 
-// y[M][N] = x[M][K] . W^T (+ b): the quantized matmul in "mode A" (exact dequant x f32).
+// Matmul numerics for quantized weights. Mode A (the default, what the B200 kernels
+// compute) multiplies the exactly dequantized weights by the f32 activations with f32 sums.
+// Mode B (oc_set_qmode(1), for analysis) restates Candle's CPU QMatMul for Q8_0 weights,
+// which follows ggml: every activation row is quantized to Q8_0 blocks (quantize_row_q8_0:
+// d = amax/127, q = round(x/d), d stored as f16) and each block contributes
+// (float)sumi * (d_w * d_x), sumi the exact int32 dot, in block order (vec_dot_q8_0_q8_0;
+// candle-core 0.8.x is not vendored here, so the published ggml form stands in). Mode B is
+// chaotic in its inputs: a 1-ulp change of the normed activations moves config-1 logits by
+// ~5e-2 (mode A: ~3e-6), so it cannot serve as a parity target for any implementation with
+// another reduction order. Q4_K weights always use mode A here.
+int g_qmode = 0;
+
+void q8_0_quantize_act(const float* x, int64_t K, int8_t* q, float* d) {
+  for (int64_t b = 0; b < K / QK8_0; b++) {
+    const float* xb = x + b * QK8_0;
+    float amax = 0.0f;
+    for (int j = 0; j < QK8_0; j++) amax = std::max(amax, std::fabs(xb[j]));
+    const float dd = amax / 127.0f;
+    const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+    d[b] = h2f(f2h(dd));
+    for (int j = 0; j < QK8_0; j++) q[b * QK8_0 + j] = (int8_t)std::round(xb[j] * id);
+  }
+}
+
+void linear_q8_0_b(const OT& W, const float* b, const float* x, int M, float* y) {
+  const int64_t N = W.rows, K = W.cols, nb = K / QK8_0;
+  std::vector<int8_t> xq((size_t)M * K);
+  std::vector<float> xd((size_t)M * nb);
+  for (int m = 0; m < M; m++) q8_0_quantize_act(x + (size_t)m * K, K, xq.data() + (size_t)m * K, xd.data() + (size_t)m * nb);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < N; r++) {
+    const uint8_t* row = W.p + (size_t)r * nb * Q8_0_BYTES;
+    for (int m = 0; m < M; m++) {
+      const int8_t* qx = xq.data() + (size_t)m * K;
+      float sumf = 0.0f;
+      for (int64_t bk = 0; bk < nb; bk++) {
+        const uint8_t* blk = row + bk * Q8_0_BYTES;
+        uint16_t dh;
+        std::memcpy(&dh, blk, 2);
+        const int8_t* qw = (const int8_t*)(blk + 2);
+        int32_t sumi = 0;
+        for (int j = 0; j < QK8_0; j++) sumi += (int32_t)qw[j] * (int32_t)qx[bk * QK8_0 + j];
+        sumf += (float)sumi * (h2f(dh) * xd[(size_t)m * nb + bk]);
+      }
+      y[(size_t)m * N + r] = b ? sumf + b[r] : sumf;
+    }
+  }
+}
+
+// y[M][N] = x[M][K] . W^T (+ b).
 void linear(const OT& W, const OT* bias, const float* x, int M, float* y) {
   const int64_t N = W.rows, K = W.cols;
   const float* b = bias ? (const float*)bias->p : nullptr;
+  if (W.dtype == SX_DTYPE_Q8_0 && g_qmode == 1) {
+    linear_q8_0_b(W, b, x, M, y);
+    return;
+  }
 #pragma omp parallel
   {
     std::vector<float> row(K);
@@ -743,6 +796,19 @@ extern "C" {
 
 const char* oc_last_error(void) { return g_err.c_str(); }
 int oc_num_threads(void) { return omp_get_max_threads(); }
+
+void oc_set_qmode(int32_t mode) { g_qmode = mode ? 1 : 0; }
+int32_t oc_get_qmode(void) { return g_qmode; }
+
+void oc_linear_q8_0(const float* x, const uint8_t* blocks, int32_t M, int32_t N, int32_t K, float* y) {
+  OT w;
+  w.dtype = SX_DTYPE_Q8_0;
+  w.rows = N;
+  w.cols = K;
+  w.p = blocks;
+  w.nbytes = (size_t)N * (K / QK8_0) * Q8_0_BYTES;
+  linear(w, nullptr, x, M, y);
+}
 
 void oc_q8_0_quantize(const float* x, int64_t n, uint8_t* blocks) {
   for (int64_t b = 0; b < n / QK8_0; b++) {

@@ -15,7 +15,10 @@
  *     cv2/attention.rs:46-119) through the same code with rotate-half RoPE and biases;
  *   - the driver loop and the seeded sampler (common/dualar.rs:161-230,
  *     common/sampling.rs:19-268).
- * Quantized matmul "mode A": exact dequantized weights x f32 activations, f32 sums.
+ * Quantized matmul: mode A (default, what the device computes) = exact dequantized weights x
+ * f32 activations; mode B (oc_set_qmode(1), Q8_0 only, for analysis) restates Candle's CPU
+ * QMatMul / ggml vec_dot_q8_0_q8_0 (activations quantized to Q8_0 blocks, exact int32
+ * block dots, f32 scale products).
  */
 #ifndef SYRINX_ORACLE_H
 #define SYRINX_ORACLE_H
@@ -34,6 +37,11 @@ typedef struct oc_session oc_session;
 
 const char* oc_last_error(void);
 int oc_num_threads(void);
+/* Quantized matmul numerics for Q8_0 weights: 0 = mode A (default), 1 = mode B. */
+void oc_set_qmode(int32_t mode);
+int32_t oc_get_qmode(void);
+/* y[M][N] = x[M][K] . W^T for Q8_0 blocks W [N][K/32 blocks], in the current mode. */
+void oc_linear_q8_0(const float* x, const uint8_t* blocks, int32_t M, int32_t N, int32_t K, float* y);
 
 /* ---- block formats ---- */
 void oc_q8_0_quantize(const float* x, int64_t n, uint8_t* blocks);       /* n % 32 == 0 */
