@@ -142,7 +142,7 @@ __device__ __forceinline__ void frag_dot(const Frag<WT>& f, const XFrag<WT, M>& 
     unsigned long long w[8];
     const uint32_t words[4] = {f.q.x, f.q.y, f.q.z, f.q.w};
 #pragma unroll
-    for (int j = 0; j < 4; j++) i8x4_to_f32x2x2(words[j], w[2 * j], w[2 * j + 1]);
+    for (int j = 0; j < 4; j++) u8b4_to_f32x2x2(words[j], w[2 * j], w[2 * j + 1]);
 #pragma unroll
     for (int m = 0; m < M; m++) {
       unsigned long long s0 = 0, s1 = 0;

@@ -7,7 +7,7 @@
 //
 //   * one persistent CTA per SM owns a balanced, contiguous range of weight rows. Rows of
 //     the SoA Q8_0 layout are contiguous in HBM, so a stage of R whole rows is ONE bulk copy
-//     of R*K quant bytes plus one of R*s_stride scales (about 24 KB per stage). The TMA
+//     of R*K quant bytes plus one of R*s_stride scales (about 40 KB per stage). The TMA
 //     engine's cost is per copy (on B200 a CTA streams ~3.7 TB/s device-wide with 2 KB
 //     copies but ~7 TB/s with 20-32 KB copies), so stages are sized by bytes, not rows;
 //   * a producer warp fills a ring of such stages (at most 108 KB of shared memory, so two
@@ -45,7 +45,7 @@ namespace {
 constexpr int kMaxWarps = 16;                      // consumer warps (the plan never needs more)
 constexpr int kRMax = 32;                          // max rows per stage
 constexpr int kMaxSlots = 8;
-constexpr int kStageTarget = 24 * 1024;  // quant bytes per stage
+constexpr int kStageTarget = 40 * 1024;  // quant bytes per stage (two slots fit the budget)
 constexpr size_t kSmemBudget = 108 * 1024;  // two CTAs (+1 KB reserved each) fit in 228 KB
 constexpr uint64_t kWaitNs = 1000000000ull;  // bound on any single mbarrier wait (1 s)
 
@@ -71,10 +71,12 @@ bool make_plan(int64_t K64, int64_t s_stride, bool pairs, TmaPlan* p) {
   const int upt = (U + 31) / 32 <= 16 ? 1 : 2;
   const int C = (U + 32 * upt - 1) / (32 * upt);
   if (C > 16) return false;
-  const int G = std::max(1, (10 + C / 2) / C);
+  int R = std::max(1, std::min(kRMax, kStageTarget / K));
+  // row groups so that each warp computes about 8 rows per stage: the per-stage work
+  // (wait, release, reduce-scatter, partials) is then spread over 8 rows
+  const int G = std::max(1, std::min(kMaxWarps / C, R / 8));
   if (G * C > kMaxWarps) return false;
   const int step = (pairs && G % 2) ? 2 * G : G;
-  int R = std::max(1, std::min(kRMax, kStageTarget / K));
   R = std::min(R, 8 * G);
   R = std::max(step, R / step * step);
   if (R > kRMax || R / G > 8) return false;
@@ -133,10 +135,10 @@ __device__ __forceinline__ int stage_rows(const GemvArgs& a, int i, int r1, int 
 // dot of one 16-column unit: exact int8 -> f32, two f32x2 chains
 __device__ __forceinline__ float dot16(const uint4 wq, const ulonglong2 (&xv)[4]) {
   unsigned long long wv[8];
-  i8x4_to_f32x2x2(wq.x, wv[0], wv[1]);
-  i8x4_to_f32x2x2(wq.y, wv[2], wv[3]);
-  i8x4_to_f32x2x2(wq.z, wv[4], wv[5]);
-  i8x4_to_f32x2x2(wq.w, wv[6], wv[7]);
+  u8b4_to_f32x2x2(wq.x, wv[0], wv[1]);
+  u8b4_to_f32x2x2(wq.y, wv[2], wv[3]);
+  u8b4_to_f32x2x2(wq.z, wv[4], wv[5]);
+  u8b4_to_f32x2x2(wq.w, wv[6], wv[7]);
   unsigned long long s0 = 0ull, s1 = 0ull;
 #pragma unroll
   for (int i = 0; i < 4; i++) {

@@ -32,7 +32,7 @@ __device__ __forceinline__ float deq_elem(const DevMat& w, int64_t r, int64_t e)
   const int64_t K = w.cols;
   if (w.dtype == SX_DTYPE_Q8_0) {
     const float d = __half2float(w.s[r * w.s_stride + e / 32]);
-    return __fmul_rn((float)((const int8_t*)w.q)[r * K + e], d);
+    return __fmul_rn((float)((int)((const uint8_t*)w.q)[r * K + e] - 128), d);
   } else if (w.dtype == SX_DTYPE_Q4_K) {
     const uint8_t* meta = w.meta + (r * (K / 256) + e / 256) * 16;
     const float d = __half2float(*reinterpret_cast<const __half*>(meta));
@@ -220,8 +220,8 @@ __global__ void k_repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols,
     const uint8_t* src = blocks + i * 34;
     const int64_t dr = r * row_mul + row_add;
     s[dr * s_stride + b] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
-    int8_t* dq = q + dr * cols + b * 32;
-    for (int j = 0; j < 32; j++) dq[j] = (int8_t)src[2 + j];
+    uint8_t* dq = reinterpret_cast<uint8_t*>(q) + dr * cols + b * 32;
+    for (int j = 0; j < 32; j++) dq[j] = (uint8_t)(src[2 + j] ^ 0x80u);  // q + 128
   }
 }
 

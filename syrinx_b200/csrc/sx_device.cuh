@@ -53,13 +53,12 @@ __device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigne
   return d;
 }
 
-// int8 x 4 (packed in a word) -> exact f32 values, two per f32x2 register.
-// Each byte b is biased to u = b ^ 0x80 = q + 128, placed in the low mantissa byte of
-// 2^23 (bit pattern 0x4B0000uu = 8388608 + u), and 8388736 = 2^23 + 128 is subtracted:
-// an exact integer conversion on the byte-permute and f32x2 pipes.
-__device__ __forceinline__ void i8x4_to_f32x2x2(uint32_t w, unsigned long long& lo,
+// The repacked Q8_0 layout stores every quant biased, u = q + 128 (one byte). Each u is
+// placed in the low mantissa byte of 2^23 (bit pattern 0x4B0000uu = 8388608 + u) and
+// 8388736 = 2^23 + 128 is subtracted: 4 biased bytes -> exact f32 q values, two per f32x2
+// register, on the byte-permute and f32x2 pipes (no per-word XOR).
+__device__ __forceinline__ void u8b4_to_f32x2x2(uint32_t u, unsigned long long& lo,
                                                 unsigned long long& hi) {
-  const uint32_t u = w ^ 0x80808080u;
   const unsigned long long bias = 0xCB000080CB000080ull;  // {-8388736.f, -8388736.f}
   lo = add2(pack2u(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541)), bias);
   hi = add2(pack2u(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543)), bias);

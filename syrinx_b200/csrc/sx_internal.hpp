@@ -1,7 +1,8 @@
 // sx_internal.hpp — device data layout and kernel launch interfaces of the B200 path.
 //
 // HBM layout (all device memory owned by the library):
-//   Q8_0 weight [N][K]  -> q : int8 [N][K] (row-major, one row = K bytes, 16-B aligned)
+//   Q8_0 weight [N][K]  -> q : u8 [N][K] = int8 quant + 128 (row-major, one row = K bytes,
+//                              16-B aligned; the bias spares the unpack an XOR per word)
 //                          s : f16  [N][s_stride] block scales, s_stride = K/32 rounded up
 //                              to 8 so every row's scales start on a 16-byte boundary (a
 //                              legal bulk-copy source for any row chunk)
