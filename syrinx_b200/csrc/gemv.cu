@@ -1,4 +1,5 @@
-// gemv.cu — fused dequant-GEMV for decode: y = x . W^T over Q8_0 / Q4_K / F32 weights.
+// gemv.cu — fused dequant-GEMV for decode: y = x . W^T over Q4_K / F32 weights (Q8_0
+// weights take the tensor-core kernel of gemv_q8.cu).
 //
 // Replaces the quantized linear of the reference hot path (`Weights::linear`,
 // crates/syrinx-fish/src/s2/nn.rs:61-68; `Qwen2Lm::linear` over candle QMatMul,
@@ -16,7 +17,7 @@
 //     contiguous run of items and streams them with 128-bit ld.global.nc.L1::no_allocate
 //     loads, ping-ponging two register buffers so the next item's weights are in flight
 //     while the current one is multiplied;
-//   * Q8_0 / Q4_K values are unpacked in registers (byte-permute into the 2^23 mantissa,
+//   * Q4_K values are unpacked in registers (byte-permute into the 2^23 mantissa,
 //     exact) and multiplied on the packed f32x2 FMA pipe against x in shared memory;
 //   * a warp-shuffle reduction per run of items, partial sums per (row, k-chunk) in shared
 //     memory, then a fixed-order sum in the epilogue (deterministic for a given grid);
@@ -38,15 +39,10 @@ constexpr int kThreads = kWarps * 32;
 
 // Elements covered by one lane-chunk (16 bytes of packed weights).
 template <int WT> struct Unit;
-template <> struct Unit<SX_DTYPE_Q8_0> { static constexpr int elems = 16; };
 template <> struct Unit<SX_DTYPE_Q4_K> { static constexpr int elems = 32; };
 template <> struct Unit<SX_DTYPE_F32> { static constexpr int elems = 4; };
 
 template <int WT> struct Frag;
-template <> struct Frag<SX_DTYPE_Q8_0> {
-  uint4 q;
-  float d;
-};
 template <> struct Frag<SX_DTYPE_Q4_K> {
   uint4 q;
   uint4 meta;
@@ -62,11 +58,7 @@ __device__ __forceinline__ int phys_row(const GemvArgs& a, int i) {
 template <int WT>
 __device__ __forceinline__ void load_frag(const GemvArgs& a, int prow, int unit, Frag<WT>& f) {
   const int64_t K = a.w.cols;
-  if constexpr (WT == SX_DTYPE_Q8_0) {
-    const int8_t* q = (const int8_t*)a.w.q + (size_t)prow * K + (size_t)unit * 16;
-    f.q = ldg_stream(q);
-    f.d = __half2float(a.w.s[(size_t)prow * a.w.s_stride + (unit >> 1)]);
-  } else if constexpr (WT == SX_DTYPE_Q4_K) {
+  if constexpr (WT == SX_DTYPE_Q4_K) {
     const uint8_t* q = (const uint8_t*)a.w.q + (size_t)prow * (K / 2) + (size_t)unit * 16;
     f.q = ldg_stream(q);
     f.meta = __ldg((const uint4*)(a.w.meta + ((size_t)prow * (K / 256) + (unit >> 3)) * 16));
@@ -93,9 +85,6 @@ __device__ __forceinline__ void q4k_sm(const uint8_t* sc12, int j, float& sc, fl
 // x fragment of one lane-unit for M tokens (read from shared memory once, shared by the
 // RPW rows of a row group).
 template <int WT, int M> struct XFrag;
-template <int M> struct XFrag<SX_DTYPE_Q8_0, M> {
-  ulonglong2 v[M][4];  // 16 f32 as 8 f32x2
-};
 template <int M> struct XFrag<SX_DTYPE_Q4_K, M> {
   ulonglong2 lo[M][4], hi[M][4];  // the low- and high-nibble runs of 16 elements
   float slo[M], shi[M];           // their sums (for the sub-block minimum term)
@@ -114,11 +103,7 @@ template <int WT, int M>
 __device__ __forceinline__ void load_x(const float* xs, int K, int unit, const float* xsum16, XFrag<WT, M>& x) {
 #pragma unroll
   for (int m = 0; m < M; m++) {
-    if constexpr (WT == SX_DTYPE_Q8_0) {
-      const ulonglong2* p = (const ulonglong2*)(xs + (size_t)m * K + unit * 16);
-#pragma unroll
-      for (int j = 0; j < 4; j++) x.v[m][j] = p[j];
-    } else if constexpr (WT == SX_DTYPE_Q4_K) {
+    if constexpr (WT == SX_DTYPE_Q4_K) {
       const int e = q4k_elem_lo(unit);
       const ulonglong2* pl = (const ulonglong2*)(xs + (size_t)m * K + e);
       const ulonglong2* ph = (const ulonglong2*)(xs + (size_t)m * K + e + 32);
@@ -138,26 +123,7 @@ __device__ __forceinline__ void load_x(const float* xs, int K, int unit, const f
 // Dot of one weight fragment with the x fragment of M tokens, accumulated into acc.
 template <int WT, int M>
 __device__ __forceinline__ void frag_dot(const Frag<WT>& f, const XFrag<WT, M>& x, int unit, float (&acc)[M]) {
-  if constexpr (WT == SX_DTYPE_Q8_0) {
-    unsigned long long w[8];
-    const uint32_t words[4] = {f.q.x, f.q.y, f.q.z, f.q.w};
-#pragma unroll
-    for (int j = 0; j < 4; j++) u8b4_to_f32x2x2(words[j], w[2 * j], w[2 * j + 1]);
-#pragma unroll
-    for (int m = 0; m < M; m++) {
-      unsigned long long s0 = 0, s1 = 0;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        s0 = fma2(w[2 * j], x.v[m][j].x, s0);
-        s1 = fma2(w[2 * j + 1], x.v[m][j].y, s1);
-      }
-      float a0, a1, b0, b1;
-      unpack2(add2(s0, s1), a0, a1);
-      (void)b0;
-      (void)b1;
-      acc[m] = fmaf(f.d, a0 + a1, acc[m]);
-    }
-  } else if constexpr (WT == SX_DTYPE_Q4_K) {
+  if constexpr (WT == SX_DTYPE_Q4_K) {
     const int jj = (unit & 7) >> 1;
     const __half2 dd = *reinterpret_cast<const __half2*>(&f.meta.x);
     const float d = __low2float(dd), dmin = __high2float(dd);
@@ -286,11 +252,8 @@ __device__ __forceinline__ void compute_group(const Geo& g, Cursor& c, int lane,
     }
   }
 }
-// Batch-1 Q8_0 (the decode step) is held to 80 registers so three CTAs (24 warps) are
-// resident per SM: more loads in flight and more warps to hide the unpack latency
-// (measured 194 -> 201 frames/s on the 4B-shape decode against two CTAs per SM).
 template <int WT, int M, int RPW, int B, int EPI>
-__global__ void __launch_bounds__(kThreads, (WT == SX_DTYPE_Q8_0 && M == 1) ? 3 : 1) k_gemv(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
   constexpr int UE = Unit<WT>::elems;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -517,8 +480,7 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
 
 template <int WT, int M>
 cudaError_t dispatch_epi(const GemvArgs& a, Epi epi, cudaStream_t st) {
-  // RPW = 4 rows share each x fragment; items per register buffer: 2 for batch-1 Q8_0 /
-  // F32 (2 x 2 x 4 x 512 B = 8 KB of weights in flight per warp), else 1
+  // RPW = 4 rows share each x fragment; one item per register buffer
   constexpr int RPW = 4;
   constexpr int B = 1;
   switch (epi) {
@@ -542,15 +504,11 @@ cudaError_t dispatch_m(const GemvArgs& a, Epi epi, cudaStream_t st) {
 
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
   if (a.M < 1 || a.M > kMaxTok || a.n_range + a.n_extra < 1) return cudaErrorInvalidValue;
-  static const bool tma = [] {
-    const char* v = getenv("SYRINX_GEMV_TMA");
-    return v && v[0] == '1';
-  }();
-  if (tma && gemv_tma_eligible(a)) return launch_gemv_tma(a, epi, st);
+  if (a.w.dtype == SX_DTYPE_Q8_0) return launch_gemv_q8(a, epi, st);
   // x and the row partial sums of all M tokens live in shared memory, sized by the
   // kernel's template M (1, 2, 4 or 8): split the tokens into launches that fit
   const size_t K = (size_t)a.w.cols;
-  const int ue = a.w.dtype == SX_DTYPE_Q8_0 ? 16 : (a.w.dtype == SX_DTYPE_Q4_K ? 32 : 4);
+  const int ue = a.w.dtype == SX_DTYPE_Q4_K ? 32 : 4;
   const size_t n_kc = (K / ue + 31) / 32;
   const size_t n_rg = (size_t)(a.n_range + a.n_extra + 3) / 4;  // row groups of 4
   static const int sms = num_sms();
@@ -566,7 +524,6 @@ cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
     if (a.amax) b.amax = a.amax + m0;
     cudaError_t e = cudaErrorInvalidValue;
     switch (a.w.dtype) {
-      case SX_DTYPE_Q8_0: e = dispatch_m<SX_DTYPE_Q8_0>(b, epi, st); break;
       case SX_DTYPE_Q4_K: e = dispatch_m<SX_DTYPE_Q4_K>(b, epi, st); break;
       case SX_DTYPE_F32: e = dispatch_m<SX_DTYPE_F32>(b, epi, st); break;
     }

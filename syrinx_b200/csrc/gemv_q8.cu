@@ -1,0 +1,378 @@
+// gemv_q8.cu — Q8_0 GEMV for decode (M = 1..8 tokens) on int8 tensor-core fragments.
+//
+// Replaces the quantized linear of the reference hot path (`Weights::linear`,
+// crates/syrinx-fish/src/s2/nn.rs:61-68; `Qwen2Lm::linear` over candle QMatMul,
+// crates/syrinx-lm/src/cv2/mod.rs:195-211) for Q8_0 weights, with the neighbouring
+// element-wise ops fused in:
+//   prologue  RMSNorm of x with a gain vector (rms_norm_w, s2/nn.rs:100-106)
+//   epilogue  + bias, residual add (s2/slow_ar.rs:195,198), SiLU(g)*u (s2/nn.rs:452-457),
+//             or the greedy argmax of the head (common/sampling.rs:189-245 with top_k = 1).
+//
+// Arithmetic. The product is the exact dequantized weight times f32 x. Per 32-wide block b
+// and token m, x is written as sx * (l0 + l1/128 + l2/128^2 + l3/128^3), sx a power of two
+// that puts the block's max |x| in [32, 64) and every limb l_i an integer in [-64, 64] (the
+// split is exact to 2^-27 of the block max; x itself carries 24 bits). One
+// mma.m16n8k32.s8 then yields, for a 16-row weight tile, the exact int32 sums
+// S_i = sum_k q_k l_i,k of all four limbs of two tokens at once (B columns 0-3 token 2p,
+// 4-7 token 2p+1). Each lane folds its two limb sums as S_0*128 + S_1 (or S_2*128 + S_3),
+// converts once and accumulates d_row * sx * S in f32; the two halves are combined with
+// weights 2^-7 and 2^-21. That is about 15 instructions per 512 weight bytes, so the
+// stream is bound by HBM, not by issue.
+//
+// Work split. Items are (virtual tile, k-chunk of 8 blocks), ordered k-chunk-major over the
+// whole grid, contiguous per CTA and per warp: a CTA touches one or two k-chunks, so it
+// splits x into limbs only for those 8-16 blocks. Every item writes its 16 row sums per
+// token to a partial buffer [vt][k-chunk][m][16]; a second small kernel (k_merge_q8) adds
+// the k-chunks of each row in a fixed order and applies the epilogue. The result does not
+// depend on the grid, on M, or on which warp ran which item.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "sx_device.cuh"
+#include "sx_internal.hpp"
+
+namespace sx {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kCB = 8;  // 32-wide k blocks per item
+
+struct Q8Geo {
+  int K, nb, nc;      // columns, 32-wide blocks, k-chunks of kCB blocks
+  int t_first, n_rt;  // first physical tile of the row range, tiles covering the range
+  int n_vt;           // virtual tiles: the range tiles, then one per extra row
+};
+
+__device__ __forceinline__ int vt_tile(const GemvArgs& a, const Q8Geo& g, int vt) {
+  return vt < g.n_rt ? g.t_first + vt : (a.extra[vt - g.n_rt] >> 4);
+}
+
+struct Item {
+  uint4 q[kCB];
+  uint32_t s[kCB];
+};
+
+__device__ __forceinline__ void load_item(const uint8_t* W, const Q8Geo& g, int tile, int kc, int lane, Item& it) {
+#pragma unroll
+  for (int j = 0; j < kCB; j++) {
+    const int b = kc * kCB + j;
+    if (b < g.nb) {
+      const uint8_t* r = W + ((size_t)tile * g.nb + b) * kQ8Rec;
+      it.q[j] = ldg_stream(r + lane * 16);
+      it.s[j] = ldg_stream32(r + 512 + (lane >> 2) * 4);
+    }
+  }
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, 3) k_gemv_q8(const GemvArgs a, const Q8Geo g) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int NP = (M + 1) / 2;  // token pairs = tensor-core instructions per record
+  __shared__ __align__(16) int8_t scr[kWarps][4][32];
+  __shared__ float red[kWarps][M];
+  __shared__ float den[M];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const long long I = (long long)g.n_vt * g.nc;
+  const long long c0 = (long long)blockIdx.x * I / gridDim.x;
+  const long long c1 = (long long)(blockIdx.x + 1) * I / gridDim.x;
+  const int kc_lo = (int)(c0 / g.n_vt), kc_hi = c1 > c0 ? (int)((c1 - 1) / g.n_vt) : kc_lo;
+  const int b_lo = kc_lo * kCB, b_hi = min(g.nb, (kc_hi + 1) * kCB);
+  // shared: B fragments [block - b_lo][NP][32 lanes] | block scales of x [block - b_lo][M]
+  uint2* bfr = reinterpret_cast<uint2*>(smem);
+  float* sxs = reinterpret_cast<float*>(smem + (size_t)(b_hi - b_lo) * NP * 256);
+  const long long w0 = c0 + (c1 - c0) * warp / kWarps, w1 = c0 + (c1 - c0) * (warp + 1) / kWarps;
+  int kc = (int)(w0 / g.n_vt), vt = (int)(w0 % g.n_vt), left = (int)(w1 - w0);
+  const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
+
+  pdl_launch_dependents();
+  // The first item's weights do not depend on the previous kernel: request them now.
+  Item it;
+  if (left > 0) load_item(W, g, vt_tile(a, g, vt), kc, lane, it);
+  pdl_wait();
+
+  // ---- RMSNorm denominators over the full K (same order as the register kernel) ----
+  if (a.norm_w) {
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) ss[m] = 0.f;
+    for (int k = threadIdx.x; k < g.K; k += kThreads)
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
+        ss[m] = fmaf(v, v, ss[m]);
+      }
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const float t = warp_sum(ss[m]);
+      if (lane == 0) red[warp][m] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x < M) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
+      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)g.K), a.eps));
+    }
+    __syncthreads();
+  }
+
+  // ---- x limbs of this CTA's blocks: one warp per (block, token) ----
+  for (int u = warp; u < (b_hi - b_lo) * M; u += kWarps) {
+    const int bi = u / M, m = u % M, k = (b_lo + bi) * 32 + lane;
+    float v = 0.f;
+    if (m < a.M) {
+      v = ld_cg(a.x + (size_t)m * g.K + k);
+      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), a.norm_w[k]);
+    }
+    const float mx = warp_max(fabsf(v));
+    const int e = (__float_as_int(mx) >> 23) & 0xff;
+    float sc = 0.f, sx = 0.f;
+    if (e == 255 || __any_sync(0xffffffffu, v != v)) {
+      sx = __int_as_float(0x7fc00000);  // inf / nan in the block: the result is nan
+    } else if (e >= 6) {               // below 2^-121 the block contributes nothing
+      sc = __int_as_float((259 - e) << 23);  // 2^(132 - e): max |x| * sc in [32, 64)
+      sx = __int_as_float((e - 5) << 23);    // 1 / sc
+    }
+    const float s = v * sc;
+    const float l0 = rintf(s);
+    float r = (s - l0) * 128.f;
+    const float l1 = rintf(r);
+    r = (r - l1) * 128.f;
+    const float l2 = rintf(r);
+    r = (r - l2) * 128.f;
+    const float l3 = rintf(r);
+    scr[warp][0][lane] = (int8_t)(int)l0;
+    scr[warp][1][lane] = (int8_t)(int)l1;
+    scr[warp][2][lane] = (int8_t)(int)l2;
+    scr[warp][3][lane] = (int8_t)(int)l3;
+    __syncwarp();
+    if (lane < 16) {  // B fragment: lane 4n + c holds limb n of k 4c..4c+3 and 16+4c..16+4c+3
+      const int n = lane >> 2, c = lane & 3;
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&scr[warp][n][4 * c]);
+      w.y = *reinterpret_cast<const uint32_t*>(&scr[warp][n][16 + 4 * c]);
+      bfr[(bi * NP + (m >> 1)) * 32 + (m & 1) * 16 + lane] = w;
+    }
+    if (lane == 0) sxs[bi * M + m] = sx;
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // ---- stream this warp's items ----
+  // lane roles in the accumulator: rows g = lane/4 and g+8; token 2p + ((lane >> 1) & 1);
+  // limb pair (0,1) on even lanes, (2,3) on odd lanes
+  const int bl = M == 1 ? (lane & 15) : lane;
+  while (left > 0) {
+    float acc[NP][2];
+#pragma unroll
+    for (int p = 0; p < NP; p++) acc[p][0] = acc[p][1] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCB; j++) {
+      const int b = kc * kCB + j;
+      if (b < g.nb) {
+        const int bi = b - b_lo;
+        const float2 ds = __half22float2(*reinterpret_cast<const __half2*>(&it.s[j]));
+#pragma unroll
+        for (int p = 0; p < NP; p++) {
+          const uint2 bf = bfr[(bi * NP + p) * 32 + bl];
+          const int tok = M == 1 ? 0 : 2 * p + ((lane >> 1) & 1);
+          const float sx = sxs[bi * M + tok];
+          int d[4];
+          mma_s8_16832(it.q[j], bf, d);
+          acc[p][0] = fmaf(__fmul_rn(ds.x, sx), (float)(d[0] * 128 + d[1]), acc[p][0]);
+          acc[p][1] = fmaf(__fmul_rn(ds.y, sx), (float)(d[2] * 128 + d[3]), acc[p][1]);
+        }
+      }
+    }
+    const int done_vt = vt, done_kc = kc;
+    if (++vt == g.n_vt) {
+      vt = 0;
+      kc++;
+    }
+    left--;
+    if (left > 0) load_item(W, g, vt_tile(a, g, vt), kc, lane, it);
+    const float wgt = (lane & 1) ? 0x1p-21f : 0x1p-7f;
+    float* P = a.part + ((size_t)done_vt * g.nc + done_kc) * M * 16;
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+      float v0 = acc[p][0] * wgt, v1 = acc[p][1] * wgt;
+      v0 += __shfl_down_sync(0xffffffffu, v0, 1);
+      v1 += __shfl_down_sync(0xffffffffu, v1, 1);
+      const int tok = 2 * p + ((lane >> 1) & 1);
+      if ((lane & 1) == 0 && tok < M) {
+        __stcg(P + tok * 16 + (lane >> 2), v0);
+        __stcg(P + tok * 16 + (lane >> 2) + 8, v1);
+      }
+    }
+  }
+}
+
+// Row sums over the k-chunks in a fixed order (four lanes per output unit each add a
+// contiguous quarter of the chunks, then the quarters are added in order), then the
+// epilogue. Units: rows (STORE / ADD / ARGMAX) or gate/up row pairs (SWIGLU) per token.
+template <int M, int EPI>
+__global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo g) {
+  pdl_launch_dependents();
+  pdl_wait();
+  constexpr int R = EPI == EPI_SWIGLU ? 8 : 16;  // units per tile and token
+  const int lane = threadIdx.x & 31, q4 = lane & 3;
+  const long long u = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+  const bool live = u < (long long)g.n_vt * R * M;
+  const int vt = live ? (int)(u / (R * M)) : 0;
+  const int m = live ? (int)((u / R) % M) : 0;
+  const int r = live ? (int)(u % R) : 0;
+  float s0 = 0.f, s1 = 0.f;
+  if (live) {
+    const float* p = a.part + ((size_t)vt * g.nc * M + m) * 16 + r;
+    const int k0 = q4 * g.nc / 4, k1 = (q4 + 1) * g.nc / 4;
+#pragma unroll 4
+    for (int kc = k0; kc < k1; kc++) {
+      s0 += __ldcg(p + (size_t)kc * M * 16);
+      if (EPI == EPI_SWIGLU) s1 += __ldcg(p + (size_t)kc * M * 16 + 8);
+    }
+  }
+  const int base = lane & ~3;
+  const float t0 = ((__shfl_sync(0xffffffffu, s0, base) + __shfl_sync(0xffffffffu, s0, base + 1)) +
+                    __shfl_sync(0xffffffffu, s0, base + 2)) +
+                   __shfl_sync(0xffffffffu, s0, base + 3);
+  const float t1 = ((__shfl_sync(0xffffffffu, s1, base) + __shfl_sync(0xffffffffu, s1, base + 1)) +
+                    __shfl_sync(0xffffffffu, s1, base + 2)) +
+                   __shfl_sync(0xffffffffu, s1, base + 3);
+  const bool lead = live && q4 == 0 && m < a.M;
+  if constexpr (EPI == EPI_SWIGLU) {
+    // tile j holds gate rows 8j..8j+7 (tile rows 0-7) and up rows 8j..8j+7 (rows 8-15)
+    const int j = (g.t_first + vt) * 8 + r;
+    if (lead && j < a.n_range / 2) a.y[(size_t)m * a.ldy + j] = __fmul_rn(silu_f(t0), t1);
+  } else {
+    int pr;
+    bool valid;
+    if (vt < g.n_rt) {
+      pr = (g.t_first + vt) * 16 + r;
+      valid = pr >= a.row_base && pr < a.row_base + a.n_range;
+    } else {
+      pr = a.extra[vt - g.n_rt];
+      valid = (pr & 15) == r;
+    }
+    valid = valid && lead;
+    float v = t0;
+    if (valid && a.bias) v = __fadd_rn(v, a.bias[pr]);
+    if constexpr (EPI == EPI_ARGMAX) {
+      unsigned long long key = 0ull;
+      if (valid) {
+        if (a.y) a.y[(size_t)m * a.ldy + pr] = v;
+        const uint32_t ur = (uint32_t)pr;
+        if ((ur >= a.allow_lo && ur <= a.allow_hi) || (ur >= a.stop_lo && ur < a.stop_hi)) key = argmax_key(v, ur);
+      }
+      // a warp covers 8 consecutive units of one (tile, token): one atomic per warp
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if (lane == 0 && key != 0ull) atomicMax(a.amax + m, key);
+    } else if (valid) {
+      float* dst = a.y + (size_t)m * a.ldy + pr;
+      if constexpr (EPI == EPI_ADD)
+        *dst = __fadd_rn(ld_cg(dst), v);
+      else
+        *dst = v;
+    }
+  }
+}
+
+int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int M, int EPI>
+cudaError_t launch_merge(const GemvArgs& a, const Q8Geo& g, cudaStream_t st) {
+  constexpr int R = EPI == EPI_SWIGLU ? 8 : 16;
+  const long long threads = (long long)g.n_vt * R * M * 4;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_cfg(dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, attr);
+  return cudaLaunchKernelEx(&cfg, k_merge_q8<M, EPI>, a, g);
+}
+
+template <int M>
+cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st) {
+  constexpr int NP = (M + 1) / 2;
+  static const int sms = num_sms();
+  auto kern = k_gemv_q8<M>;
+  const long long I = (long long)g.n_vt * g.nc;
+  // persistent grid of up to three CTAs per SM; shared memory holds the limbs of the
+  // k-chunks a CTA spans (at most ceil(items per CTA / n_vt) + 1 of them)
+  int per_sm = 3, grid = 1;
+  size_t smem = 0;
+  for (;;) {
+    grid = (int)std::max(1LL, std::min(I, (long long)per_sm * sms));
+    const long long ipc = (I + grid - 1) / grid;
+    const long long spans = std::min<long long>(g.nc, (ipc + g.n_vt - 1) / g.n_vt + 1);
+    smem = (size_t)spans * kCB * (NP * 256 + M * 4);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    int occ = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (occ >= per_sm || per_sm == 1) break;
+    per_sm = std::max(1, std::min(per_sm - 1, occ));
+  }
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kThreads), smem, st, attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, g);
+  if (e != cudaSuccess) return e;
+  switch (epi) {
+    case EPI_STORE: return launch_merge<M, EPI_STORE>(a, g, st);
+    case EPI_ADD: return launch_merge<M, EPI_ADD>(a, g, st);
+    case EPI_SWIGLU: return launch_merge<M, EPI_SWIGLU>(a, g, st);
+    case EPI_ARGMAX: return launch_merge<M, EPI_ARGMAX>(a, g, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+bool make_geo(const GemvArgs& a, Q8Geo* g) {
+  const int64_t K = a.w.cols;
+  if (K <= 0 || K % 32 || a.n_range < 0 || a.n_extra < 0 || a.n_extra > 4 || a.n_range + a.n_extra < 1) return false;
+  if (a.row_base < 0 || (int64_t)a.row_base + a.n_range > a.w.rows) return false;
+  for (int i = 0; i < a.n_extra; i++)
+    if (a.extra[i] < 0 || a.extra[i] >= a.w.rows) return false;
+  g->K = (int)K;
+  g->nb = (int)(K / 32);
+  g->nc = (g->nb + kCB - 1) / kCB;
+  g->t_first = a.row_base / kQ8Tile;
+  g->n_rt = a.n_range > 0 ? (a.row_base + a.n_range + kQ8Tile - 1) / kQ8Tile - g->t_first : 0;
+  g->n_vt = g->n_rt + a.n_extra;
+  return true;
+}
+
+}  // namespace
+
+size_t q8_part_floats(const DevMat& w, int64_t n_rows, int M) {
+  const int64_t nc = (w.cols / 32 + kCB - 1) / kCB;
+  return (size_t)(q8_tiles(n_rows) + 1 + 4) * nc * M * 16;
+}
+
+cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st) {
+  Q8Geo g;
+  if (a.w.dtype != SX_DTYPE_Q8_0 || !a.part || a.M < 1 || a.M > kMaxTok || !make_geo(a, &g))
+    return cudaErrorInvalidValue;
+  // the SwiGLU pairing is per tile of the whole interleaved matrix
+  if (epi == EPI_SWIGLU && (a.row_base != 0 || a.n_extra != 0)) return cudaErrorInvalidValue;
+  const int Mt = a.M <= 1 ? 1 : a.M <= 2 ? 2 : a.M <= 4 ? 4 : 8;
+  if ((size_t)g.n_vt * g.nc * Mt * 16 > a.part_cap) return cudaErrorInvalidValue;
+  switch (Mt) {
+    case 1: return launch_m<1>(a, epi, g, st);
+    case 2: return launch_m<2>(a, epi, g, st);
+    case 4: return launch_m<4>(a, epi, g, st);
+    default: return launch_m<8>(a, epi, g, st);
+  }
+}
+
+}  // namespace sx

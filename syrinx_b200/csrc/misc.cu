@@ -31,8 +31,10 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAtt
 __device__ __forceinline__ float deq_elem(const DevMat& w, int64_t r, int64_t e) {
   const int64_t K = w.cols;
   if (w.dtype == SX_DTYPE_Q8_0) {
-    const float d = __half2float(w.s[r * w.s_stride + e / 32]);
-    return __fmul_rn((float)((int)((const uint8_t*)w.q)[r * K + e] - 128), d);
+    const uint8_t* rec = (const uint8_t*)w.q + ((r / kQ8Tile) * (K / 32) + e / 32) * kQ8Rec;
+    const int rr = (int)(r % kQ8Tile), kk = (int)(e % 32);
+    const float d = __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(rr)));
+    return __fmul_rn((float)(int8_t)rec[q8_quant_off(rr, kk)], d);
   } else if (w.dtype == SX_DTYPE_Q4_K) {
     const uint8_t* meta = w.meta + (r * (K / 256) + e / 256) * 16;
     const float d = __half2float(*reinterpret_cast<const __half*>(meta));
@@ -210,18 +212,22 @@ __global__ void k_advance(const AdvanceArgs a) {
   a.tok_pos[m] = len;
 }
 
-__global__ void k_repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
-                              int64_t s_stride, int row_mul, int row_add) {
+// GGML Q8_0 blocks {f16 d; i8 q[32]} of source row r -> the tile records of destination row
+// (r / grp) * grp * row_mul + row_add * grp + r % grp.
+__global__ void k_repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul,
+                              int row_add, int grp) {
   const int64_t nb = cols / 32;
   const int64_t total = rows * nb;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / nb, b = i % nb;
     const uint8_t* src = blocks + i * 34;
-    const int64_t dr = r * row_mul + row_add;
-    s[dr * s_stride + b] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
-    uint8_t* dq = reinterpret_cast<uint8_t*>(q) + dr * cols + b * 32;
-    for (int j = 0; j < 32; j++) dq[j] = (uint8_t)(src[2 + j] ^ 0x80u);  // q + 128
+    const int64_t dr = (r / grp) * grp * row_mul + (int64_t)row_add * grp + r % grp;
+    const int rr = (int)(dr % kQ8Tile);
+    uint8_t* dst = rec + ((dr / kQ8Tile) * nb + b) * kQ8Rec;
+    dst[q8_scale_off(rr)] = src[0];
+    dst[q8_scale_off(rr) + 1] = src[1];
+    for (int kk = 0; kk < 32; kk++) dst[q8_quant_off(rr, kk)] = src[2 + kk];
   }
 }
 
@@ -331,10 +337,11 @@ cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, k_advance, a);
 }
 
-cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
-                        int64_t s_stride, int row_mul, int row_add, cudaStream_t st) {
+cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul, int row_add,
+                        int grp, cudaStream_t st) {
+  if (grp < 1 || cols % 32) return cudaErrorInvalidValue;
   (void)cudaGetLastError();  // report this launch's status, not an earlier one
-  k_repack_q8_0<<<1184, 256, 0, st>>>(blocks, rows, cols, q, s, s_stride, row_mul, row_add);
+  k_repack_q8_0<<<1184, 256, 0, st>>>(blocks, rows, cols, rec, row_mul, row_add, grp);
   return cudaGetLastError();
 }
 

@@ -21,7 +21,7 @@ namespace sx {
 
 size_t DevMat::bytes() const {
   switch (dtype) {
-    case SX_DTYPE_Q8_0: return (size_t)rows * cols + (size_t)rows * s_stride * 2;
+    case SX_DTYPE_Q8_0: return (size_t)q8_tiles(rows) * (cols / 32) * kQ8Rec;
     case SX_DTYPE_Q4_K: return (size_t)rows * cols / 2 + (size_t)rows * (cols / 256) * 16;
     case SX_DTYPE_F32: return (size_t)rows * cols * 4;
   }
@@ -129,10 +129,9 @@ struct Loader {
       dst->rows = total_rows;
       dst->cols = cols;
       if (t->dtype == SX_DTYPE_Q8_0) {
-        int8_t* q;
-        SX_RC(dalloc(m->allocs, &q, (size_t)total_rows * cols));
-        dst->s_stride = q8_scale_stride(cols);
-        SX_RC(dalloc(m->allocs, &dst->s, (size_t)total_rows * dst->s_stride));
+        uint8_t* q;
+        SX_RC(dalloc(m->allocs, &q, dst->bytes()));
+        SX_CU(cudaMemset(q, 0, dst->bytes()));  // rows past N of the last tile stay zero
         dst->q = q;
       } else if (t->dtype == SX_DTYPE_Q4_K) {
         uint8_t* q;
@@ -161,8 +160,9 @@ struct Loader {
       staging_cap = t->nbytes;
     }
     SX_CU(cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
+    // Q8_0 interleaves w1/w3 per 16-row tile (8 gate rows, then their 8 up rows)
     if (t->dtype == SX_DTYPE_Q8_0)
-      SX_CU(repack_q8_0(staging, rows, cols, (int8_t*)dst->q, dst->s, dst->s_stride, row_mul, row_add, 0));
+      SX_CU(repack_q8_0(staging, rows, cols, (uint8_t*)dst->q, row_mul, row_add, row_mul == 2 ? 8 : 1, 0));
     else
       SX_CU(repack_q4_k(staging, rows, cols, (uint8_t*)dst->q, dst->meta, row_mul, row_add, 0));
     SX_CU(cudaStreamSynchronize(0));
@@ -366,6 +366,23 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
       (rc = dalloc(s->allocs, &s->hidden, (size_t)max_batch * dim)) ||
       (rc = dalloc(s->allocs, &s->amax, (size_t)max_batch)))
     return fail(rc);
+  {
+    // partial sums of the largest Q8_0 GEMV at the most tokens one launch takes
+    size_t cap = 0;
+    auto need = [&](const DevMat& w) {
+      if (w.dtype == SX_DTYPE_Q8_0) cap = std::max(cap, q8_part_floats(w, w.rows, kMaxTok));
+    };
+    for (const auto* ls : {&m->slow, &m->fast})
+      for (const DevLayer& L : *ls) {
+        need(L.wqkv);
+        need(L.wo);
+        need(L.w13);
+        need(L.w2);
+      }
+    for (const DevMat* w : {&m->emb, &m->cb_emb, &m->out_w, &m->fast_out, &m->fast_emb}) need(*w);
+    s->q8_part_cap = cap;
+    if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
+  }
   if (cudaMemset(s->amax, 0, (size_t)max_batch * 8) != cudaSuccess ||
       cudaMemset(s->err, 0, 4) != cudaSuccess || cudaMemset(s->frames, 0, (size_t)max_batch * width * 4) != cudaSuccess)
     return fail(SX_E_CUDA);
@@ -399,9 +416,10 @@ int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
   return std::max(1, std::min(kMaxCluster, (s->max_ctx + 63) / 64));
 }
 
-// Every GEMV reports bounded-wait timeouts through the session's device error flag.
+// Every GEMV gets the session's Q8_0 partial-sum buffer.
 int gemv(GemvArgs a, Epi epi, sx_session* s) {
-  a.err = s->err;
+  a.part = s->q8_part;
+  a.part_cap = s->q8_part_cap;
   SX_CU(launch_gemv(a, epi, s->st));
   return SX_OK;
 }

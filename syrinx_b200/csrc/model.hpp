@@ -65,6 +65,8 @@ struct sx_session {
   float* fast_logits = nullptr;  // [max_batch][R]
   float* hidden = nullptr;       // [max_batch][dim]
   unsigned long long* amax = nullptr;  // [max_batch]
+  float* q8_part = nullptr;  // Q8_0 GEMV partial sums [tile][k-chunk][token][16]
+  size_t q8_part_cap = 0;    // floats
   std::vector<int> len;  // host mirror of per-sequence cache lengths
   bool device_len_dirty = false;  // device seq_len advanced by a graph loop
   std::vector<GreedyGraph> graphs;

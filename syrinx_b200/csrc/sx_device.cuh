@@ -26,6 +26,20 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                : "l"(p));
   return v;
 }
+__device__ __forceinline__ uint32_t ldg_stream32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// ---- int8 tensor-core fragment product ------------------------------------------------
+// d = A (16 x 32, s8, row-major fragment a) x B (32 x 8, s8, column fragment b), exact s32.
+__device__ __forceinline__ void mma_s8_16832(const uint4& a, const uint2& b, int (&d)[4]) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(0));
+}
 
 // ---- packed f32x2 arithmetic (sm_100 FADD2/FFMA2: two lanes of IEEE f32 per issue) ------
 __device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
@@ -51,17 +65,6 @@ __device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigne
   unsigned long long d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
-}
-
-// The repacked Q8_0 layout stores every quant biased, u = q + 128 (one byte). Each u is
-// placed in the low mantissa byte of 2^23 (bit pattern 0x4B0000uu = 8388608 + u) and
-// 8388736 = 2^23 + 128 is subtracted: 4 biased bytes -> exact f32 q values, two per f32x2
-// register, on the byte-permute and f32x2 pipes (no per-word XOR).
-__device__ __forceinline__ void u8b4_to_f32x2x2(uint32_t u, unsigned long long& lo,
-                                                unsigned long long& hi) {
-  const unsigned long long bias = 0xCB000080CB000080ull;  // {-8388736.f, -8388736.f}
-  lo = add2(pack2u(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541)), bias);
-  hi = add2(pack2u(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543)), bias);
 }
 
 // 4-bit values in bytes (each byte 0..15, packed in a word) -> exact f32, two per f32x2.
@@ -106,76 +109,5 @@ __device__ __forceinline__ uint32_t argmax_row(unsigned long long key) {
 }
 
 __device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
-
-// ---- mbarrier + bulk asynchronous copy (TMA engine, no multicast) ----------------------
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-// Makes mbarrier initialisation visible to the asynchronous proxy (the copy engine).
-__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// try_wait with an explicit suspend-time hint: the thread sleeps until the phase completes
-// (woken by the barrier itself) or about `hint_ns` passes, whichever is first.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait on an mbarrier phase: gives up after about `limit_ns` nanoseconds of wall
-// time (globaltimer; each try_wait sleeps at most ~100 us) and returns false, so the caller
-// can record an error and stop; it never spins forever.
-constexpr uint32_t kTryWaitHintNs = 100000;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (;;) {
-    if (mbar_try_wait_hint(bar, parity, kTryWaitHintNs)) return true;
-    if (global_ns() - t0 > limit_ns) return false;
-  }
-}
-// Bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
-// dst, src 16-byte aligned; bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
 
 }  // namespace sx

@@ -1,18 +1,22 @@
 // sx_internal.hpp — device data layout and kernel launch interfaces of the B200 path.
 //
 // HBM layout (all device memory owned by the library):
-//   Q8_0 weight [N][K]  -> q : u8 [N][K] = int8 quant + 128 (row-major, one row = K bytes,
-//                              16-B aligned; the bias spares the unpack an XOR per word)
-//                          s : f16  [N][s_stride] block scales, s_stride = K/32 rounded up
-//                              to 8 so every row's scales start on a 16-byte boundary (a
-//                              legal bulk-copy source for any row chunk)
+//   Q8_0 weight [N][K]  -> tile records: ceil(N/16) tiles of 16 rows, each stored as K/32
+//                          consecutive 544-byte records, one per 32-wide k block:
+//                            [0, 512)   the 16 x 32 int8 quants in the A-operand fragment
+//                                       order of mma.m16n8k32 (row-major A): lane t = 4g + c
+//                                       owns bytes [16t, 16t + 16) = {row g, k 4c..4c+3 |
+//                                       row g+8, same k | row g, k 16+4c.. | row g+8, k 16+4c..}
+//                            [512, 544) the 16 f16 block scales as 8 words {d[w], d[w+8]}
+//                          so one coalesced 16-byte load per lane feeds one tensor-core
+//                          instruction and a matrix is one contiguous stream of exactly
+//                          N x K x 34/32 bytes. Rows past N are zero. w1/w3 are interleaved
+//                          per tile: tile j holds gate rows 8j..8j+7 then up rows 8j..8j+7.
 //   Q4_K weight [N][K]  -> q : u8   [N][K/2] (GGML nibble order inside each 256 super-block)
 //                          meta : 16 B [N][K/256] = {f16 d, f16 dmin, u8 scales[12]}
-//   F32  weight [N][K]  -> f : f32 [N][K]
-//   The GGML array-of-blocks layout (34-B Q8_0 blocks are not 16-B aligned) is split into
-//   these structure-of-arrays forms at load, losslessly, so every GEMV lane issues 128-bit
-//   coalesced loads. w1/w3 are interleaved row by row (g0,u0,g1,u1,...) so one warp owns a
-//   gate/up pair and applies SiLU(g)*u in its epilogue.
+//                          w1/w3 interleaved row by row (g0,u0,g1,u1,...).
+//   F32  weight [N][K]  -> f : f32 [N][K] (w1/w3 interleaved row by row)
+//   The GGML array-of-blocks layouts are rewritten into these forms at load, losslessly.
 //   KV cache: f32 (default) or bf16 pages of PAGE positions, per layer
 //   [2][n_pages][Hkv][PAGE][hd], with a per-sequence page table [max_batch][pages_per_seq]
 //   of int32 page ids.
@@ -38,13 +42,21 @@ constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one 
 struct DevMat {
   int dtype = -1;
   int64_t rows = 0, cols = 0;
-  void* q = nullptr;     // Q8_0 int8 / Q4_K nibbles / F32 values
-  __half* s = nullptr;   // Q8_0 scales
-  int64_t s_stride = 0;  // Q8_0 scales per row in memory (K/32 rounded up to 8)
+  void* q = nullptr;        // Q8_0 tile records / Q4_K nibbles / F32 values
   uint8_t* meta = nullptr;  // Q4_K 16-B super-block headers
   size_t bytes() const;
 };
-inline int64_t q8_scale_stride(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
+
+// Q8_0 tile-record geometry (see the layout above).
+constexpr int kQ8Tile = 16;
+constexpr int kQ8Rec = 544;
+inline int64_t q8_tiles(int64_t rows) { return (rows + kQ8Tile - 1) / kQ8Tile; }
+// byte offset of quant (tile row rr, k kk) inside its record
+__host__ __device__ inline int q8_quant_off(int rr, int kk) {
+  return ((rr & 7) * 4 + ((kk & 15) >> 2)) * 16 + ((kk >> 4) * 2 + (rr >> 3)) * 4 + (kk & 3);
+}
+// byte offset of tile row rr's f16 scale inside its record
+__host__ __device__ inline int q8_scale_off(int rr) { return 512 + (rr & 7) * 4 + (rr >> 3) * 2; }
 
 struct DevLayer {
   float* attn_norm = nullptr;
@@ -61,7 +73,7 @@ struct DevLayer {
 enum Epi : int {
   EPI_STORE = 0,   // y[m][row] = acc (+ bias[row])
   EPI_ADD = 1,     // y[m][row] = y[m][row] + (acc (+ bias[row]))   (residual add)
-  EPI_SWIGLU = 2,  // rows (2j, 2j+1) = (gate_j, up_j): y[m][j] = silu(g) * u
+  EPI_SWIGLU = 2,  // y[m][j] = silu(gate_j) * up_j, pairs as the w1/w3 interleave places them
   EPI_ARGMAX = 3,  // logits (stored if y != null) + packed argmax over allowed rows
 };
 
@@ -81,8 +93,12 @@ struct GemvArgs {
   // argmax epilogue: allowed = [allow_lo, allow_hi] U [stop_lo, stop_hi) (stops when !mask)
   unsigned long long* amax = nullptr;  // [M] packed (orderable f32 << 32 | ~row)
   uint32_t allow_lo = 0, allow_hi = 0, stop_lo = 0, stop_hi = 0;
-  int* err = nullptr;  // device error flag (2 = a bounded pipeline wait timed out)
+  // Q8_0 only: per-(tile, k-chunk) partial sums, part_cap floats (q8_part_floats)
+  float* part = nullptr;
+  size_t part_cap = 0;
 };
+// floats of partial sums a Q8_0 GEMV over `w` with `n_rows` logical rows needs at M tokens
+size_t q8_part_floats(const DevMat& w, int64_t n_rows, int M);
 
 struct AttnArgs {
   const float* qkv = nullptr;  // [M][(H + 2 Hkv) hd]
@@ -108,11 +124,10 @@ struct AttnArgs {
 };
 
 // ---- launchers (stream-ordered, programmatic dependent launch enabled) ----------------
-// launch_gemv runs the register-streaming kernel; with SYRINX_GEMV_TMA=1 it runs the
-// TMA-fed batch-1 Q8_0 kernel for the shapes that kernel accepts.
+// launch_gemv: Q8_0 weights run the tensor-core kernel plus its merge (gemv_q8.cu),
+// Q4_K / F32 the register-streaming kernel (gemv.cu).
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st);
-bool gemv_tma_eligible(const GemvArgs& a);
-cudaError_t launch_gemv_tma(const GemvArgs& a, Epi epi, cudaStream_t st);
+cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st);
 
@@ -173,9 +188,10 @@ struct AdvanceArgs {
 cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st);
 
 // repack / dequant
-// destination row of source row r is r * row_mul + row_add (w1/w3 interleave)
-cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* q, __half* s,
-                        int64_t s_stride, int row_mul, int row_add, cudaStream_t st);
+// destination row of source row r is r * row_mul + row_add (w1/w3 interleave); for Q8_0
+// it is (r / grp) * grp * row_mul + row_add * grp + r % grp (grp 8: the per-tile interleave)
+cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul, int row_add,
+                        int grp, cudaStream_t st);
 cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* q, uint8_t* meta,
                         int row_mul, int row_add, cudaStream_t st);
 cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out,
