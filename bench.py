@@ -34,10 +34,11 @@ PROMPT_T = 512
 PROMPT_SEMANTIC = 430
 SEED = 2
 METRIC = "semantic frames/s/GPU, 4B-shape Q8_0 dual-AR decode b1/b8; % of HBM roofline"
-# DRAM bytes (read + write) of one launch of the dominant kernel, the batch-1 w1|w3 GEMV,
-# from one `ncu --set full` capture (python -m syrinx_b200.profile --what gemv --kind 2
-# --layers 8 --launches 16): 52.99 MB read + 0.15 MB written against 52.92 MB algorithmic.
-W13_DRAM_BYTES = 53137664
+# DRAM bytes (read + write) of one launch of the dominant kernel, the batch-1 w1|w3 GEMV
+# (k_gemv_q8<1>), from one `ncu --set full` capture (python -m syrinx_b200.profile --what
+# gemv --kind 2 --layers 8 --launches 16): 52.97 MB read + 0.11 MB written against 52.92 MB
+# algorithmic.
+W13_DRAM_BYTES = 53085184
 
 
 def peaks():
@@ -228,7 +229,7 @@ def bench_device(args):
         "hbm_roofline": {"bytes_per_frame": fb_sem["total"], "frac_of_peak": round(
             fb_sem["total"] * value / world / (peak * 1e9), 4), "peak_gbs": peak, "peak_kind": peak_kind,
             "note": "semantic-only head (4097 rows) counted, as streamed"},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv Q8_0 M=1 w1|w3 (+RMSNorm prologue, SwiGLU epilogue)",
+        "roofline": {"bound": "hbm", "kernel": "k_gemv_q8<1> + k_merge_q8<1,SwiGLU>: Q8_0 w1|w3 at M=1 (timed as the pair)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": W13_DRAM_BYTES,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
