@@ -122,6 +122,15 @@ int sx_synth_blob_write(const sx_model_desc* desc, int32_t wtype, uint64_t seed,
  * (s2/mod.rs:119-167) and `Qwen2Lm::load_quantized` (cv2/load.rs:68-122). */
 int sx_model_create(const sx_model_desc* desc, const void* blob, size_t blob_size, int32_t device,
                     sx_model** out);
+/* Tensor-parallel shard (no reference counterpart: the reference decodes on one device).
+ * Rank tp_rank of tp_size (<= 8; one process per GPU) uploads query heads
+ * [r*H/tp, (r+1)*H/tp) and kv heads [r*Hkv/tp, ...) of every wqkv, FFN rows
+ * [r*F/tp, (r+1)*F/tp) of w1 and w3, and the matching input columns of wo and w2; norms,
+ * embeddings and heads are replicated. Q8_0 weights; heads, kv heads and F must divide by
+ * tp_size into whole 32-column blocks. Every rank loads the same blob and must then make
+ * the same calls in the same order (they exchange residual rows after wo and w2). */
+int sx_model_create_tp(const sx_model_desc* desc, const void* blob, size_t blob_size, int32_t device,
+                       int32_t tp_rank, int32_t tp_size, sx_model** out);
 int sx_model_destroy(sx_model* model);
 /* Device bytes held by the model's weights. */
 int sx_model_weight_bytes(const sx_model* model, size_t* bytes_out);
@@ -134,6 +143,18 @@ int sx_model_weight_bytes(const sx_model* model, size_t* bytes_out);
 int sx_session_create(sx_model* model, int32_t max_batch, int32_t max_ctx, sx_session** out);
 int sx_session_create_ex(sx_model* model, int32_t max_batch, int32_t max_ctx, int32_t kv_dtype,
                          sx_session** out);
+/* Tensor-parallel sessions (no reference counterpart). Each rank writes its session's
+ * SX_TP_HANDLE_BYTES-byte handle (a CUDA IPC handle of its exchange region, its GPU's UUID,
+ * rank and size), the caller gathers all handles in rank order (e.g. an all-gather over
+ * torch.distributed), and every rank passes the whole array to sx_session_tp_connect before
+ * its first decode call. Ranks on the same GPU are refused. A peer that does not reach a
+ * residual exchange within 5 s makes the call return SX_E_DEVICE. */
+#define SX_TP_HANDLE_BYTES 128
+int sx_session_tp_handle(sx_session* s, void* handle_out);
+int sx_session_tp_connect(sx_session* s, const void* handles);
+/* Unmap the peers' regions (after the group's last decode call, before any rank destroys
+ * its session: put a barrier between the two). */
+int sx_session_tp_disconnect(sx_session* s);
 /* Clear every sequence (the reference `reset`, dualar.rs:73). */
 int sx_session_reset(sx_session* s);
 int sx_session_destroy(sx_session* s);

@@ -25,10 +25,15 @@ SIGNATURES = {
     "sx_synth_blob_size": (C.c_int, [C.POINTER(SxModelDesc), C.c_int32, C.POINTER(C.c_size_t)]),
     "sx_synth_blob_write": (C.c_int, [C.POINTER(SxModelDesc), C.c_int32, C.c_uint64, C.c_void_p, C.c_size_t]),
     "sx_model_create": (C.c_int, [C.POINTER(SxModelDesc), C.c_void_p, C.c_size_t, C.c_int32, C.POINTER(C.c_void_p)]),
+    "sx_model_create_tp": (C.c_int, [C.POINTER(SxModelDesc), C.c_void_p, C.c_size_t, C.c_int32, C.c_int32, C.c_int32,
+                                      C.POINTER(C.c_void_p)]),
     "sx_model_destroy": (C.c_int, [C.c_void_p]),
     "sx_model_weight_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
     "sx_session_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "sx_session_create_ex": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "sx_session_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "sx_session_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "sx_session_tp_disconnect": (C.c_int, [C.c_void_p]),
     "sx_session_reset": (C.c_int, [C.c_void_p]),
     "sx_session_destroy": (C.c_int, [C.c_void_p]),
     "sx_session_len": (C.c_int, [C.c_void_p, C.c_int32, _i32p]),

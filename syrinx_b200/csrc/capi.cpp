@@ -137,6 +137,23 @@ int sx_model_create(const sx_model_desc* desc, const void* blob, size_t blob_siz
   SX_GUARD({ return model_create(desc, blob, blob_size, device, out); })
 }
 
+int sx_model_create_tp(const sx_model_desc* desc, const void* blob, size_t blob_size, int32_t device,
+                       int32_t tp_rank, int32_t tp_size, sx_model** out) {
+  SX_GUARD({ return model_create(desc, blob, blob_size, device, out, tp_rank, tp_size); })
+}
+
+int sx_session_tp_handle(sx_session* s, void* handle_out) {
+  SX_GUARD({ return session_tp_handle(s, handle_out); })
+}
+
+int sx_session_tp_connect(sx_session* s, const void* handles) {
+  SX_GUARD({ return session_tp_connect(s, handles); })
+}
+
+int sx_session_tp_disconnect(sx_session* s) {
+  SX_GUARD({ return session_tp_disconnect(s); })
+}
+
 int sx_model_destroy(sx_model* model) {
   SX_GUARD({
     model_destroy(model);

@@ -283,6 +283,82 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
   }
 }
 
+// Residual add of a K-split (tensor-parallel) GEMV. Each rank adds up its own k-chunk
+// partials per row exactly as k_merge_q8 does and publishes those rows in its exchange
+// buffer; thread 0 then tells every peer (a release store into the peer's flag for this CTA,
+// over NVLink) and waits, bounded by %globaltimer, until every peer's flag for this CTA shows
+// the same exchange. The rows of all ranks are then added in rank order, so every rank
+// computes bit-identical residuals. Exchange e uses buffer half e % 2: a rank reaches
+// exchange e + 2 only after every peer has signalled e + 1, which each peer does only after
+// its kernel for exchange e (its reads of half e % 2) has completed.
+// After a timeout the session's error flag stays raised until the host reads it, and later
+// exchanges skip their wait, so a lost peer costs one bounded wait, not one per exchange.
+constexpr uint64_t kTpWaitNs = 5000000000ull;
+
+template <int M>
+__global__ void __launch_bounds__(256) k_merge_q8_tp(const GemvArgs a, const Q8Geo g) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  const TpComm& tp = a.tp;
+  const int lane = threadIdx.x & 31, q4 = lane & 3;
+  const long long u = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+  const bool live = u < (long long)g.n_vt * 16 * M;
+  const int vt = live ? (int)(u / (16 * M)) : 0;
+  const int m = live ? (int)((u / 16) % M) : 0;
+  const int r = live ? (int)(u % 16) : 0;
+  float s0 = 0.f;
+  if (live) {
+    const float* p = a.part + ((size_t)vt * g.nc * M + m) * 16 + r;
+    const int k0 = q4 * g.nc / 4, k1 = (q4 + 1) * g.nc / 4;
+#pragma unroll 4
+    for (int kc = k0; kc < k1; kc++) s0 += __ldcg(p + (size_t)kc * M * 16);
+  }
+  const int base = lane & ~3;
+  const float t0 = ((__shfl_sync(0xffffffffu, s0, base) + __shfl_sync(0xffffffffu, s0, base + 1)) +
+                    __shfl_sync(0xffffffffu, s0, base + 2)) +
+                   __shfl_sync(0xffffffffu, s0, base + 3);
+  const int pr = (g.t_first + vt) * 16 + r;
+  const bool valid = live && q4 == 0 && m < a.M && pr >= a.row_base && pr < a.row_base + a.n_range;
+  if (threadIdx.x == 0) {
+    s_epoch = tp.epochs[blockIdx.x] + 1;
+    tp.epochs[blockIdx.x] = s_epoch;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t ep = s_epoch;
+  const size_t off = (size_t)(ep & 1) * tp.xb_cap + (size_t)m * a.ldy + pr;
+  if (valid) tp.xb[tp.rank][off] = t0;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int p = 0; p < tp.size; p++)
+      if (p != tp.rank) st_release_sys(tp.flags[p] + (size_t)tp.rank * kMaxTpCtas + blockIdx.x, ep);
+    if (ld_cg(tp.err) != 0) s_ok = 0;
+    const uint64_t t_start = global_ns();
+    for (int p = 0; p < tp.size && s_ok; p++) {
+      if (p == tp.rank) continue;
+      const uint32_t* f = tp.flags[tp.rank] + (size_t)p * kMaxTpCtas + blockIdx.x;
+      while ((int)(ld_acquire_sys(f) - ep) < 0) {
+        if (global_ns() - t_start > kTpWaitNs) {
+          s_ok = 0;
+          atomicExch(tp.err, 3);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_ok || !valid) return;
+  float tot = 0.f;
+  for (int q = 0; q < tp.size; q++) tot += q == tp.rank ? tp.xb[q][off] : ld_relaxed_sys(tp.xb[q] + off);
+  float v = tot;
+  if (a.bias) v = __fadd_rn(v, a.bias[pr]);
+  float* dst = a.y + (size_t)m * a.ldy + pr;
+  *dst = __fadd_rn(ld_cg(dst), v);
+}
+
 int num_sms() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -328,6 +404,13 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
   cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kThreads), smem, st, attr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, g);
   if (e != cudaSuccess) return e;
+  if (epi == EPI_ADD && a.tp.size > 1) {
+    const long long blocks = ((long long)g.n_vt * 16 * M * 4 + 255) / 256;
+    if (blocks > kMaxTpCtas || a.n_extra != 0 || (long long)M * a.ldy > a.tp.xb_cap) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr2[1];
+    cudaLaunchConfig_t cfg2 = launch_cfg(dim3((unsigned)blocks), dim3(256), 0, st, attr2);
+    return cudaLaunchKernelEx(&cfg2, k_merge_q8_tp<M>, a, g);
+  }
   switch (epi) {
     case EPI_STORE: return launch_merge<M, EPI_STORE>(a, g, st);
     case EPI_ADD: return launch_merge<M, EPI_ADD>(a, g, st);

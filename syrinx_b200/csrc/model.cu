@@ -114,12 +114,72 @@ struct Loader {
     return SX_OK;
   }
 
-  // Upload `name` [rows x cols] into dst at destination rows r*row_mul + row_add;
-  // dst spans total_rows rows and is allocated on first use.
-  int mat(const std::string& name, int64_t rows, int64_t cols, DevMat* dst, int64_t total_rows,
-          int row_mul = 1, int row_add = 0) {
-    const BlobTensor* t = get(name, rows, cols);
+  // A tensor-parallel shard of a blob tensor: the listed row ranges, concatenated, and the
+  // element columns [c0, c0 + cols) (cols < 0: all), block-aligned for quantized types.
+  struct Slice {
+    std::vector<std::pair<int64_t, int64_t>> rows;  // (first row, count)
+    int64_t c0 = 0, cols = -1;
+  };
+
+  int slice(const BlobTensor& t, const Slice& sl, std::vector<uint8_t>* host, BlobTensor* v) {
+    const int64_t per = t.dtype == SX_DTYPE_Q8_0 ? 32 : t.dtype == SX_DTYPE_Q4_K ? 256 : 1;
+    const size_t bb = t.dtype == SX_DTYPE_Q8_0 ? 34 : t.dtype == SX_DTYPE_Q4_K ? 144 : 4;
+    const int64_t cols = sl.cols < 0 ? t.cols : sl.cols;
+    if (sl.c0 % per || cols % per || sl.c0 < 0 || sl.c0 + cols > t.cols) {
+      set_error("tensor-parallel shard of " + t.name + " is not aligned to its quantization blocks");
+      return SX_E_UNSUPPORTED;
+    }
+    int64_t nrows = 0;
+    for (const auto& r : sl.rows) {
+      if (r.first < 0 || r.first + r.second > t.rows) {
+        set_error("tensor-parallel shard of " + t.name + " is out of range");
+        return SX_E_INVALID;
+      }
+      nrows += r.second;
+    }
+    const size_t src_row = row_bytes(t.dtype, t.cols), dst_row = (size_t)(cols / per) * bb;
+    const size_t off = (size_t)(sl.c0 / per) * bb;
+    host->resize((size_t)nrows * dst_row);
+    uint8_t* dst = host->data();
+    for (const auto& r : sl.rows)
+      for (int64_t i = r.first; i < r.first + r.second; i++, dst += dst_row)
+        std::memcpy(dst, t.data + (size_t)i * src_row + off, dst_row);
+    *v = t;
+    v->rows = nrows;
+    v->cols = cols;
+    v->data = host->data();
+    v->nbytes = host->size();
+    return SX_OK;
+  }
+
+  int vec_slice(const std::string& name, int64_t n, const Slice& sl, float** out) {
+    const BlobTensor* t = get(name, 1, n);
     if (!t) return SX_E_BLOB;
+    if (t->dtype != SX_DTYPE_F32) {
+      set_error("weight blob: " + name + " must be f32");
+      return SX_E_BLOB;
+    }
+    std::vector<float> v;
+    for (const auto& r : sl.rows)
+      v.insert(v.end(), (const float*)t->data + r.first, (const float*)t->data + r.first + r.second);
+    SX_RC(dalloc(m->allocs, out, v.size()));
+    SX_CU(cudaMemcpy(*out, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+    m->weight_bytes += v.size() * 4;
+    return SX_OK;
+  }
+
+  // Upload `name` [rows x cols] (or its shard `sl`) into dst at destination rows
+  // r*row_mul + row_add; dst spans total_rows rows and is allocated on first use.
+  int mat(const std::string& name, int64_t rows, int64_t cols, DevMat* dst, int64_t total_rows,
+          int row_mul = 1, int row_add = 0, const Slice* sl = nullptr) {
+    const BlobTensor* full = get(name, rows, cols);
+    if (!full) return SX_E_BLOB;
+    BlobTensor view = *full;
+    std::vector<uint8_t> host;
+    if (sl) SX_RC(slice(*full, *sl, &host, &view));
+    const BlobTensor* t = &view;
+    rows = t->rows;
+    cols = t->cols;
     if (t->dtype != SX_DTYPE_Q8_0 && t->dtype != SX_DTYPE_Q4_K && t->dtype != SX_DTYPE_F32) {
       set_error("weight blob: " + name + " has an unsupported dtype (Q8_0, Q4_K or F32)");
       return SX_E_UNSUPPORTED;
@@ -169,25 +229,47 @@ struct Loader {
     return SX_OK;
   }
 
+  // One transformer stack in the blob's (global) geometry `td`. Under tensor parallelism
+  // rank r keeps query heads [r*H/tp, (r+1)*H/tp) and kv heads [r*Hkv/tp, ...) of wqkv (its
+  // q, k and v rows), FFN rows [r*F/tp, (r+1)*F/tp) of w1 and w3, and the matching input
+  // columns of wo and w2, whose outputs the residual merge adds up across ranks.
   int layers(const sx_transformer_desc& td, const char* prefix, std::vector<DevLayer>* out) {
-    const int64_t qkv = (int64_t)(td.n_head + 2 * td.n_local_heads) * td.head_dim;
+    const int tp = m->tp_size, r = m->tp_rank;
+    const int64_t hd = td.head_dim, H = td.n_head, Hkv = td.n_local_heads, F = td.intermediate_size;
+    const int64_t Hl = H / tp, Hkvl = Hkv / tp, Fl = F / tp;
+    const int64_t qkv = (H + 2 * Hkv) * hd, qkv_l = (Hl + 2 * Hkvl) * hd;
+    Slice s_qkv, s_wo, s_f, s_w2;
+    s_qkv.rows = {{r * Hl * hd, Hl * hd}, {H * hd + r * Hkvl * hd, Hkvl * hd},
+                  {(H + Hkv) * hd + r * Hkvl * hd, Hkvl * hd}};
+    s_wo.rows = {{0, td.dim}};
+    s_wo.c0 = r * Hl * hd;
+    s_wo.cols = Hl * hd;
+    s_f.rows = {{r * Fl, Fl}};
+    s_w2.rows = {{0, td.dim}};
+    s_w2.c0 = r * Fl;
+    s_w2.cols = Fl;
+    const bool sh = tp > 1;
     for (int l = 0; l < td.n_layer; l++) {
       const std::string p = std::string(prefix) + "." + std::to_string(l) + ".";
       DevLayer L;
       SX_RC(vec(p + "attention_norm.weight", td.dim, &L.attn_norm));
-      SX_RC(mat(p + "attention.wqkv.weight", qkv, td.dim, &L.wqkv, qkv));
-      if (td.qkv_bias) SX_RC(vec(p + "attention.wqkv.bias", qkv, &L.bqkv));
+      SX_RC(mat(p + "attention.wqkv.weight", qkv, td.dim, &L.wqkv, qkv_l, 1, 0, sh ? &s_qkv : nullptr));
+      if (td.qkv_bias) {
+        if (sh)
+          SX_RC(vec_slice(p + "attention.wqkv.bias", qkv, s_qkv, &L.bqkv));
+        else
+          SX_RC(vec(p + "attention.wqkv.bias", qkv, &L.bqkv));
+      }
       if (td.qk_norm) {
         SX_RC(vec(p + "attention.q_norm.weight", td.head_dim, &L.qn));
         SX_RC(vec(p + "attention.k_norm.weight", td.head_dim, &L.kn));
       }
-      SX_RC(mat(p + "attention.wo.weight", td.dim, (int64_t)td.n_head * td.head_dim, &L.wo, td.dim));
+      SX_RC(mat(p + "attention.wo.weight", td.dim, H * hd, &L.wo, td.dim, 1, 0, sh ? &s_wo : nullptr));
       if (td.o_bias) SX_RC(vec(p + "attention.wo.bias", td.dim, &L.bo));
       SX_RC(vec(p + "ffn_norm.weight", td.dim, &L.ffn_norm));
-      const int64_t F = td.intermediate_size;
-      SX_RC(mat(p + "feed_forward.w1.weight", F, td.dim, &L.w13, 2 * F, 2, 0));
-      SX_RC(mat(p + "feed_forward.w3.weight", F, td.dim, &L.w13, 2 * F, 2, 1));
-      SX_RC(mat(p + "feed_forward.w2.weight", td.dim, F, &L.w2, td.dim));
+      SX_RC(mat(p + "feed_forward.w1.weight", F, td.dim, &L.w13, 2 * Fl, 2, 0, sh ? &s_f : nullptr));
+      SX_RC(mat(p + "feed_forward.w3.weight", F, td.dim, &L.w13, 2 * Fl, 2, 1, sh ? &s_f : nullptr));
+      SX_RC(mat(p + "feed_forward.w2.weight", td.dim, F, &L.w2, td.dim, 1, 0, sh ? &s_w2 : nullptr));
       out->push_back(L);
     }
     return SX_OK;
@@ -207,9 +289,27 @@ int upload_inv_freq(sx_model* m, const sx_transformer_desc& td, float** out) {
 
 }  // namespace
 
-int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out) {
+// A transformer stack divides over tp ranks when its heads, kv heads and FFN rows do, and
+// the wo / w2 input-column shards stay whole Q8_0 blocks (Q4_K super-blocks).
+int check_tp(const sx_transformer_desc& t, int tp, const char* what) {
+  if (t.n_layer <= 0 || tp == 1) return SX_OK;
+  if (t.n_head % tp || t.n_local_heads % tp || t.intermediate_size % tp ||
+      ((int64_t)t.n_head / tp * t.head_dim) % 32 || (t.intermediate_size / tp) % 32) {
+    set_error(std::string(what) + ": heads, kv heads and FFN rows must split evenly over the " +
+              "tensor-parallel ranks into shards of whole 32-column blocks");
+    return SX_E_UNSUPPORTED;
+  }
+  return SX_OK;
+}
+
+int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out,
+                 int tp_rank, int tp_size) {
   if (!desc || !blob || !out) {
     set_error("sx_model_create: null argument");
+    return SX_E_INVALID;
+  }
+  if (tp_size < 1 || tp_size > kMaxTp || tp_rank < 0 || tp_rank >= tp_size) {
+    set_error("sx_model_create_tp: need 1 <= tp_size <= 8 and 0 <= tp_rank < tp_size");
     return SX_E_INVALID;
   }
   const sx_model_desc& d = *desc;
@@ -230,6 +330,8 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
     set_error("sx_model_desc: bad vocab / codebook / stop configuration");
     return SX_E_INVALID;
   }
+  SX_RC(check_tp(d.slow, tp_size, "slow"));
+  SX_RC(check_tp(d.fast, tp_size, "fast"));
   int ndev = 0;
   SX_CU(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) {
@@ -240,6 +342,8 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
   auto m = new sx_model();
   m->d = d;
   m->device = device;
+  m->tp_rank = tp_rank;
+  m->tp_size = tp_size;
   Loader L{m};
   std::string err;
   int rc = parse_blob(blob, size, &L.idx, &err);
@@ -275,6 +379,12 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
   }
   if ((rc = upload_inv_freq(m, d.slow, &m->inv_slow))) return fail(rc);
   if (d.fast.n_layer > 0 && (rc = upload_inv_freq(m, d.fast, &m->inv_fast))) return fail(rc);
+  // every later use sees this rank's geometry
+  for (sx_transformer_desc* t : {&m->d.slow, &m->d.fast}) {
+    t->n_head /= tp_size;
+    t->n_local_heads /= tp_size;
+    t->intermediate_size /= tp_size;
+  }
   *out = m;
   return SX_OK;
 }
@@ -383,6 +493,26 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
     s->q8_part_cap = cap;
     if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
   }
+  if (m->tp_size > 1) {
+    // exchange region: rows [2][xb_cap] | flags [kMaxTp][kMaxTpCtas]; peers map it by IPC
+    const int xb_cap = kMaxTok * dim;
+    s->tp_region_bytes = (size_t)2 * xb_cap * 4 + (size_t)kMaxTp * kMaxTpCtas * 4;
+    uint8_t* region = nullptr;
+    uint32_t* epochs = nullptr;
+    if ((rc = dalloc(s->allocs, &region, s->tp_region_bytes)) || (rc = dalloc(s->allocs, &epochs, kMaxTpCtas)))
+      return fail(rc);
+    if (cudaMemset(region, 0, s->tp_region_bytes) != cudaSuccess ||
+        cudaMemset(epochs, 0, (size_t)kMaxTpCtas * 4) != cudaSuccess)
+      return fail(SX_E_CUDA);
+    s->tp_region = region;
+    s->tp.rank = m->tp_rank;
+    s->tp.size = m->tp_size;
+    s->tp.xb_cap = xb_cap;
+    s->tp.xb[m->tp_rank] = reinterpret_cast<float*>(region);
+    s->tp.flags[m->tp_rank] = reinterpret_cast<uint32_t*>(region + (size_t)2 * xb_cap * 4);
+    s->tp.epochs = epochs;
+    s->tp.err = s->err;
+  }
   if (cudaMemset(s->amax, 0, (size_t)max_batch * 8) != cudaSuccess ||
       cudaMemset(s->err, 0, 4) != cudaSuccess || cudaMemset(s->frames, 0, (size_t)max_batch * width * 4) != cudaSuccess)
     return fail(SX_E_CUDA);
@@ -395,11 +525,94 @@ void session_destroy(sx_session* s) {
   cudaSetDevice(s->m->device);
   if (s->st) cudaStreamSynchronize(s->st);
   if (s->own_st) cudaStreamSynchronize(s->own_st);
+  for (void* p : s->tp_opened) cudaIpcCloseMemHandle(p);
   for (auto& g : s->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
   for (void* p : s->allocs) cudaFree(p);
   if (s->own_st) cudaStreamDestroy(s->own_st);
   delete s;
+}
+
+// Handle record: cudaIpcMemHandle_t (64 B) | device UUID (16 B) | rank | size (int32 each).
+int session_tp_handle(sx_session* s, void* out) {
+  if (!s || !out) {
+    set_error("sx_session_tp_handle: null argument");
+    return SX_E_INVALID;
+  }
+  if (s->m->tp_size < 2) {
+    set_error("sx_session_tp_handle: the model is not tensor-parallel");
+    return SX_E_INVALID;
+  }
+  SX_CU(cudaSetDevice(s->m->device));
+  cudaIpcMemHandle_t h;
+  SX_CU(cudaIpcGetMemHandle(&h, s->tp_region));
+  cudaDeviceProp prop;
+  SX_CU(cudaGetDeviceProperties(&prop, s->m->device));
+  uint8_t* o = static_cast<uint8_t*>(out);
+  std::memset(o, 0, SX_TP_HANDLE_BYTES);
+  std::memcpy(o, &h, sizeof(h));
+  std::memcpy(o + 64, &prop.uuid, 16);
+  const int32_t rs[2] = {s->m->tp_rank, s->m->tp_size};
+  std::memcpy(o + 80, rs, 8);
+  return SX_OK;
+}
+
+int session_tp_connect(sx_session* s, const void* handles) {
+  if (!s || !handles) {
+    set_error("sx_session_tp_connect: null argument");
+    return SX_E_INVALID;
+  }
+  const int tp = s->m->tp_size, me = s->m->tp_rank;
+  if (tp < 2 || s->tp_connected) {
+    set_error("sx_session_tp_connect: not a tensor-parallel session, or already connected");
+    return SX_E_INVALID;
+  }
+  const uint8_t* h = static_cast<const uint8_t*>(handles);
+  for (int q = 0; q < tp; q++) {
+    int32_t rs[2];
+    std::memcpy(rs, h + (size_t)q * SX_TP_HANDLE_BYTES + 80, 8);
+    if (rs[0] != q || rs[1] != tp) {
+      set_error("sx_session_tp_connect: handle " + std::to_string(q) + " is not rank " + std::to_string(q) +
+                " of " + std::to_string(tp));
+      return SX_E_INVALID;
+    }
+    for (int p = 0; p < q; p++)
+      if (!std::memcmp(h + (size_t)q * SX_TP_HANDLE_BYTES + 64, h + (size_t)p * SX_TP_HANDLE_BYTES + 64, 16)) {
+        // ranks that wait on one another must never share a GPU
+        set_error("sx_session_tp_connect: ranks " + std::to_string(p) + " and " + std::to_string(q) +
+                  " are on the same GPU");
+        return SX_E_INVALID;
+      }
+  }
+  SX_CU(cudaSetDevice(s->m->device));
+  const size_t flags_off = (size_t)2 * s->tp.xb_cap * 4;
+  for (int q = 0; q < tp; q++) {
+    if (q == me) continue;
+    cudaIpcMemHandle_t ih;
+    std::memcpy(&ih, h + (size_t)q * SX_TP_HANDLE_BYTES, sizeof(ih));
+    void* p = nullptr;
+    SX_CU(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess));
+    s->tp_opened.push_back(p);
+    s->tp.xb[q] = static_cast<float*>(p);
+    s->tp.flags[q] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p) + flags_off);
+  }
+  s->tp_connected = true;
+  return SX_OK;
+}
+
+int session_tp_disconnect(sx_session* s) {
+  if (!s) {
+    set_error("sx_session_tp_disconnect: null argument");
+    return SX_E_INVALID;
+  }
+  SX_CU(cudaSetDevice(s->m->device));
+  SX_CU(cudaStreamSynchronize(s->st));
+  for (void* p : s->tp_opened) SX_CU(cudaIpcCloseMemHandle(p));
+  s->tp_opened.clear();
+  for (int q = 0; q < kMaxTp; q++)
+    if (q != s->tp.rank) s->tp.xb[q] = nullptr, s->tp.flags[q] = nullptr;
+  s->tp_connected = false;
+  return SX_OK;
 }
 
 int session_reset(sx_session* s) {
@@ -416,10 +629,22 @@ int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
   return std::max(1, std::min(kMaxCluster, (s->max_ctx + 63) / 64));
 }
 
-// Every GEMV gets the session's Q8_0 partial-sum buffer.
+// Every GEMV gets the session's Q8_0 partial-sum buffer; residual adds of a tensor-parallel
+// model (wo, w2: input columns split over the ranks) also get the exchange communicator.
 int gemv(GemvArgs a, Epi epi, sx_session* s) {
   a.part = s->q8_part;
   a.part_cap = s->q8_part_cap;
+  if (epi == EPI_ADD && s->m->tp_size > 1) {
+    if (!s->tp_connected) {
+      set_error("tensor-parallel session: call sx_session_tp_connect before decoding");
+      return SX_E_INVALID;
+    }
+    if (a.w.dtype != SX_DTYPE_Q8_0) {
+      set_error("tensor parallelism needs Q8_0 weights");
+      return SX_E_UNSUPPORTED;
+    }
+    a.tp = s->tp;
+  }
   SX_CU(launch_gemv(a, epi, s->st));
   return SX_OK;
 }
@@ -522,6 +747,10 @@ int check_err(sx_session* s) {
     SX_CU(cudaStreamSynchronize(s->st));
     if (e == 2) {
       set_error("a kernel's bounded pipeline wait timed out (device error flag)");
+      return SX_E_DEVICE;
+    }
+    if (e == 3) {
+      set_error("a tensor-parallel peer did not reach the residual exchange within 5 s");
       return SX_E_DEVICE;
     }
     set_error("token id or codebook code out of range");

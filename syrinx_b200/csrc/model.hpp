@@ -20,6 +20,9 @@ struct sx_model {
   float* inv_fast = nullptr;
   std::vector<void*> allocs;
   size_t weight_bytes = 0;
+  // tensor parallelism: this model holds rank tp_rank's shard of tp_size; d holds the
+  // per-rank geometry (n_head, n_local_heads, intermediate_size divided by tp_size)
+  int tp_rank = 0, tp_size = 1;
 };
 
 struct GreedyGraph {
@@ -67,6 +70,13 @@ struct sx_session {
   unsigned long long* amax = nullptr;  // [max_batch]
   float* q8_part = nullptr;  // Q8_0 GEMV partial sums [tile][k-chunk][token][16]
   size_t q8_part_cap = 0;    // floats
+  // tensor parallelism: the exchange region (rows [2][xb_cap] | flags [kMaxTp][kMaxTpCtas])
+  // peers map through CUDA IPC, and the communicator the residual merges use
+  void* tp_region = nullptr;
+  size_t tp_region_bytes = 0;
+  bool tp_connected = false;
+  std::vector<void*> tp_opened;  // peers' regions opened on this device
+  sx::TpComm tp;
   std::vector<int> len;  // host mirror of per-sequence cache lengths
   bool device_len_dirty = false;  // device seq_len advanced by a graph loop
   std::vector<GreedyGraph> graphs;
@@ -74,7 +84,12 @@ struct sx_session {
 };
 
 namespace sx {
-int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out);
+int model_create(const sx_model_desc* desc, const void* blob, size_t size, int device, sx_model** out,
+                 int tp_rank = 0, int tp_size = 1);
+// tensor-parallel exchange setup (see sx_session_tp_handle / sx_session_tp_connect)
+int session_tp_handle(sx_session* s, void* out);
+int session_tp_connect(sx_session* s, const void* handles);
+int session_tp_disconnect(sx_session* s);
 void model_destroy(sx_model* m);
 int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_session** out);
 void session_destroy(sx_session* s);

@@ -77,6 +77,19 @@ enum Epi : int {
   EPI_ARGMAX = 3,  // logits (stored if y != null) + packed argmax over allowed rows
 };
 
+// Tensor parallelism: one process per GPU; the wo / w2 residual merges exchange per-rank
+// partial rows over NVLink (peer pointers from CUDA IPC) instead of an all-reduce call.
+constexpr int kMaxTp = 8;         // ranks in a tensor-parallel group
+constexpr int kMaxTpCtas = 1024;  // merge CTAs one exchange may use (flags per source rank)
+struct TpComm {
+  int rank = 0, size = 1;          // size 1: no tensor parallelism
+  float* xb[kMaxTp] = {};          // each rank's exchange rows [2][xb_cap] as mapped on this GPU
+  uint32_t* flags[kMaxTp] = {};    // each rank's flags [kMaxTp source ranks][kMaxTpCtas]
+  uint32_t* epochs = nullptr;      // this rank's per-CTA exchange counters
+  int* err = nullptr;              // this rank's device error flag (3: a peer did not arrive)
+  int xb_cap = 0;                  // floats per parity half of an exchange buffer
+};
+
 struct GemvArgs {
   DevMat w;
   const float* x = nullptr;  // [M][K] activations (row stride K)
@@ -96,6 +109,8 @@ struct GemvArgs {
   // Q8_0 only: per-(tile, k-chunk) partial sums, part_cap floats (q8_part_floats)
   float* part = nullptr;
   size_t part_cap = 0;
+  // residual add across a tensor-parallel group (EPI_ADD of a K-split matrix, Q8_0 only)
+  TpComm tp;
 };
 // floats of partial sums a Q8_0 GEMV over `w` with `n_rows` logical rows needs at M tokens
 size_t q8_part_floats(const DevMat& w, int64_t n_rows, int M);

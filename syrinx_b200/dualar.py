@@ -35,15 +35,25 @@ def synth_blob(cfg: ModelConfig, wtype: int = SX_DTYPE_Q8_0, seed: int = 0) -> n
     return buf
 
 
+TP_HANDLE_BYTES = 128  # SX_TP_HANDLE_BYTES
+
+
 class Model:
     """Weights resident on one GPU (replaces `S2Pro::load_with_dtype`, s2/mod.rs:119-167)."""
 
-    def __init__(self, cfg: ModelConfig, blob: np.ndarray, device: int = 0):
+    def __init__(self, cfg: ModelConfig, blob: np.ndarray, device: int = 0, tp_rank: int = 0, tp_size: int = 1):
+        """tp_size > 1: this process holds rank tp_rank's tensor-parallel shard (one process
+        per GPU; see syrinx_b200.tp)."""
         self.cfg = cfg
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         self._desc = cfg.to_c()
         self.handle = C.c_void_p()
-        _lib.check(_lib.lib().sx_model_create(C.byref(self._desc), blob.ctypes.data, blob.nbytes,
-                                              device, C.byref(self.handle)))
+        if tp_size == 1:
+            _lib.check(_lib.lib().sx_model_create(C.byref(self._desc), blob.ctypes.data, blob.nbytes,
+                                                  device, C.byref(self.handle)))
+        else:
+            _lib.check(_lib.lib().sx_model_create_tp(C.byref(self._desc), blob.ctypes.data, blob.nbytes,
+                                                     device, tp_rank, tp_size, C.byref(self.handle)))
 
     def weight_bytes(self) -> int:
         n = C.c_size_t()
@@ -83,6 +93,25 @@ class B200DualAr:
         self.handle = C.c_void_p()
         _lib.check(_lib.lib().sx_session_create_ex(model.handle, max_batch, max_ctx, kv_dtype,
                                                    C.byref(self.handle)))
+
+    # -- tensor parallelism ----------------------------------------------------------------
+    def tp_handle(self) -> bytes:
+        """This rank's exchange handle (SX_TP_HANDLE_BYTES bytes) for the other ranks."""
+        buf = (C.c_uint8 * TP_HANDLE_BYTES)()
+        _lib.check(_lib.lib().sx_session_tp_handle(self.handle, buf))
+        return bytes(buf)
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        """Map every rank's exchange region; `handles` in rank order, this rank's included."""
+        blob = b"".join(handles)
+        if len(blob) != TP_HANDLE_BYTES * len(handles):
+            raise ValueError("tensor-parallel handles must be SX_TP_HANDLE_BYTES each")
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _lib.check(_lib.lib().sx_session_tp_connect(self.handle, buf))
+
+    def tp_disconnect(self) -> None:
+        """Unmap the peers (every rank, before any rank closes its session)."""
+        _lib.check(_lib.lib().sx_session_tp_disconnect(self.handle))
 
     # -- DualArBackend ------------------------------------------------------------------
     def config(self) -> ModelConfig:

@@ -1,0 +1,85 @@
+"""Tensor-parallel decode on two GPUs (config 5 shape: Qwen3-4B, Q8_0, seed 3), one process
+per GPU, against the CPU oracle: step-0 logits within 2e-2 and 32 greedy frames
+token-identical on both ranks. The residual merges after wo and w2 exchange rows over NVLink
+inside the library; the ranks meet on the host only for the handle exchange (gloo).
+Skipped when fewer than two GPUs are visible."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import syrinx_b200 as sx
+from syrinx_b200 import tp
+from syrinx_b200.configs import SX_DTYPE_Q8_0
+from syrinx_b200.workloads import dual_ar_prompt
+from oracle import oracle as oc
+
+pytestmark = pytest.mark.gpu
+
+N_FRAMES = 32
+MAX_CTX = 192
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180))
+    try:
+        cfg = sx.QWEN3_4B
+        blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=3)
+        model = sx.Model(cfg, blob, device=rank, tp_rank=rank, tp_size=world)
+        be = sx.B200DualAr(model, max_ctx=MAX_CTX)
+        tp.connect(be, dist)
+        prompt = dual_ar_prompt(cfg, 64, 54, seed=3)
+        st = be.prefill(prompt)
+        frames = be.decode_greedy(N_FRAMES, mask_stop=True)
+        tp.close(be, model, dist)
+        q.put((rank, st.semantic_logits, frames, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp2_config5_matches_oracle():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=900) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+    for rank, _, _, err in out:
+        assert err is None, f"rank {rank}: {err}"
+    assert all(p.exitcode == 0 for p in procs)
+    (_, l0, f0, _), (_, l1, f1, _) = out
+    assert np.array_equal(l0, l1), "ranks disagree on the logits"
+    assert np.array_equal(f0, f1), "ranks disagree on the frames"
+
+    cfg = sx.QWEN3_4B
+    blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=3)
+    prompt = dual_ar_prompt(cfg, 64, 54, seed=3)
+    om = oc.OracleModel(cfg, blob)
+    os_ = oc.OracleSession(om, MAX_CTX, kv_bf16=False)
+    ol, _ = os_.prefill(prompt)
+    err0 = float(np.max(np.abs(l0.astype(np.float64) - ol)))
+    os_.reset()
+    ofr, margins = os_.drive_greedy(prompt, N_FRAMES, mask_stop=True)
+    print(f"tp2 config5 step-0 logits max-abs {err0:.3e}, min margin {margins.min():.3e}")
+    assert err0 <= 2e-2
+    bad = np.argwhere(f0 != ofr)
+    assert bad.size == 0, f"first mismatch frame {bad[0]}, semantic top-2 margin {margins[bad[0][0]]:.2e}"
