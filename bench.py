@@ -9,6 +9,7 @@ id masked so every step produces a frame. One step = one frame: semantic head + 
 every step streams them from HBM; no L2 flush is needed.
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+  torchrun --nproc-per-node N bench.py --tp N --steps 1024   (config 5, tensor parallel)
 
 Multi-GPU: one process per GPU (torchrun); utterances are independent, each rank decodes
 its own (weak scaling, no collective on the data path); timing is the max over ranks.
@@ -102,14 +103,16 @@ class Clocks:
 
 
 def kernels_per_frame(cfg) -> int:
-    """Kernel launches in one greedy frame graph (mirrors the sequence in model.cu)."""
-    per_layer = 5  # wqkv gemv, attention, wo gemv, w1|w3 gemv, w2 gemv
-    n = 1 + 1  # semantic head gemv, take_semantic
+    """Kernel launches in one greedy frame graph (mirrors the sequence in model.cu). A Q8_0
+    GEMV is two launches: k_gemv_q8 and its k_merge_q8."""
+    gemv = 2
+    per_layer = 4 * gemv + 1  # wqkv, wo, w1|w3, w2 + attention
+    n = gemv + 1  # semantic head, take_semantic
     if cfg.has_fast:
         C = cfg.num_codebooks
         n += C * cfg.fast.n_layer * per_layer  # fast steps 0..C-1
-        n += 1  # code-0 embedding
-        n += (C - 1) * 2  # fast head + take_code
+        n += 1  # code-0 embedding (take_code)
+        n += (C - 1) * (gemv + 1)  # fast head + take_code
     n += 1 + cfg.slow.n_layer * per_layer + 1  # embed, slow stack, advance
     return n
 
@@ -254,6 +257,96 @@ def bench_device(args):
         print(json.dumps(res), flush=True)
 
 
+TP_METRIC = "semantic frames/s per tensor-parallel group, config 5 (4B-shape Q8_0 dual-AR b1, KV grown to 8192)"
+
+
+def bench_tp(args):
+    """--tp N (config 5): one utterance decoded by a tensor-parallel group of N GPUs (one
+    process per GPU under torchrun). The cache is brought to args.tp_ctx - steps - warmup
+    positions: all but the last 64 hold seeded synthetic K/V (sx_session_fill_kv_synthetic;
+    a 7K-token prefill at 8 tokens per GEMV launch would stream every weight ~900 times),
+    the last 64 are a real prompt prefilled on top of them. Then `warmup` untimed and
+    `steps` timed greedy frames attend over the whole cache (which ends near args.tp_ctx).
+    value = frames/s of the group (strong scaling: the work per frame is fixed); the timing
+    is the max over ranks of the CUDA-event time of the timed frames."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import syrinx_b200 as sx
+    from syrinx_b200 import dp, tp
+    from syrinx_b200.configs import SX_DTYPE_Q8_0, frame_bytes
+    from syrinx_b200.workloads import dual_ar_prompt
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.tp:
+        raise SystemExit(f"--tp {args.tp} needs {args.tp} processes (torchrun --nproc-per-node {args.tp})")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    cfg = sx.QWEN3_4B
+    K, W = args.steps, args.warmup
+    T = args.tp_ctx - K - W
+    blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=3)
+    model = sx.Model(cfg, blob, device=local, tp_rank=rank, tp_size=world)
+    be = sx.B200DualAr(model, max_ctx=args.tp_ctx + 16)
+    stream = torch.cuda.Stream()
+    be.set_stream(stream.cuda_stream)
+    if world > 1:
+        tp.connect(be, dist)
+    tail = 64
+    prompt = dual_ar_prompt(cfg, tail, 54, seed=3)
+    t0 = time.time()
+    be.fill_kv_synthetic(T - tail, seed=3)
+    be.prefill(prompt)
+    t_prefill = time.time() - t0
+    be.decode_greedy(W, mask_stop=True)
+    ctx_start = be.seq_len()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            frames = be.decode_greedy(K, mask_stop=True)
+            end.record(stream)
+        torch.cuda.synchronize()
+    ms = dp.max_over_ranks(start.elapsed_time(end), dist if world > 1 else None, device="cuda")
+    assert frames.shape[0] == K, frames.shape
+    peak, peak_kind = peaks()
+    mean_ctx = ctx_start + (K - 1) / 2.0
+    fb = frame_bytes(cfg, SX_DTYPE_Q8_0, ctx=mean_ctx, semantic_head=True, kv_elem=4)
+    # per GPU: layers and KV split over the ranks; the heads are replicated
+    fast_out = (cfg.num_codebooks - 1) * cfg.codebook_size * cfg.fast.dim * 34 / 32
+    per_gpu = (fb["slow"] + fb["fast"] - fast_out + fb["kv"]) / world + fb["head"] + fast_out
+    value = K / (ms * 1e-3)
+    res = {
+        "metric": TP_METRIC, "value": round(value, 2), "unit": "frames/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q8_0 weights, f32 activations/accumulation, f32 KV",
+        "data": "synthetic (seed 3)",
+        "config": {"workload": f"config5 qwen3-4b-shaped dual-AR Q8_0 b1, tp{world}: {T - tail} synthetic KV "
+                               f"positions + {tail}-token prompt, {W}+{K} greedy frames, KV to {args.tp_ctx}",
+                   "ctx_mean": mean_ctx, "parallelism": f"tp{world}",
+                   "exchange": "residual rows after wo and w2 over NVLink in the merge kernel (no NCCL call)"},
+        "hbm_roofline": {"bytes_per_frame_per_gpu": per_gpu, "frac_of_peak": round(per_gpu * value / (peak * 1e9), 4),
+                         "peak_gbs": peak, "peak_kind": peak_kind,
+                         "note": "layers and KV divided over the ranks; semantic head and fast_output replicated"},
+        "gpu_launches": kernels_per_frame(cfg) * K, "clocks": clk.summary(), "prefill_s": round(t_prefill, 2),
+    }
+    if world > 1:
+        tp.close(be, model, dist)
+        dist.destroy_process_group()
+    else:
+        be.close()
+        model.close()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
 def cpu_baseline(cfg, blob, budget_s: float, frames: int | None = None) -> dict:
     """The oracle (CPU restatement of the reference path) decoding frames of the same
     workload on all host cores: a bounded sample (short prompt, a few frames)."""
@@ -314,10 +407,14 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--tp", type=int, default=0, help="config 5: tensor-parallel group of N GPUs")
+    ap.add_argument("--tp-ctx", type=int, default=8192)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.tp:
+        bench_tp(args)
+    elif args.impl == "reference":
         bench_reference(args)
     else:
         bench_device(args)

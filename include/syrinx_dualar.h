@@ -155,6 +155,11 @@ int sx_session_tp_connect(sx_session* s, const void* handles);
 /* Unmap the peers' regions (after the group's last decode call, before any rank destroys
  * its session: put a barrier between the two). */
 int sx_session_tp_disconnect(sx_session* s);
+/* Benchmark surface, no reference counterpart: give the empty sequence `seq` a slow-AR KV
+ * cache of `len` positions of seeded values in [-1, 1), as if `len` tokens had been
+ * prefilled. A following sx_prefill appends after them and decoding attends over all of
+ * them, so long-context decode can be timed without a long prefill. */
+int sx_session_fill_kv_synthetic(sx_session* s, int32_t seq, int32_t len, uint64_t seed);
 /* Clear every sequence (the reference `reset`, dualar.rs:73). */
 int sx_session_reset(sx_session* s);
 int sx_session_destroy(sx_session* s);

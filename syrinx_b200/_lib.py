@@ -34,6 +34,7 @@ SIGNATURES = {
     "sx_session_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sx_session_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sx_session_tp_disconnect": (C.c_int, [C.c_void_p]),
+    "sx_session_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_uint64]),
     "sx_session_reset": (C.c_int, [C.c_void_p]),
     "sx_session_destroy": (C.c_int, [C.c_void_p]),
     "sx_session_len": (C.c_int, [C.c_void_p, C.c_int32, _i32p]),

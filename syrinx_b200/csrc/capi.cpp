@@ -154,6 +154,10 @@ int sx_session_tp_disconnect(sx_session* s) {
   SX_GUARD({ return session_tp_disconnect(s); })
 }
 
+int sx_session_fill_kv_synthetic(sx_session* s, int32_t seq, int32_t len, uint64_t seed) {
+  SX_GUARD({ return fill_kv_synthetic(s, seq, len, seed); })
+}
+
 int sx_model_destroy(sx_model* model) {
   SX_GUARD({
     model_destroy(model);
@@ -249,7 +253,7 @@ int sx_prefill(sx_session* s, const uint32_t* prompt, int32_t T, float* logits_o
       set_error("null prompt");
       return SX_E_INVALID;
     }
-    if (s->len[0] != 0) {
+    if (s->len[0] != s->synthetic_len[0]) {
       set_error("prefill on a non-empty session (reset first)");
       return SX_E_STATE;
     }

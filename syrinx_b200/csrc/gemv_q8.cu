@@ -284,13 +284,17 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
 }
 
 // Residual add of a K-split (tensor-parallel) GEMV. Each rank adds up its own k-chunk
-// partials per row exactly as k_merge_q8 does and publishes those rows in its exchange
-// buffer; thread 0 then tells every peer (a release store into the peer's flag for this CTA,
-// over NVLink) and waits, bounded by %globaltimer, until every peer's flag for this CTA shows
-// the same exchange. The rows of all ranks are then added in rank order, so every rank
-// computes bit-identical residuals. Exchange e uses buffer half e % 2: a rank reaches
-// exchange e + 2 only after every peer has signalled e + 1, which each peer does only after
-// its kernel for exchange e (its reads of half e % 2) has completed.
+// partials per row exactly as k_merge_q8 does; the lane that owns a row then stores the
+// 8-byte word {row sum, exchange epoch} into that row's slot of every peer's receive region
+// (over NVLink), polls its own region until every peer's word for the row carries the same
+// epoch (bounded by %globaltimer), and adds all ranks' values in rank order, so every rank
+// computes bit-identical residuals. No fence, flag or barrier sits on the path: the value
+// and its tag arrive in one single-copy-atomic store. The epoch belongs to the slot (token,
+// row): only exchanges that carry the slot advance it, the same way on every rank, so an
+// old word can never show the epoch a receiver waits for. Exchange e of a slot uses parity
+// e % 2: a rank starts exchange e + 2 only after its exchange e + 1 kernel completed, which
+// needed every peer's e + 1 word, which each peer stores only after its exchange e kernel
+// (and with it every read of parity e % 2) completed.
 // After a timeout the session's error flag stays raised until the host reads it, and later
 // exchanges skip their wait, so a lost peer costs one bounded wait, not one per exchange.
 constexpr uint64_t kTpWaitNs = 5000000000ull;
@@ -299,8 +303,6 @@ template <int M>
 __global__ void __launch_bounds__(256) k_merge_q8_tp(const GemvArgs a, const Q8Geo g) {
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ uint32_t s_epoch;
-  __shared__ int s_ok;
   const TpComm& tp = a.tp;
   const int lane = threadIdx.x & 31, q4 = lane & 3;
   const long long u = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
@@ -321,38 +323,37 @@ __global__ void __launch_bounds__(256) k_merge_q8_tp(const GemvArgs a, const Q8G
                    __shfl_sync(0xffffffffu, s0, base + 3);
   const int pr = (g.t_first + vt) * 16 + r;
   const bool valid = live && q4 == 0 && m < a.M && pr >= a.row_base && pr < a.row_base + a.n_range;
-  if (threadIdx.x == 0) {
-    s_epoch = tp.epochs[blockIdx.x] + 1;
-    tp.epochs[blockIdx.x] = s_epoch;
-    s_ok = 1;
-  }
-  __syncthreads();
-  const uint32_t ep = s_epoch;
-  const size_t off = (size_t)(ep & 1) * tp.xb_cap + (size_t)m * a.ldy + pr;
-  if (valid) tp.xb[tp.rank][off] = t0;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < tp.size; p++)
-      if (p != tp.rank) st_release_sys(tp.flags[p] + (size_t)tp.rank * kMaxTpCtas + blockIdx.x, ep);
-    if (ld_cg(tp.err) != 0) s_ok = 0;
-    const uint64_t t_start = global_ns();
-    for (int p = 0; p < tp.size && s_ok; p++) {
-      if (p == tp.rank) continue;
-      const uint32_t* f = tp.flags[tp.rank] + (size_t)p * kMaxTpCtas + blockIdx.x;
-      while ((int)(ld_acquire_sys(f) - ep) < 0) {
-        if (global_ns() - t_start > kTpWaitNs) {
-          s_ok = 0;
-          atomicExch(tp.err, 3);
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (!s_ok || !valid) return;
+  if (!valid) return;
+  const size_t idx = (size_t)m * a.ldy + pr;
+  const uint32_t ep = ld_cg(tp.slot_epochs + idx) + 1;  // only this thread touches slot idx here
+  tp.slot_epochs[idx] = ep;
+  const size_t par = (size_t)(ep & 1) * kMaxTp;
+  const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(t0);
+  for (int p = 0; p < tp.size; p++)
+    if (p != tp.rank) st_relaxed_sys_u64(tp.rx[p] + (par + tp.rank) * tp.xb_cap + idx, word);
+  bool ok = ld_cg(tp.err) == 0;
   float tot = 0.f;
-  for (int q = 0; q < tp.size; q++) tot += q == tp.rank ? tp.xb[q][off] : ld_relaxed_sys(tp.xb[q] + off);
+  for (int q = 0; q < tp.size; q++) {
+    float v = t0;
+    if (q != tp.rank) {
+      const uint64_t* src = tp.rx[tp.rank] + (par + q) * tp.xb_cap + idx;
+      uint64_t w = ld_relaxed_sys_u64(src);
+      if (ok && (uint32_t)(w >> 32) != ep) {
+        const uint64_t t_start = global_ns();
+        do {
+          w = ld_relaxed_sys_u64(src);
+          if (global_ns() - t_start > kTpWaitNs) {
+            ok = false;
+            atomicExch(tp.err, 3);
+            break;
+          }
+        } while ((uint32_t)(w >> 32) != ep);
+      }
+      v = __uint_as_float((uint32_t)w);
+    }
+    tot += v;
+  }
+  if (!ok) return;
   float v = tot;
   if (a.bias) v = __fadd_rn(v, a.bias[pr]);
   float* dst = a.y + (size_t)m * a.ldy + pr;
@@ -406,7 +407,7 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
   if (e != cudaSuccess) return e;
   if (epi == EPI_ADD && a.tp.size > 1) {
     const long long blocks = ((long long)g.n_vt * 16 * M * 4 + 255) / 256;
-    if (blocks > kMaxTpCtas || a.n_extra != 0 || (long long)M * a.ldy > a.tp.xb_cap) return cudaErrorInvalidValue;
+    if (a.n_extra != 0 || (long long)M * a.ldy > a.tp.xb_cap) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr2[1];
     cudaLaunchConfig_t cfg2 = launch_cfg(dim3((unsigned)blocks), dim3(256), 0, st, attr2);
     return cudaLaunchKernelEx(&cfg2, k_merge_q8_tp<M>, a, g);

@@ -417,6 +417,7 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
   s->kv_f32 = kv_dtype == SX_DTYPE_F32;
   s->kv_elem = s->kv_f32 ? 4 : 2;
   s->len.assign(max_batch, 0);
+  s->synthetic_len.assign(max_batch, 0);
   auto fail = [&](int r) {
     session_destroy(s);
     return r;
@@ -494,23 +495,22 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
     if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
   }
   if (m->tp_size > 1) {
-    // exchange region: rows [2][xb_cap] | flags [kMaxTp][kMaxTpCtas]; peers map it by IPC
+    // receive region rx [2][kMaxTp][xb_cap] 8-byte words; peers map it by IPC
     const int xb_cap = kMaxTok * dim;
-    s->tp_region_bytes = (size_t)2 * xb_cap * 4 + (size_t)kMaxTp * kMaxTpCtas * 4;
+    s->tp_region_bytes = (size_t)2 * kMaxTp * xb_cap * 8;
     uint8_t* region = nullptr;
     uint32_t* epochs = nullptr;
-    if ((rc = dalloc(s->allocs, &region, s->tp_region_bytes)) || (rc = dalloc(s->allocs, &epochs, kMaxTpCtas)))
+    if ((rc = dalloc(s->allocs, &region, s->tp_region_bytes)) || (rc = dalloc(s->allocs, &epochs, (size_t)xb_cap)))
       return fail(rc);
     if (cudaMemset(region, 0, s->tp_region_bytes) != cudaSuccess ||
-        cudaMemset(epochs, 0, (size_t)kMaxTpCtas * 4) != cudaSuccess)
+        cudaMemset(epochs, 0, (size_t)xb_cap * 4) != cudaSuccess)
       return fail(SX_E_CUDA);
     s->tp_region = region;
     s->tp.rank = m->tp_rank;
     s->tp.size = m->tp_size;
     s->tp.xb_cap = xb_cap;
-    s->tp.xb[m->tp_rank] = reinterpret_cast<float*>(region);
-    s->tp.flags[m->tp_rank] = reinterpret_cast<uint32_t*>(region + (size_t)2 * xb_cap * 4);
-    s->tp.epochs = epochs;
+    s->tp.rx[m->tp_rank] = reinterpret_cast<uint64_t*>(region);
+    s->tp.slot_epochs = epochs;
     s->tp.err = s->err;
   }
   if (cudaMemset(s->amax, 0, (size_t)max_batch * 8) != cudaSuccess ||
@@ -585,7 +585,6 @@ int session_tp_connect(sx_session* s, const void* handles) {
       }
   }
   SX_CU(cudaSetDevice(s->m->device));
-  const size_t flags_off = (size_t)2 * s->tp.xb_cap * 4;
   for (int q = 0; q < tp; q++) {
     if (q == me) continue;
     cudaIpcMemHandle_t ih;
@@ -593,8 +592,7 @@ int session_tp_connect(sx_session* s, const void* handles) {
     void* p = nullptr;
     SX_CU(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess));
     s->tp_opened.push_back(p);
-    s->tp.xb[q] = static_cast<float*>(p);
-    s->tp.flags[q] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p) + flags_off);
+    s->tp.rx[q] = static_cast<uint64_t*>(p);
   }
   s->tp_connected = true;
   return SX_OK;
@@ -610,13 +608,14 @@ int session_tp_disconnect(sx_session* s) {
   for (void* p : s->tp_opened) SX_CU(cudaIpcCloseMemHandle(p));
   s->tp_opened.clear();
   for (int q = 0; q < kMaxTp; q++)
-    if (q != s->tp.rank) s->tp.xb[q] = nullptr, s->tp.flags[q] = nullptr;
+    if (q != s->tp.rank) s->tp.rx[q] = nullptr;
   s->tp_connected = false;
   return SX_OK;
 }
 
 int session_reset(sx_session* s) {
   std::fill(s->len.begin(), s->len.end(), 0);
+  std::fill(s->synthetic_len.begin(), s->synthetic_len.end(), 0);
   return SX_OK;
 }
 
@@ -776,6 +775,62 @@ EmbedArgs embed_args(sx_session* s) {
 }
 
 }  // namespace
+
+namespace {
+// Seeded pseudo-random K/V values in [-1, 1) for positions [0, len) of one sequence, every
+// slow layer (SplitMix64 of seed and the element's coordinates).
+__global__ void k_fill_kv(uint8_t* kv, size_t layer_elems, int n_layer, int first_page, int Hkv, int hd, int len,
+                          int kv_f32, uint64_t seed) {
+  const size_t half = layer_elems / 2;
+  const size_t per_layer = (size_t)2 * len * Hkv * hd;
+  const size_t total = per_layer * n_layer;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    size_t r = i;
+    const int d = (int)(r % hd);
+    r /= hd;
+    const int h = (int)(r % Hkv);
+    r /= Hkv;
+    const int pos = (int)(r % len);
+    r /= len;
+    const int which = (int)(r % 2);
+    const int l = (int)(r / 2);
+    uint64_t z = seed + 0x9E3779B97F4A7C15ull * (i + 1);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const float v = (float)(z >> 40) * (1.0f / 8388608.0f) - 1.0f;
+    const size_t page = (size_t)first_page + pos / kPage;
+    const size_t e = (size_t)l * layer_elems + which * half + ((page * Hkv + h) * kPage + pos % kPage) * hd + d;
+    if (kv_f32)
+      reinterpret_cast<float*>(kv)[e] = v;
+    else
+      reinterpret_cast<__nv_bfloat16*>(kv)[e] = __float2bfloat16(v);
+  }
+}
+}  // namespace
+
+// Benchmark surface: sequence `seq` (empty) gets a slow-AR KV cache of `len` positions of
+// seeded values, as if that many tokens had been prefilled; a following prefill appends to
+// it and decoding attends over all of it.
+int fill_kv_synthetic(sx_session* s, int seq, int len, uint64_t seed) {
+  if (!s || seq < 0 || seq >= s->max_batch || len < 1 || len > s->max_ctx) {
+    set_error("sx_session_fill_kv_synthetic: bad sequence or length");
+    return SX_E_INVALID;
+  }
+  if (s->len[seq] != 0) {
+    set_error("sx_session_fill_kv_synthetic: the sequence is not empty");
+    return SX_E_STATE;
+  }
+  const auto& sl = s->m->d.slow;
+  (void)cudaGetLastError();
+  k_fill_kv<<<1184, 256, 0, s->st>>>(s->kv, s->kv_layer_elems, sl.n_layer, seq * s->pages_per_seq, sl.n_local_heads,
+                                     sl.head_dim, len, s->kv_f32, seed);
+  SX_CU(cudaGetLastError());
+  SX_CU(cudaStreamSynchronize(s->st));
+  s->len[seq] = len;
+  s->synthetic_len[seq] = len;
+  return SX_OK;
+}
 
 int prefill_seq(sx_session* s, int seq, const uint32_t* prompt, int T) {
   const sx_model_desc& d = s->m->d;

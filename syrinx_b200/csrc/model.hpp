@@ -70,14 +70,15 @@ struct sx_session {
   unsigned long long* amax = nullptr;  // [max_batch]
   float* q8_part = nullptr;  // Q8_0 GEMV partial sums [tile][k-chunk][token][16]
   size_t q8_part_cap = 0;    // floats
-  // tensor parallelism: the exchange region (rows [2][xb_cap] | flags [kMaxTp][kMaxTpCtas])
-  // peers map through CUDA IPC, and the communicator the residual merges use
+  // tensor parallelism: the receive region (rx [2][kMaxTp][xb_cap] 8-byte words) peers map
+  // through CUDA IPC, and the communicator the residual merges use
   void* tp_region = nullptr;
   size_t tp_region_bytes = 0;
   bool tp_connected = false;
   std::vector<void*> tp_opened;  // peers' regions opened on this device
   sx::TpComm tp;
   std::vector<int> len;  // host mirror of per-sequence cache lengths
+  std::vector<int> synthetic_len;  // positions filled by fill_kv_synthetic (a prefill may follow)
   bool device_len_dirty = false;  // device seq_len advanced by a graph loop
   std::vector<GreedyGraph> graphs;
   std::vector<void*> allocs;
@@ -90,6 +91,7 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
 int session_tp_handle(sx_session* s, void* out);
 int session_tp_connect(sx_session* s, const void* handles);
 int session_tp_disconnect(sx_session* s);
+int fill_kv_synthetic(sx_session* s, int seq, int len, uint64_t seed);
 void model_destroy(sx_model* m);
 int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_session** out);
 void session_destroy(sx_session* s);

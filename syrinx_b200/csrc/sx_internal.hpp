@@ -79,15 +79,17 @@ enum Epi : int {
 
 // Tensor parallelism: one process per GPU; the wo / w2 residual merges exchange per-rank
 // partial rows over NVLink (peer pointers from CUDA IPC) instead of an all-reduce call.
-constexpr int kMaxTp = 8;         // ranks in a tensor-parallel group
-constexpr int kMaxTpCtas = 1024;  // merge CTAs one exchange may use (flags per source rank)
+// Every rank owns a receive region rx[2 parities][kMaxTp source ranks][xb_cap] of 8-byte
+// words {f32 value | u32 exchange epoch << 32}; senders store straight into the peers'
+// regions, receivers poll their own words until the epoch matches. The epoch of a slot
+// (token m, row) counts the exchanges that carried that slot, identically on every rank.
+constexpr int kMaxTp = 8;  // ranks in a tensor-parallel group
 struct TpComm {
-  int rank = 0, size = 1;          // size 1: no tensor parallelism
-  float* xb[kMaxTp] = {};          // each rank's exchange rows [2][xb_cap] as mapped on this GPU
-  uint32_t* flags[kMaxTp] = {};    // each rank's flags [kMaxTp source ranks][kMaxTpCtas]
-  uint32_t* epochs = nullptr;      // this rank's per-CTA exchange counters
-  int* err = nullptr;              // this rank's device error flag (3: a peer did not arrive)
-  int xb_cap = 0;                  // floats per parity half of an exchange buffer
+  int rank = 0, size = 1;             // size 1: no tensor parallelism
+  uint64_t* rx[kMaxTp] = {};          // each rank's receive region as mapped on this GPU
+  uint32_t* slot_epochs = nullptr;    // this rank's per-slot exchange counters [xb_cap]
+  int* err = nullptr;                 // this rank's device error flag (3: a peer did not arrive)
+  int xb_cap = 0;                     // slots (tokens x rows) per (parity, source rank)
 };
 
 struct GemvArgs {

@@ -109,6 +109,11 @@ class B200DualAr:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         _lib.check(_lib.lib().sx_session_tp_connect(self.handle, buf))
 
+    def fill_kv_synthetic(self, length: int, seed: int, seq: int = 0) -> None:
+        """Benchmark surface: an empty sequence gets `length` positions of seeded KV values
+        (as if prefilled); a later prefill appends after them."""
+        _lib.check(_lib.lib().sx_session_fill_kv_synthetic(self.handle, seq, length, seed))
+
     def tp_disconnect(self) -> None:
         """Unmap the peers (every rank, before any rank closes its session)."""
         _lib.check(_lib.lib().sx_session_tp_disconnect(self.handle))
