@@ -225,3 +225,20 @@ def test_profile_gemv_runs(tiny):
     for kind in range(4):
         be.profile_gemv(kind, 3)
     be.close()
+
+
+def test_long_context_token_identical(tiny):
+    """A 1200-token prompt in a 2100-position session (attention keys split over an 8-CTA
+    cluster of ~150 keys each), then 16 greedy frames against the oracle."""
+    cfg, model, om = tiny
+    prompt = prompt_for(cfg, 1200, seed=5)
+    be = sx.B200DualAr(model, max_ctx=2100)
+    st = be.prefill(prompt)
+    frames = be.decode_greedy(16, mask_stop=True)
+    os_ = oc.OracleSession(om, 2100, kv_bf16=False)
+    ol, _ = os_.prefill(prompt)
+    assert maxabs(st.semantic_logits, ol) <= LOGIT_TOL
+    os_.reset()
+    ofr, margins = os_.drive_greedy(prompt, 16, mask_stop=True)
+    assert np.array_equal(frames, ofr), f"first mismatch at {np.argwhere(frames != ofr)[:1]}, margins {margins[:8]}"
+    be.close()
