@@ -353,6 +353,8 @@ def cpu_baseline(cfg, blob, budget_s: float, frames: int | None = None) -> dict:
     from oracle import oracle as oc
     from syrinx_b200.workloads import dual_ar_prompt
 
+    # all host cores, whatever OMP_NUM_THREADS a launcher (torchrun sets 1) left behind
+    oc.set_num_threads(len(os.sched_getaffinity(0)))
     om = oc.OracleModel(cfg, blob)
     sess = oc.OracleSession(om, max_ctx=256, kv_bf16=False)
     prompt = dual_ar_prompt(cfg, 16, 13, seed=SEED)

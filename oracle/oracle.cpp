@@ -796,6 +796,9 @@ extern "C" {
 
 const char* oc_last_error(void) { return g_err.c_str(); }
 int oc_num_threads(void) { return omp_get_max_threads(); }
+void oc_set_num_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
 
 void oc_set_qmode(int32_t mode) { g_qmode = mode ? 1 : 0; }
 int32_t oc_get_qmode(void) { return g_qmode; }

@@ -37,6 +37,8 @@ typedef struct oc_session oc_session;
 
 const char* oc_last_error(void);
 int oc_num_threads(void);
+/* OpenMP threads of later calls (a launcher may have set OMP_NUM_THREADS=1). */
+void oc_set_num_threads(int n);
 /* Quantized matmul numerics for Q8_0 weights: 0 = mode A (default), 1 = mode B. */
 void oc_set_qmode(int32_t mode);
 int32_t oc_get_qmode(void);

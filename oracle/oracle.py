@@ -30,6 +30,7 @@ def lib() -> C.CDLL:
         sig = {
             "oc_last_error": (C.c_char_p, []),
             "oc_num_threads": (C.c_int, []),
+            "oc_set_num_threads": (None, [C.c_int]),
             "oc_set_qmode": (None, [C.c_int32]),
             "oc_get_qmode": (C.c_int32, []),
             "oc_linear_q8_0": (None, [_f32p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, _f32p]),
@@ -250,6 +251,10 @@ class OracleSession:
 
 def num_threads() -> int:
     return int(lib().oc_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    lib().oc_set_num_threads(int(n))
 
 
 def set_qmode(mode: int) -> None:
