@@ -239,6 +239,17 @@ void sx_sampling_params_default(sx_sampling_params* p);
 int sx_drive(sx_session* s, const uint32_t* prompt, int32_t T, int32_t max_frames, uint64_t seed,
              const sx_sampling_params* params, uint32_t* codes_out, int32_t* n_frames_out);
 
+/* The sampled frame loop kept on the device (the reference `drive` with `Sampler`,
+ * dualar.rs:188-219, sampling.rs:132-268), for sequence 0 after sx_prefill: per frame the
+ * semantic draw (constraint, top-p / top-k, temperature, RAS with its second draw), the
+ * residual-code draws and the slow step run in one CUDA graph with no host round trip. The
+ * SplitMix64 stream seeded `seed` is consumed in the reference order, so the draws equal
+ * sx_drive's for the same prompt, seed and parameters (up to an f64 exp ulp landing on a
+ * comparison). frames_out is [n_frames][1 + C] (semantic id, codes); *n_frames_out counts
+ * the frames before a stop id was drawn. ras_win_size must be <= 64. */
+int sx_decode_sample(sx_session* s, int32_t n_frames, uint64_t seed, const sx_sampling_params* params,
+                     uint32_t* frames_out, int32_t* n_frames_out);
+
 /* ---- batched path (DualArBackend::*_batch, dualar.rs:105-135; drive_batch 246-364) ---- *
  * Sequences keep their own lengths in the paged cache, so no left padding is needed:
  * sample i's real positions are 0..T_i exactly as in a batch-1 run. */

@@ -49,6 +49,7 @@ SIGNATURES = {
     "sx_decode_greedy": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, _u32p, _i32p]),
     "sx_sampling_params_default": (None, [C.POINTER(SxSamplingParams)]),
     "sx_drive": (C.c_int, [C.c_void_p, _u32p, C.c_int32, C.c_int32, C.c_uint64, C.POINTER(SxSamplingParams), _u32p, _i32p]),
+    "sx_decode_sample": (C.c_int, [C.c_void_p, C.c_int32, C.c_uint64, C.POINTER(SxSamplingParams), _u32p, _i32p]),
     "sx_prefill_batch": (C.c_int, [C.c_void_p, _u32p, _i32p, C.c_int32, _f32p, _f32p]),
     "sx_slow_step_batch": (C.c_int, [C.c_void_p, _u32p, _u8p, C.c_int32, _f32p, _f32p]),
     "sx_fast_expand_batch_greedy": (C.c_int, [C.c_void_p, _u32p, _u8p, C.c_int32, _u32p]),

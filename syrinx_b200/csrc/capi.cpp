@@ -154,6 +154,15 @@ int sx_session_tp_disconnect(sx_session* s) {
   SX_GUARD({ return session_tp_disconnect(s); })
 }
 
+int sx_decode_sample(sx_session* s, int32_t n_frames, uint64_t seed, const sx_sampling_params* params,
+                     uint32_t* frames_out, int32_t* n_frames_out) {
+  SX_GUARD({
+    int rc = need_session(s);
+    if (rc) return rc;
+    return decode_sample(s, n_frames, seed, params, frames_out, n_frames_out);
+  })
+}
+
 int sx_session_fill_kv_synthetic(sx_session* s, int32_t seq, int32_t len, uint64_t seed) {
   SX_GUARD({ return fill_kv_synthetic(s, seq, len, seed); })
 }

@@ -475,7 +475,8 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
       (rc = dalloc(s->allocs, &s->logits, (size_t)max_batch * d.vocab_size)) ||
       (rc = dalloc(s->allocs, &s->fast_logits, (size_t)max_batch * std::max(1, d.codebook_size))) ||
       (rc = dalloc(s->allocs, &s->hidden, (size_t)max_batch * dim)) ||
-      (rc = dalloc(s->allocs, &s->amax, (size_t)max_batch)))
+      (rc = dalloc(s->allocs, &s->amax, (size_t)max_batch)) || (rc = dalloc(s->allocs, &s->sstate, 1)) ||
+      (rc = dalloc(s->allocs, &s->dparams, 1)))
     return fail(rc);
   {
     // partial sums of the largest Q8_0 GEMV at the most tokens one launch takes
@@ -986,7 +987,24 @@ int fast_head(sx_session* s, int n, Epi epi) {
 
 }  // namespace
 
-int fast_expand_rows(sx_session* s, int n, const int* /*seqs*/) {
+namespace {
+// Draw arguments of the device sampler over rows [0, R) of the fast head's logits.
+SampleArgs codebook_sample_args(sx_session* s) {
+  const sx_model_desc& d = s->m->d;
+  SampleArgs a;
+  a.logits = s->fast_logits;
+  a.ranges = 1;
+  a.lo[0] = 0;
+  a.hi[0] = (uint32_t)d.codebook_size;
+  a.params = s->dparams;
+  a.full_last = (uint32_t)d.codebook_size - 1;
+  a.st = s->sstate;
+  a.amax = s->amax;
+  return a;
+}
+}  // namespace
+
+int fast_expand_rows(sx_session* s, int n, const int* /*seqs*/, bool sampled) {
   sx_model* m = s->m;
   const int C = m->d.num_codebooks;
   SX_RC(run_stack(s, true, n, s->fx, s->tok_seq, nullptr, 0, true));
@@ -997,7 +1015,12 @@ int fast_expand_rows(sx_session* s, int n, const int* /*seqs*/) {
   SX_CU(launch_take_code(f, s->st));
   for (int cb = 1; cb < C; cb++) {
     SX_RC(run_stack(s, true, n, s->fx, s->tok_seq, nullptr, cb, true));
-    SX_RC(fast_head(s, n, EPI_ARGMAX));
+    if (sampled) {
+      SX_RC(fast_head(s, n, EPI_STORE));
+      SX_CU(launch_sample(codebook_sample_args(s), s->st));
+    } else {
+      SX_RC(fast_head(s, n, EPI_ARGMAX));
+    }
     FrameArgs t = frame_args(s, n);
     t.amax = s->amax;
     t.slot = 1 + cb;
@@ -1057,11 +1080,67 @@ int fast_expand_sampled(sx_session* s, uint32_t first_code, sx_sample_fn fn, voi
 
 namespace {
 
-// head -> semantic -> (fast AR) for rows [0, n): leaves the frame in s->frames
-int greedy_frame_front(sx_session* s, int n, int mask_stop) {
+// The semantic constraint's allowed ids (sampling.rs:84-106) as ascending disjoint ranges:
+// the semantic range [begin, end] and the stop ids.
+bool semantic_sample_args(sx_session* s, SampleArgs* a) {
+  const sx_model_desc& d = s->m->d;
+  const uint32_t sem_hi = std::min<uint32_t>(d.semantic_end_id, (uint32_t)d.vocab_size - 1);
+  const uint32_t s0 = d.semantic_begin_id, s1 = sem_hi + 1;
+  const uint32_t t0 = d.stop_token_id, t1 = d.stop_token_id + (uint32_t)d.num_stop_tokens;
+  a->logits = s->logits;
+  a->ranges = 1;
+  a->lo[0] = s0;
+  a->hi[0] = s1;
+  if (t1 > t0 && !(t0 >= s0 && t1 <= s1)) {
+    if (t1 <= s0) {
+      a->ranges = 2, a->lo[0] = t0, a->hi[0] = t1, a->lo[1] = s0, a->hi[1] = s1;
+    } else if (t0 >= s1 && t1 <= (uint32_t)d.vocab_size) {
+      a->ranges = 2, a->lo[1] = t0, a->hi[1] = t1;
+    } else {
+      return false;  // stop ids straddle the semantic range
+    }
+  }
+  a->params = s->dparams;
+  a->semantic = 1;
+  a->sem_lo = s0;
+  a->sem_hi = sem_hi;
+  a->stop_lo = t0;
+  a->stop_hi = t1;
+  a->full_last = (uint32_t)d.vocab_size - 1;
+  a->st = s->sstate;
+  a->amax = s->amax;
+  return true;
+}
+
+// head -> semantic -> (fast AR) for rows [0, n): leaves the frame in s->frames. Sampled
+// (one sequence): the head stores the allowed rows' logits and the device sampler draws.
+int greedy_frame_front(sx_session* s, int n, int mask_stop, bool sampled) {
   sx_model* m = s->m;
   const sx_model_desc& d = m->d;
-  SX_RC(run_head(s, n, false, true, mask_stop != 0));
+  if (sampled) {
+    SampleArgs sa;
+    if (!semantic_sample_args(s, &sa)) {
+      set_error("decode_sample: stop ids straddle the semantic range");
+      return SX_E_UNSUPPORTED;
+    }
+    GemvArgs g;
+    g.w = m->out_w;
+    g.x = s->h;
+    g.norm_w = m->norm;
+    g.eps = d.slow.norm_eps;
+    g.bias = m->out_b;
+    g.M = 1;
+    g.y = s->logits;
+    g.ldy = d.vocab_size;
+    g.row_base = (int)sa.sem_lo;
+    g.n_range = (int)(sa.sem_hi - sa.sem_lo + 1);
+    for (uint32_t id = sa.stop_lo; id < sa.stop_hi; id++)
+      if (id < sa.sem_lo || id > sa.sem_hi) g.extra[g.n_extra++] = (int)id;
+    SX_RC(gemv(g, EPI_STORE, s));
+    SX_CU(launch_sample(sa, s->st));
+  } else {
+    SX_RC(run_head(s, n, false, true, mask_stop != 0));
+  }
   FrameArgs f = frame_args(s, n);
   f.amax = s->amax;
   f.slot = 0;
@@ -1076,16 +1155,16 @@ int greedy_frame_front(sx_session* s, int n, int mask_stop) {
     f.eps = d.slow.norm_eps;
   }
   SX_CU(launch_take_semantic(f, s->st));
-  if (d.fast.n_layer > 0) SX_RC(fast_expand_rows(s, n, nullptr));
+  if (d.fast.n_layer > 0) SX_RC(fast_expand_rows(s, n, nullptr, sampled));
   return SX_OK;
 }
 
-int build_graph(sx_session* s, int n, int mask_stop, cudaGraphExec_t* exec) {
+int build_graph(sx_session* s, int n, int mask_stop, bool sampled, cudaGraphExec_t* exec) {
   const sx_model_desc& d = s->m->d;
   const int width = 1 + d.num_codebooks;
   SX_CU(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
   auto body = [&]() -> int {
-    SX_RC(greedy_frame_front(s, n, mask_stop));
+    SX_RC(greedy_frame_front(s, n, mask_stop, sampled));
     EmbedArgs e = embed_args(s);
     e.tok_seq = s->tok_seq;
     e.frames = s->frames;
@@ -1131,7 +1210,31 @@ int build_graph(sx_session* s, int n, int mask_stop, cudaGraphExec_t* exec) {
 
 }  // namespace
 
+namespace {
+int run_frames(sx_session* s, int n, int n_frames, int mask_stop, bool sampled, uint32_t* frames_out,
+               int* n_frames_out);
+}  // namespace
+
 int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* frames_out, int* n_frames_out) {
+  return run_frames(s, n, n_frames, mask_stop, false, frames_out, n_frames_out);
+}
+
+int decode_sample(sx_session* s, int n_frames, uint64_t seed, const sx_sampling_params* p, uint32_t* frames_out,
+                  int* n_frames_out) {
+  if (!p || p->ras_win_size > kMaxRasWin) {
+    set_error("decode_sample: null parameters or ras_win_size above 64");
+    return SX_E_INVALID;
+  }
+  SampleState st{};
+  st.rng = seed;
+  SX_CU(cudaMemcpyAsync(s->sstate, &st, sizeof(st), cudaMemcpyHostToDevice, s->st));
+  SX_CU(cudaMemcpyAsync(s->dparams, p, sizeof(*p), cudaMemcpyHostToDevice, s->st));
+  return run_frames(s, 1, n_frames, 0, true, frames_out, n_frames_out);
+}
+
+namespace {
+int run_frames(sx_session* s, int n, int n_frames, int mask_stop, bool sampled, uint32_t* frames_out,
+               int* n_frames_out) {
   const sx_model_desc& d = s->m->d;
   const int width = 1 + d.num_codebooks;
   if (n < 1 || n > s->max_batch || n_frames < 0) {
@@ -1160,12 +1263,13 @@ int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* f
   SX_CU(cudaMemcpyAsync(s->frame_count, zeros.data(), n * 4, cudaMemcpyHostToDevice, s->st));
   GreedyGraph* gg = nullptr;
   for (auto& g : s->graphs)
-    if (g.M == n && g.mask_stop == mask_stop) gg = &g;
+    if (g.M == n && g.mask_stop == mask_stop && g.sampled == (int)sampled) gg = &g;
   if (!gg) {
     GreedyGraph g;
     g.M = n;
     g.mask_stop = mask_stop;
-    SX_RC(build_graph(s, n, mask_stop, &g.exec));
+    g.sampled = sampled;
+    SX_RC(build_graph(s, n, mask_stop, sampled, &g.exec));
     s->graphs.push_back(g);
     gg = &s->graphs.back();
   }
@@ -1189,6 +1293,7 @@ int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* f
   }
   return check_err(s);
 }
+}  // namespace
 
 int profile_gemv(sx_session* s, int kind, int n_launches) {
   sx_model* m = s->m;
@@ -1252,7 +1357,7 @@ int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, ui
     const std::vector<int> ts{0}, tp{s->len[0]};
     SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
   }
-  SX_RC(greedy_frame_front(s, 1, mask_stop));
+  SX_RC(greedy_frame_front(s, 1, mask_stop, false));
   SX_CU(cudaMemcpyAsync(frame_out, s->frames, (size_t)width * 4, cudaMemcpyDeviceToHost, s->st));
   SX_CU(cudaStreamSynchronize(s->st));
   if (stopped)

@@ -29,6 +29,7 @@ struct GreedyGraph {
   cudaGraphExec_t exec = nullptr;
   int M = 0;
   int mask_stop = 0;
+  int sampled = 0;  // 1: the device-sampled frame (sx_decode_sample)
 };
 
 struct sx_session {
@@ -68,6 +69,8 @@ struct sx_session {
   float* fast_logits = nullptr;  // [max_batch][R]
   float* hidden = nullptr;       // [max_batch][dim]
   unsigned long long* amax = nullptr;  // [max_batch]
+  sx::SampleState* sstate = nullptr;    // device sampler state of sequence 0
+  sx_sampling_params* dparams = nullptr;  // device copy of the sampling parameters
   float* q8_part = nullptr;  // Q8_0 GEMV partial sums [tile][k-chunk][token][16]
   size_t q8_part_cap = 0;    // floats
   // tensor parallelism: the receive region (rx [2][kMaxTp][xb_cap] 8-byte words) peers map
@@ -92,6 +95,9 @@ int session_tp_handle(sx_session* s, void* out);
 int session_tp_connect(sx_session* s, const void* handles);
 int session_tp_disconnect(sx_session* s);
 int fill_kv_synthetic(sx_session* s, int seq, int len, uint64_t seed);
+// device-sampled frames of sequence 0 (after prefill): the reference drive loop's draws
+int decode_sample(sx_session* s, int n_frames, uint64_t seed, const sx_sampling_params* p, uint32_t* frames_out,
+                  int* n_frames_out);
 void model_destroy(sx_model* m);
 int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_session** out);
 void session_destroy(sx_session* s);
@@ -108,7 +114,7 @@ int run_head(sx_session* s, int n, bool want_logits, bool want_argmax, bool mask
 // fast-AR prefix hidden of rows [0, n) into s->hidden
 int make_hidden(sx_session* s, int n);
 // greedy fast AR for rows [0, n) with first codes already in frames[seq][1]
-int fast_expand_rows(sx_session* s, int n, const int* seqs);
+int fast_expand_rows(sx_session* s, int n, const int* seqs, bool sampled = false);
 int fast_expand_sampled(sx_session* s, uint32_t first_code, sx_sample_fn fn, void* user,
                         uint32_t* codes_out);
 int profile_gemv(sx_session* s, int kind, int n_launches);

@@ -216,6 +216,28 @@ cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, f
 // sx_dequantize through static device scratch (noalloc.cu): returns an SX_* status
 int dequantize_noalloc(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device);
 
+// device sampler (sample_dev.cu): the reference Sampler for one sequence, one CTA per draw
+constexpr int kSampleMaxIds = 8192;  // allowed ids per draw
+constexpr int kMaxRasWin = 64;       // longest RAS window the device keeps
+struct SampleState {                 // per sequence, in device memory
+  unsigned long long rng;            // SplitMix64 state
+  int win_count;                     // semantic ids pushed so far
+  uint32_t win[kMaxRasWin];          // ring of the last ras_win_size of them
+};
+struct SampleArgs {
+  const float* logits = nullptr;          // indexed by vocabulary id (allowed rows written)
+  int ranges = 1;                         // allowed ids [lo[j], hi[j]), ascending, disjoint
+  uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
+  const sx_sampling_params* params = nullptr;  // device copy
+  int semantic = 0;                       // 1: sample_semantic (normal + RAS high draw)
+  uint32_t sem_lo = 0, sem_hi = 0;        // is_semantic: [sem_lo, sem_hi]
+  uint32_t stop_lo = 0, stop_hi = 0;      // stop ids: [stop_lo, stop_hi) (not pushed to the window)
+  uint32_t full_last = 0;                 // last id of the reference's full logits array
+  SampleState* st = nullptr;
+  unsigned long long* amax = nullptr;     // out: packed key of the drawn id
+};
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st);
+
 // host helpers
 void set_error(const std::string& msg);
 // Programmatic dependent launch is on unless SYRINX_PDL=0 (plain stream ordering).

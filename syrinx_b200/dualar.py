@@ -218,6 +218,16 @@ class B200DualAr:
                                                C.byref(n)))
         return out[: n.value]
 
+    def decode_sample(self, n_frames: int, seed: int, sampling: "SamplingParams") -> np.ndarray:
+        """Device-sampled frames of sequence 0 after prefill ([frames, 1 + C]); the same draws
+        as the reference drive loop with Sampler(seed, sampling)."""
+        out = np.zeros((n_frames, self.cfg.frame_width), np.uint32)
+        n = C.c_int32()
+        params = sampling.to_c()
+        _lib.check(_lib.lib().sx_decode_sample(self.handle, n_frames, seed & 0xFFFFFFFFFFFFFFFF, C.byref(params),
+                                               _p(out, C.c_uint32), C.byref(n)))
+        return out[: n.value]
+
     def decode_greedy_batch(self, n: int, n_frames: int, mask_stop: bool = False) -> list[np.ndarray]:
         out = np.zeros((n, n_frames, self.cfg.frame_width), np.uint32)
         counts = np.zeros(n, np.int32)
