@@ -210,6 +210,21 @@ def bench_device(args):
     torch.cuda.synchronize()
     ms_e2e = dp.max_over_ranks(s3.elapsed_time(e3), dist, device="cuda")
 
+    # ---- the device-sampled loop (reference Sampler defaults, seed per rank), same session ----
+    K_s = max(0, min(64, be.max_ctx - be.seq_len() - 1))
+    sampled = None
+    if K_s > 0:
+        s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s4.record(stream)
+        got = be.decode_sample(K_s, seed=dp.rank_seed(SEED, rank), sampling=sx.SamplingParams())
+        e4.record(stream)
+        torch.cuda.synchronize()
+        ms_s = s4.elapsed_time(e4)
+        if got.shape[0] > 0:
+            sampled = {"value": round(got.shape[0] / (ms_s * 1e-3), 2), "unit": "frames/s", "frames": int(got.shape[0]),
+                       "api": "sx_decode_sample (device sampler: top-p 0.9, top-k 30, RAS; timed with CUDA events)"}
+
     frames_total = K * world
     value = frames_total / (ms_all * 1e-3)
     res = {
@@ -245,6 +260,7 @@ def bench_device(args):
         "gpu_launches": kernels_per_frame(cfg) * K,
         "clocks": clk.summary(),
         "load_s": round(t_load, 1),
+        "sampled": sampled,
     }
     if rank == 0 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg, blob, budget_s=args.cpu_budget)
