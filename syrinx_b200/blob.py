@@ -40,3 +40,31 @@ def write_blob(tensors: dict) -> np.ndarray:
         out[header + o: header + o + raw.size] = raw
     out[: len(hdr)] = np.frombuffer(bytes(hdr), np.uint8)
     return out
+
+
+def read_blob(blob) -> dict:
+    """name -> f32 ndarray, or (dtype, (rows, cols), raw uint8 blocks [rows, bytes per row]),
+    from an SXW1 blob (the inverse of write_blob)."""
+    b = np.asarray(blob, np.uint8).reshape(-1)
+    mv = memoryview(b.tobytes())
+    magic, version, n, _, data_off = struct.unpack_from("<4sIIIQ", mv, 0)
+    if magic != b"SXW1" or version != 1:
+        raise ValueError("not an SXW1 blob")
+    pos, out = 24, {}
+    for _ in range(n):
+        (ln,) = struct.unpack_from("<I", mv, pos)
+        name = bytes(mv[pos + 4: pos + 4 + ln]).decode()
+        pos += 4 + ln
+        dt, nd = struct.unpack_from("<II", mv, pos)
+        pos += 8
+        shape = struct.unpack_from("<" + "Q" * nd, mv, pos)
+        pos += 8 * nd
+        off, nbytes = struct.unpack_from("<QQ", mv, pos)
+        pos += 16
+        raw = b[data_off + off: data_off + off + nbytes]
+        if dt == SX_DTYPE_F32:
+            out[name] = raw.view(np.float32).reshape(shape).copy()
+        else:
+            rows = int(shape[0]) if nd == 2 else 1
+            out[name] = (dt, tuple(int(s) for s in shape), raw.reshape(rows, -1).copy())
+    return out
