@@ -146,7 +146,9 @@ def bench_device(args):
     be.set_stream(stream.cuda_stream)
     # each rank decodes its own utterance (independent prompts: seed + rank)
     prompt = dual_ar_prompt(cfg, PROMPT_T, PROMPT_SEMANTIC, seed=dp.rank_seed(SEED, rank))
+    t_pf = time.time()
     be.prefill(prompt)
+    t_prefill = time.time() - t_pf
 
     def barrier():
         if dist:
@@ -260,6 +262,7 @@ def bench_device(args):
         "gpu_launches": kernels_per_frame(cfg) * K,
         "clocks": clk.summary(),
         "load_s": round(t_load, 1),
+        "prefill_s": round(t_prefill, 3),
         "sampled": sampled,
     }
     if rank == 0 and not args.no_cpu_baseline:

@@ -66,8 +66,10 @@ __device__ __forceinline__ void load_item(const uint8_t* W, const Q8Geo& g, int 
   }
 }
 
+// Up to 8 tokens (decode) at three CTAs per SM; prefill chunks of 16..64 tokens hold one
+// accumulator pair per token pair and run one CTA per SM.
 template <int M>
-__global__ void __launch_bounds__(kThreads, 3) k_gemv_q8(const GemvArgs a, const Q8Geo g) {
+__global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const GemvArgs a, const Q8Geo g) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int NP = (M + 1) / 2;  // token pairs = tensor-core instructions per record
   __shared__ __align__(16) int8_t scr[kWarps][4][32];
@@ -445,17 +447,21 @@ size_t q8_part_floats(const DevMat& w, int64_t n_rows, int M) {
 
 cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st) {
   Q8Geo g;
-  if (a.w.dtype != SX_DTYPE_Q8_0 || !a.part || a.M < 1 || a.M > kMaxTok || !make_geo(a, &g))
+  if (a.w.dtype != SX_DTYPE_Q8_0 || !a.part || a.M < 1 || a.M > kMaxPrefillTok || !make_geo(a, &g))
     return cudaErrorInvalidValue;
   // the SwiGLU pairing is per tile of the whole interleaved matrix
   if (epi == EPI_SWIGLU && (a.row_base != 0 || a.n_extra != 0)) return cudaErrorInvalidValue;
-  const int Mt = a.M <= 1 ? 1 : a.M <= 2 ? 2 : a.M <= 4 ? 4 : 8;
+  int Mt = 1;
+  while (Mt < a.M) Mt <<= 1;
   if ((size_t)g.n_vt * g.nc * Mt * 16 > a.part_cap) return cudaErrorInvalidValue;
   switch (Mt) {
     case 1: return launch_m<1>(a, epi, g, st);
     case 2: return launch_m<2>(a, epi, g, st);
     case 4: return launch_m<4>(a, epi, g, st);
-    default: return launch_m<8>(a, epi, g, st);
+    case 8: return launch_m<8>(a, epi, g, st);
+    case 16: return launch_m<16>(a, epi, g, st);
+    case 32: return launch_m<32>(a, epi, g, st);
+    default: return launch_m<64>(a, epi, g, st);
   }
 }
 

@@ -460,18 +460,18 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
   const int dim = sl.dim;
   s->ring_frames = max_ctx;
   if ((rc = dalloc(s->allocs, &s->tok_seq, kMaxTok)) || (rc = dalloc(s->allocs, &s->tok_pos, kMaxTok)) ||
-      (rc = dalloc(s->allocs, &s->ptok_seq, kMaxTok)) || (rc = dalloc(s->allocs, &s->ptok_pos, kMaxTok)) ||
+      (rc = dalloc(s->allocs, &s->ptok_seq, kMaxPrefillTok)) || (rc = dalloc(s->allocs, &s->ptok_pos, kMaxPrefillTok)) ||
       (rc = dalloc(s->allocs, &s->seq_len, max_batch)) || (rc = dalloc(s->allocs, &s->done, max_batch)) ||
       (rc = dalloc(s->allocs, &s->frame_count, max_batch)) || (rc = dalloc(s->allocs, &s->err, 1)) ||
       (rc = dalloc(s->allocs, &s->frames, (size_t)max_batch * width)) ||
       (rc = dalloc(s->allocs, &s->ring, (size_t)s->ring_frames * max_batch * width)) ||
       (rc = dalloc(s->allocs, &s->prompt, (size_t)width * max_ctx)) ||
       (rc = dalloc(s->allocs, &s->h, (size_t)max_batch * dim)) ||
-      (rc = dalloc(s->allocs, &s->hp, (size_t)kMaxTok * dim)) ||
+      (rc = dalloc(s->allocs, &s->hp, (size_t)kMaxPrefillTok * dim)) ||
       (rc = dalloc(s->allocs, &s->fx, (size_t)max_batch * dim)) ||
-      (rc = dalloc(s->allocs, &s->xqkv, (size_t)kMaxTok * max_qkv)) ||
-      (rc = dalloc(s->allocs, &s->attn, (size_t)kMaxTok * max_att)) ||
-      (rc = dalloc(s->allocs, &s->act, (size_t)kMaxTok * max_F)) ||
+      (rc = dalloc(s->allocs, &s->xqkv, (size_t)kMaxPrefillTok * max_qkv)) ||
+      (rc = dalloc(s->allocs, &s->attn, (size_t)kMaxPrefillTok * max_att)) ||
+      (rc = dalloc(s->allocs, &s->act, (size_t)kMaxPrefillTok * max_F)) ||
       (rc = dalloc(s->allocs, &s->logits, (size_t)max_batch * d.vocab_size)) ||
       (rc = dalloc(s->allocs, &s->fast_logits, (size_t)max_batch * std::max(1, d.codebook_size))) ||
       (rc = dalloc(s->allocs, &s->hidden, (size_t)max_batch * dim)) ||
@@ -479,25 +479,26 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
       (rc = dalloc(s->allocs, &s->dparams, 1)))
     return fail(rc);
   {
-    // partial sums of the largest Q8_0 GEMV at the most tokens one launch takes
+    // partial sums of the largest Q8_0 GEMV at the most tokens one launch takes: a prefill
+    // chunk for the layer matrices, a decode batch for the heads
     size_t cap = 0;
-    auto need = [&](const DevMat& w) {
-      if (w.dtype == SX_DTYPE_Q8_0) cap = std::max(cap, q8_part_floats(w, w.rows, kMaxTok));
+    auto need = [&](const DevMat& w, int M) {
+      if (w.dtype == SX_DTYPE_Q8_0) cap = std::max(cap, q8_part_floats(w, w.rows, M));
     };
     for (const auto* ls : {&m->slow, &m->fast})
       for (const DevLayer& L : *ls) {
-        need(L.wqkv);
-        need(L.wo);
-        need(L.w13);
-        need(L.w2);
+        need(L.wqkv, kMaxPrefillTok);
+        need(L.wo, kMaxPrefillTok);
+        need(L.w13, kMaxPrefillTok);
+        need(L.w2, kMaxPrefillTok);
       }
-    for (const DevMat* w : {&m->emb, &m->cb_emb, &m->out_w, &m->fast_out, &m->fast_emb}) need(*w);
+    for (const DevMat* w : {&m->emb, &m->cb_emb, &m->out_w, &m->fast_out, &m->fast_emb}) need(*w, kMaxTok);
     s->q8_part_cap = cap;
     if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
   }
   if (m->tp_size > 1) {
     // receive region rx [2][kMaxTp][xb_cap] 8-byte words; peers map it by IPC
-    const int xb_cap = kMaxTok * dim;
+    const int xb_cap = kMaxPrefillTok * dim;
     s->tp_region_bytes = (size_t)2 * kMaxTp * xb_cap * 8;
     uint8_t* region = nullptr;
     uint32_t* epochs = nullptr;
@@ -847,8 +848,8 @@ int prefill_seq(sx_session* s, int seq, const uint32_t* prompt, int T) {
   SX_CU(cudaMemcpyAsync(s->prompt, prompt, (size_t)rows * T * 4, cudaMemcpyHostToDevice, s->st));
   const int base = s->len[seq];
   int last_M = 0;
-  for (int c0 = 0; c0 < T; c0 += kMaxTok) {
-    const int M = std::min(kMaxTok, T - c0);
+  for (int c0 = 0; c0 < T; c0 += kMaxPrefillTok) {
+    const int M = std::min(kMaxPrefillTok, T - c0);
     std::vector<int> ts(M, seq), tp(M);
     for (int i = 0; i < M; i++) tp[i] = base + c0 + i;
     SX_RC(upload_tokens(s, s->ptok_seq, s->ptok_pos, ts, tp));

@@ -60,11 +60,11 @@ struct sx_session {
   uint32_t* prompt = nullptr;  // [(1+C) * max_ctx]
   // activations
   float* h = nullptr;     // [max_batch][dim] decode residual (h_last after prefill)
-  float* hp = nullptr;    // [kMaxTok][dim] prefill residual
+  float* hp = nullptr;    // [kMaxPrefillTok][dim] prefill residual
   float* fx = nullptr;    // [max_batch][fast dim] fast residual
-  float* xqkv = nullptr;  // [kMaxTok][max qkv]
-  float* attn = nullptr;  // [kMaxTok][max H*hd]
-  float* act = nullptr;   // [kMaxTok][max F]
+  float* xqkv = nullptr;  // [kMaxPrefillTok][max qkv]
+  float* attn = nullptr;  // [kMaxPrefillTok][max H*hd]
+  float* act = nullptr;   // [kMaxPrefillTok][max F]
   float* logits = nullptr;       // [max_batch][vocab]
   float* fast_logits = nullptr;  // [max_batch][R]
   float* hidden = nullptr;       // [max_batch][dim]

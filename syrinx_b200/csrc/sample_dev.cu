@@ -7,9 +7,11 @@
 // CDF in index order on a SplitMix64 draw) and the RAS rule of sample_semantic (143-167:
 // a second draw at the high temperature / top-p replaces a semantic draw found in the
 // window of recent semantic ids). Every floating-point step follows the host restatement
-// (syrinx_b200/csrc/sampling.cpp) in the same order and precision, so the device draws the
-// same ids from the same logits and seed; the only source of difference is the last bit of
-// the f64 exp, which can only matter when a top-p or draw comparison lands within an ulp.
+// (syrinx_b200/csrc/sampling.cpp) in the same order and precision, except the softmax
+// normaliser of the top-p cut (a fixed-order tree sum instead of one thread's rank-order
+// loop), so the device draws the same ids from the same logits and seed; that sum and the
+// last bit of the f64 exp can only matter when a top-p or draw comparison lands within an
+// ulp. The kept ids' sums (the probabilities and the draw) keep the reference's index order.
 //
 // Ids outside the constraint carry -inf logits in the reference: they sort last, add exact
 // zeros to every sum and are never drawn, so the kernel works on the allowed ids only.
@@ -46,8 +48,40 @@ struct Smem {
   double* exps;              // [n] by rank: exp(logit - max)
   float* lg;                 // [n] logits in index order
   float* pf;                 // [n] probabilities in index order (kept ids only)
+  int* kept;                 // [n] the kept ids' indices, ascending
   uint8_t* keep;             // [n] kept flags in index order
 };
+
+// Compact the kept flags into an ascending index list (block-wide exclusive scan).
+__device__ void compact_kept(const Smem& m, int n) {
+  __shared__ int s_warp[kThreadsS / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (n + kThreadsS - 1) / kThreadsS, i0 = tid * per, i1 = min(n, i0 + per);
+  int c = 0;
+  for (int i = i0; i < i1; i++) c += m.keep[i];
+  int incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kThreadsS / 32 ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += v;
+    }
+    if (lane < kThreadsS / 32) s_warp[lane] = w;  // inclusive totals per warp
+  }
+  __syncthreads();
+  int pos = incl - c + (warp > 0 ? s_warp[warp - 1] : 0);
+  for (int i = i0; i < i1; i++)
+    if (m.keep[i]) m.kept[pos++] = i;
+  __syncthreads();
+}
 
 __device__ __forceinline__ int order_at(const Smem& m, int r) { return (int)(0xFFFFFFFFu - (uint32_t)m.keys[r]); }
 
@@ -84,35 +118,34 @@ __device__ uint32_t draw(const SampleArgs& a, const Smem& m, int n, double sum, 
   mx = warp_max(mx);
   if ((tid & 31) == 0) s_red[tid >> 5] = mx;
   __syncthreads();
+  compact_kept(m, n);  // the index-order loops below visit only the rend kept ids
   if (tid == 0) {
     float kept_max = -INFINITY;
     for (int w = 0; w < kThreadsS / 32; w++) kept_max = fmaxf(kept_max, s_red[w]);
     double psum = 0.0;
-    for (int i = 0; i < n; i++)
-      if (m.keep[i]) {
-        const double e = exp((double)(__fdiv_rn(m.lg[i], t) - kept_max));
-        m.pf[i] = (float)e;
-        psum += e;
-      }
+    for (int j = 0; j < rend; j++) {
+      const int i = m.kept[j];
+      const double e = exp((double)(__fdiv_rn(m.lg[i], t) - kept_max));
+      m.pf[i] = (float)e;
+      psum += e;
+    }
     if (psum > 0.0)
-      for (int i = 0; i < n; i++)
-        if (m.keep[i]) m.pf[i] = (float)((double)m.pf[i] / psum);
+      for (int j = 0; j < rend; j++) m.pf[m.kept[j]] = (float)((double)m.pf[m.kept[j]] / psum);
     double total = 0.0;
-    for (int i = 0; i < n; i++)
-      if (m.keep[i]) total += (double)m.pf[i];
+    for (int j = 0; j < rend; j++) total += (double)m.pf[m.kept[j]];
     uint32_t pick = 0;
     if (total > 0.0) {
       const double u = next_f64(a.st) * total;
       double acc = 0.0;
       pick = a.full_last;
-      for (int i = 0; i < n; i++)
-        if (m.keep[i]) {
-          acc += (double)m.pf[i];
-          if (u < acc) {
-            pick = id_of(a, i);
-            break;
-          }
+      for (int j = 0; j < rend; j++) {
+        const int i = m.kept[j];
+        acc += (double)m.pf[i];
+        if (u < acc) {
+          pick = id_of(a, i);
+          break;
         }
+      }
     }
     s_pick = pick;
   }
@@ -132,7 +165,8 @@ __global__ void __launch_bounds__(kThreadsS, 1) k_sample(const SampleArgs a) {
   m.exps = reinterpret_cast<double*>(m.keys + np);
   m.lg = reinterpret_cast<float*>(m.exps + n);
   m.pf = m.lg + n;
-  m.keep = reinterpret_cast<uint8_t*>(m.pf + n);
+  m.kept = reinterpret_cast<int*>(m.pf + n);
+  m.keep = reinterpret_cast<uint8_t*>(m.kept + n);
   const int tid = threadIdx.x;
   for (int i = tid; i < np; i += kThreadsS) {
     unsigned long long key = 0ull;  // padding sorts last
@@ -163,10 +197,24 @@ __global__ void __launch_bounds__(kThreadsS, 1) k_sample(const SampleArgs a) {
   for (int r = tid; r < n; r += kThreadsS) m.exps[r] = exp((double)(m.lg[order_at(m, r)] - mx));
   __syncthreads();
   __shared__ double s_sum;
-  if (tid == 0) {
-    double s = 0.0;
-    for (int r = 0; r < n; r++) s += m.exps[r];
-    s_sum = s;
+  {
+    // The softmax normaliser of the top-p cut, as a fixed-order tree (strided per-thread
+    // sums, then warp and block trees): deterministic, and within an ulp or two of the
+    // reference's rank-order sum. It only scales the cumulative sums compared with top_p, so
+    // like the last bit of exp it can matter only when such a comparison lands within an ulp.
+    __shared__ double s_part[kThreadsS / 32];
+    double part = 0.0;
+    for (int r = tid; r < n; r += kThreadsS) part += m.exps[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if ((tid & 31) == 0) s_part[tid >> 5] = part;
+    __syncthreads();
+    if (tid < 32) {
+      double v = tid < kThreadsS / 32 ? s_part[tid] : 0.0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (tid == 0) s_sum = v;
+    }
   }
   __syncthreads();
   const double sum = s_sum;
@@ -196,7 +244,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) k_sample(const SampleArgs a) {
 size_t sample_smem_bytes(int n) {
   int np = 1;
   while (np < n) np <<= 1;
-  return (size_t)np * 8 + (size_t)n * (8 + 4 + 4 + 1);
+  return (size_t)np * 8 + (size_t)n * (8 + 4 + 4 + 4 + 1);
 }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {

@@ -34,7 +34,8 @@
 namespace sx {
 
 constexpr int kPage = 64;         // KV positions per page
-constexpr int kMaxTok = 8;        // max tokens per GEMV launch (batched decode / prefill chunk)
+constexpr int kMaxTok = 8;        // max sequences of a batched decode step
+constexpr int kMaxPrefillTok = 64;  // tokens per prefill chunk (max tokens per GEMV launch)
 constexpr int kAttnThreads = 256;  // 8 warps per attention CTA
 constexpr int kMaxCluster = 8;     // max splits of the attention key axis (one portable cluster)
 constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one CTA
@@ -217,7 +218,7 @@ cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, f
 int dequantize_noalloc(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device);
 
 // device sampler (sample_dev.cu): the reference Sampler for one sequence, one CTA per draw
-constexpr int kSampleMaxIds = 8192;  // allowed ids per draw
+constexpr int kSampleMaxIds = 7168;  // allowed ids per draw (shared memory: 216 KB at the cap)
 constexpr int kMaxRasWin = 64;       // longest RAS window the device keeps
 struct SampleState {                 // per sequence, in device memory
   unsigned long long rng;            // SplitMix64 state
