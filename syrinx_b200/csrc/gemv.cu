@@ -3,7 +3,8 @@
 //
 // Replaces the quantized linear of the reference hot path (`Weights::linear`,
 // crates/syrinx-fish/src/s2/nn.rs:61-68; `Qwen2Lm::linear` over candle QMatMul,
-// crates/syrinx-lm/src/cv2/mod.rs:195-211) at M = 1..8 tokens, with the neighbouring
+// crates/syrinx-lm/src/cv2/mod.rs:195-211) at M = 1..8 tokens per launch (longer prefill
+// chunks are split into launches of up to 8), with the neighbouring
 // element-wise ops fused in:
 //   prologue  RMSNorm of x with a gain vector (rms_norm_w, s2/nn.rs:100-106)
 //   epilogue  + bias, residual add (s2/slow_ar.rs:195,198), SiLU(g)*u (s2/nn.rs:452-457),

@@ -1,4 +1,6 @@
-// gemv_q8.cu — Q8_0 GEMV for decode (M = 1..8 tokens) on int8 tensor-core fragments.
+// gemv_q8.cu — Q8_0 GEMV on int8 tensor-core fragments: decode (M = 1..8 tokens) and
+// prefill chunks (up to 64 tokens), plus the merge kernels, including the tensor-parallel
+// residual exchange.
 //
 // Replaces the quantized linear of the reference hot path (`Weights::linear`,
 // crates/syrinx-fish/src/s2/nn.rs:61-68; `Qwen2Lm::linear` over candle QMatMul,
@@ -307,59 +309,66 @@ __global__ void __launch_bounds__(256) k_merge_q8_tp(const GemvArgs a, const Q8G
   pdl_wait();
   const TpComm& tp = a.tp;
   const int lane = threadIdx.x & 31, q4 = lane & 3;
-  const long long u = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
-  const bool live = u < (long long)g.n_vt * 16 * M;
-  const int vt = live ? (int)(u / (16 * M)) : 0;
-  const int m = live ? (int)((u / 16) % M) : 0;
-  const int r = live ? (int)(u % 16) : 0;
-  float s0 = 0.f;
-  if (live) {
-    const float* p = a.part + ((size_t)vt * g.nc * M + m) * 16 + r;
-    const int k0 = q4 * g.nc / 4, k1 = (q4 + 1) * g.nc / 4;
-#pragma unroll 4
-    for (int kc = k0; kc < k1; kc++) s0 += __ldcg(p + (size_t)kc * M * 16);
-  }
-  const int base = lane & ~3;
-  const float t0 = ((__shfl_sync(0xffffffffu, s0, base) + __shfl_sync(0xffffffffu, s0, base + 1)) +
-                    __shfl_sync(0xffffffffu, s0, base + 2)) +
-                   __shfl_sync(0xffffffffu, s0, base + 3);
-  const int pr = (g.t_first + vt) * 16 + r;
-  const bool valid = live && q4 == 0 && m < a.M && pr >= a.row_base && pr < a.row_base + a.n_range;
-  if (!valid) return;
-  const size_t idx = (size_t)m * a.ldy + pr;
-  const uint32_t ep = ld_cg(tp.slot_epochs + idx) + 1;  // only this thread touches slot idx here
-  tp.slot_epochs[idx] = ep;
-  const size_t par = (size_t)(ep & 1) * kMaxTp;
-  const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(t0);
-  for (int p = 0; p < tp.size; p++)
-    if (p != tp.rank) st_relaxed_sys_u64(tp.rx[p] + (par + tp.rank) * tp.xb_cap + idx, word);
+  const long long n_units = (long long)g.n_vt * 16 * M;
+  // grid-stride over units (4 lanes each), warp-uniform trip count: the grid is capped so
+  // that every CTA of the exchange is co-resident, and a CTA waiting for its counterpart on
+  // a peer never waits for a CTA that cannot be scheduled
+  const long long stride = (long long)gridDim.x * (blockDim.x >> 2);
   bool ok = ld_cg(tp.err) == 0;
-  float tot = 0.f;
-  for (int q = 0; q < tp.size; q++) {
-    float v = t0;
-    if (q != tp.rank) {
-      const uint64_t* src = tp.rx[tp.rank] + (par + q) * tp.xb_cap + idx;
-      uint64_t w = ld_relaxed_sys_u64(src);
-      if (ok && (uint32_t)(w >> 32) != ep) {
-        const uint64_t t_start = global_ns();
-        do {
-          w = ld_relaxed_sys_u64(src);
-          if (global_ns() - t_start > kTpWaitNs) {
-            ok = false;
-            atomicExch(tp.err, 3);
-            break;
-          }
-        } while ((uint32_t)(w >> 32) != ep);
-      }
-      v = __uint_as_float((uint32_t)w);
+  for (long long u0 = ((long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >> 2; u0 < n_units; u0 += stride) {
+    const long long u = u0 + (lane >> 2);
+    const bool live = u < n_units;
+    const int vt = live ? (int)(u / (16 * M)) : 0;
+    const int m = live ? (int)((u / 16) % M) : 0;
+    const int r = live ? (int)(u % 16) : 0;
+    float s0 = 0.f;
+    if (live) {
+      const float* p = a.part + ((size_t)vt * g.nc * M + m) * 16 + r;
+      const int k0 = q4 * g.nc / 4, k1 = (q4 + 1) * g.nc / 4;
+#pragma unroll 4
+      for (int kc = k0; kc < k1; kc++) s0 += __ldcg(p + (size_t)kc * M * 16);
     }
-    tot += v;
+    const int base = lane & ~3;
+    const float t0 = ((__shfl_sync(0xffffffffu, s0, base) + __shfl_sync(0xffffffffu, s0, base + 1)) +
+                      __shfl_sync(0xffffffffu, s0, base + 2)) +
+                     __shfl_sync(0xffffffffu, s0, base + 3);
+    const int pr = (g.t_first + vt) * 16 + r;
+    const bool valid = live && q4 == 0 && m < a.M && pr >= a.row_base && pr < a.row_base + a.n_range;
+    if (!valid) continue;
+    const size_t idx = (size_t)m * a.ldy + pr;
+    const uint32_t ep = ld_cg(tp.slot_epochs + idx) + 1;  // only this thread touches slot idx here
+    tp.slot_epochs[idx] = ep;
+    const size_t par = (size_t)(ep & 1) * kMaxTp;
+    const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(t0);
+    for (int p = 0; p < tp.size; p++)
+      if (p != tp.rank) st_relaxed_sys_u64(tp.rx[p] + (par + tp.rank) * tp.xb_cap + idx, word);
+    float tot = 0.f;
+    for (int q = 0; q < tp.size; q++) {
+      float v = t0;
+      if (q != tp.rank) {
+        const uint64_t* src = tp.rx[tp.rank] + (par + q) * tp.xb_cap + idx;
+        uint64_t w = ld_relaxed_sys_u64(src);
+        if (ok && (uint32_t)(w >> 32) != ep) {
+          const uint64_t t_start = global_ns();
+          do {
+            w = ld_relaxed_sys_u64(src);
+            if (global_ns() - t_start > kTpWaitNs) {
+              ok = false;
+              atomicExch(tp.err, 3);
+              break;
+            }
+          } while ((uint32_t)(w >> 32) != ep);
+        }
+        v = __uint_as_float((uint32_t)w);
+      }
+      tot += v;
+    }
+    if (!ok) continue;
+    float v = tot;
+    if (a.bias) v = __fadd_rn(v, a.bias[pr]);
+    float* dst = a.y + (size_t)m * a.ldy + pr;
+    *dst = __fadd_rn(ld_cg(dst), v);
   }
-  if (!ok) return;
-  float v = tot;
-  if (a.bias) v = __fadd_rn(v, a.bias[pr]);
-  float* dst = a.y + (size_t)m * a.ldy + pr;
-  *dst = __fadd_rn(ld_cg(dst), v);
 }
 
 int num_sms() {
@@ -408,7 +417,8 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, g);
   if (e != cudaSuccess) return e;
   if (epi == EPI_ADD && a.tp.size > 1) {
-    const long long blocks = ((long long)g.n_vt * 16 * M * 4 + 255) / 256;
+    // at most four CTAs per SM (every one co-resident once the GEMV drains)
+    const long long blocks = std::min<long long>(((long long)g.n_vt * 16 * M * 4 + 255) / 256, 4LL * sms);
     if (a.n_extra != 0 || (long long)M * a.ldy > a.tp.xb_cap) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr2[1];
     cudaLaunchConfig_t cfg2 = launch_cfg(dim3((unsigned)blocks), dim3(256), 0, st, attr2);
