@@ -37,6 +37,27 @@ def test_every_declared_symbol_is_exported():
     assert set(_lib.SIGNATURES) == syms, "ctypes signature table out of sync with the header"
 
 
+def declared_param_counts():
+    """sx_name -> number of parameters, from the prototypes in include/*.h."""
+    out = {}
+    for name in os.listdir(os.path.join(ROOT, "include")):
+        if name.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", name)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            for fn, params in re.findall(r"\b(sx_[a-z0-9_]+)\s*\(([^;{)]*)\)\s*;", text, flags=re.S):
+                params = params.strip()
+                out[fn] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_header_parameter_counts():
+    counts = declared_param_counts()
+    assert len(counts) >= 25
+    bad = {fn: (n, len(_lib.SIGNATURES[fn][1])) for fn, n in counts.items()
+           if fn in _lib.SIGNATURES and len(_lib.SIGNATURES[fn][1]) != n}
+    assert not bad, f"parameter counts differ (header, ctypes): {bad}"
+
+
 def test_version_and_error_string():
     L = _lib.lib()
     assert b"sm_100a" in L.sx_version()
