@@ -172,6 +172,8 @@ def bench_device(args):
     ms_all = dp.max_over_ranks(ms, dist, device="cuda")
     mean_ctx = ctx_start + (K - 1) / 2.0
     fb_sem = frame_bytes(cfg, SX_DTYPE_Q8_0, ctx=mean_ctx, semantic_head=True, kv_elem=4)
+    # the algorithmic bytes as defined for the path count the KV cache at bf16
+    fb_bf16 = frame_bytes(cfg, SX_DTYPE_Q8_0, ctx=mean_ctx, semantic_head=True, kv_elem=2)
 
     # ---- roofline of the dominant kernel: the batch-1 Q8_0 GEMV, timed alone live ----
     peak, peak_kind = peaks()
@@ -248,7 +250,10 @@ def bench_device(args):
                    "l2": "inputs larger than L2 (4.8 GB of weights; 8.4 GB streamed per frame)"},
         "hbm_roofline": {"bytes_per_frame": fb_sem["total"], "frac_of_peak": round(
             fb_sem["total"] * value / world / (peak * 1e9), 4), "peak_gbs": peak, "peak_kind": peak_kind,
-            "note": "semantic-only head (4097 rows) counted, as streamed"},
+            "bytes_per_frame_kv_bf16": fb_bf16["total"],
+            "frac_of_peak_kv_bf16": round(fb_bf16["total"] * value / world / (peak * 1e9), 4),
+            "note": "semantic-only head (4097 rows) counted, as streamed; the session's KV cache is f32 "
+                    "(bytes_per_frame), the kv_bf16 figures count the same KV at bf16"},
         "roofline": {"bound": "hbm", "kernel": "k_gemv_q8<1> + k_merge_q8<1,SwiGLU>: Q8_0 w1|w3 at M=1 (timed as the pair)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": W13_DRAM_BYTES,
@@ -266,7 +271,7 @@ def bench_device(args):
         "sampled": sampled,
     }
     if rank == 0 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline(cfg, blob, budget_s=args.cpu_budget)
+        res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
     be.close()
     model.close()
     if dist:
@@ -366,54 +371,79 @@ def bench_tp(args):
         print(json.dumps(res), flush=True)
 
 
-def cpu_baseline(cfg, blob, budget_s: float, frames: int | None = None) -> dict:
-    """The oracle (CPU restatement of the reference path) decoding frames of the same
-    workload on all host cores: a bounded sample (short prompt, a few frames)."""
+def cpu_decoder(cfg, seed: int):
+    """The oracle (CPU restatement of the reference path) on all host cores, prefilled with
+    the GPU arm's 512-token prompt (untimed). Its weights come from the oracle library's copy
+    of the seeded writer, so this arm never loads the product library."""
     from oracle import oracle as oc
+    from syrinx_b200.configs import SX_DTYPE_Q8_0
     from syrinx_b200.workloads import dual_ar_prompt
 
     # all host cores, whatever OMP_NUM_THREADS a launcher (torchrun sets 1) left behind
     oc.set_num_threads(len(os.sched_getaffinity(0)))
+    blob = oc.synth_blob(cfg, SX_DTYPE_Q8_0, seed)
     om = oc.OracleModel(cfg, blob)
-    sess = oc.OracleSession(om, max_ctx=256, kv_bf16=False)
-    prompt = dual_ar_prompt(cfg, 16, 13, seed=SEED)
+    sess = oc.OracleSession(om, max_ctx=PROMPT_T + 1024, kv_bf16=False)
+    prompt = dual_ar_prompt(cfg, PROMPT_T, PROMPT_SEMANTIC, seed=seed)
+    t0 = time.perf_counter()
     logits, hidden = sess.prefill(prompt)
+    state = {"om": om, "sess": sess, "logits": logits, "hidden": hidden, "blob": blob,
+             "prefill_s": time.perf_counter() - t0, "cores": oc.num_threads()}
+
+    def frame():
+        tok, _ = om.greedy_semantic(state["logits"], mask_stop=True)
+        codes, _ = sess.fast_expand_greedy(state["hidden"], om.first_code(tok))
+        state["logits"], state["hidden"] = sess.slow_step(np.concatenate([[tok], codes]).astype(np.uint32))
+
+    return frame, state
+
+
+def cpu_baseline(cfg, budget_s: float) -> dict:
+    """A bounded sample of the bench workload on the CPU oracle: greedy frames after the same
+    512-token prompt, timed until the budget is spent (prefill excluded)."""
+    frame, st = cpu_decoder(cfg, SEED)
     n, t_total = 0, 0.0
-    limit = frames if frames is not None else 10_000
-    while n < limit:
+    while t_total < budget_s and n < 1000:
         t0 = time.perf_counter()
-        tok, _ = om.greedy_semantic(logits, mask_stop=True)
-        codes, _ = sess.fast_expand_greedy(hidden, om.first_code(tok))
-        logits, hidden = sess.slow_step(np.concatenate([[tok], codes]).astype(np.uint32))
+        frame()
         t_total += time.perf_counter() - t0
         n += 1
-        if frames is None and t_total >= budget_s:
-            break
-    return {"value": round(n / t_total, 4), "unit": "frames/s", "cores": oc.num_threads(), "kind": "port",
-            "sample": f"config3 Q8_0 weights, 16-token prompt, {n} greedy frames decoded on the CPU oracle "
-                      f"({t_total:.1f} s, prefill excluded)"}
+    return {"value": round(n / t_total, 4), "unit": "frames/s", "cores": st["cores"], "kind": "port",
+            "sample": f"config3 Q8_0 weights, the same 512-token prompt (prefill {st['prefill_s']:.1f} s, "
+                      f"excluded), {n} greedy frames decoded on the CPU oracle ({t_total:.1f} s)"}
 
 
 def bench_reference(args):
-    """--impl reference: the reference path on the host cores (CPU restatement)."""
+    """--impl reference: the reference path on the host cores (the CPU restatement: the
+    Rust/Candle reference cannot be built here). Same workload as the GPU arm: config 3 after
+    the 512-token prompt (prefill untimed), `warmup` untimed frames, then `steps` timed frames."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import syrinx_b200 as sx
-    from syrinx_b200.configs import SX_DTYPE_Q8_0
+    from syrinx_b200.configs import QWEN3_4B
 
-    cfg = sx.QWEN3_4B
-    blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=SEED)
-    budget = min(120.0, max(10.0, 1.0 * (args.steps + args.warmup)))
-    base = cpu_baseline(cfg, blob, budget_s=budget)
+    cfg = QWEN3_4B
+    frame, st = cpu_decoder(cfg, SEED)
+    for _ in range(args.warmup):
+        frame()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        frame()
+    secs = time.perf_counter() - t0
+    value = args.steps / secs
+    sample = (f"config3 Q8_0 weights, the GPU arm's 512-token prompt (prefill {st['prefill_s']:.1f} s, untimed), "
+              f"{args.warmup} warm-up + {args.steps} timed greedy frames on the CPU oracle ({secs:.1f} s)")
     res = {
-        "metric": METRIC, "value": base["value"], "unit": "frames/s", "n_gpus": 0, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(1000.0 / base["value"], 2) if base["value"] else None,
+        "metric": METRIC, "value": round(value, 4), "unit": "frames/s", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1000.0 * secs / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "impl": "reference",
-        "dtype": "q8_0 weights, f32 activations", "data": "synthetic",
-        "config": {"workload": "config3 qwen3-4b-shaped dual-AR Q8_0 b1, greedy frames (bounded CPU sample)"},
-        "cpu_baseline": base,
-        "e2e": {"value": base["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "dtype": "q8_0 weights, f32 activations, f32 KV", "data": "synthetic (same seeded weights and prompt)",
+        "config": {"workload": "config3 qwen3-4b-shaped dual-AR Q8_0 b1: prompt 512 (430 semantic), "
+                               "greedy frames, stop masked", "global_batch": 1, "seq_len": PROMPT_T,
+                   "same_config": True},
+        "cpu_baseline": {"value": round(value, 4), "unit": "frames/s", "cores": st["cores"], "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "Rust/Candle reference cannot be built here (no cargo/rustc, candle not vendored); "
                 "timed arm is the oracle/ CPU restatement of the same path",
     }

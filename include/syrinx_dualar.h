@@ -148,13 +148,21 @@ int sx_session_create_ex(sx_model* model, int32_t max_batch, int32_t max_ctx, in
  * rank and size), the caller gathers all handles in rank order (e.g. an all-gather over
  * torch.distributed), and every rank passes the whole array to sx_session_tp_connect before
  * its first decode call. Ranks on the same GPU are refused. A peer that does not reach a
- * residual exchange within 5 s makes the call return SX_E_DEVICE. */
+ * residual exchange within the session's wait limit (5 s unless sx_session_tp_set_timeout)
+ * makes the call return SX_E_DEVICE on every rank of the group: the rank that waited pushes
+ * poison words that fail its peers' exchanges too. The session then refuses to decode
+ * (SX_E_STATE) until the group reconnects: every rank calls sx_session_tp_disconnect, meets
+ * the others (a barrier), and runs handle / gather / connect again, which clears the
+ * exchange state; then sx_session_reset and prefill. */
 #define SX_TP_HANDLE_BYTES 128
 int sx_session_tp_handle(sx_session* s, void* handle_out);
 int sx_session_tp_connect(sx_session* s, const void* handles);
 /* Unmap the peers' regions (after the group's last decode call, before any rank destroys
  * its session: put a barrier between the two). */
 int sx_session_tp_disconnect(sx_session* s);
+/* Longest wait of a residual exchange for a peer's row, in ns of the GPU's global timer
+ * (default 5 s). Set before the session's first decode loop. No reference counterpart. */
+int sx_session_tp_set_timeout(sx_session* s, int64_t timeout_ns);
 /* Benchmark surface, no reference counterpart: give the empty sequence `seq` a slow-AR KV
  * cache of `len` positions of seeded values in [-1, 1), as if `len` tokens had been
  * prefilled. A following sx_prefill appends after them and decoding attends over all of
@@ -279,6 +287,15 @@ int sx_decode_greedy_batch(sx_session* s, int32_t n, int32_t n_frames, int32_t m
  * return the last position's logits [vocab] (head bias included). Replaces
  * `Qwen2Lm::step_logits_cached` (cv2/generate.rs:119-123) for token inputs. */
 int sx_lm_step_tokens(sx_session* s, const uint32_t* tokens, int32_t t_new, float* logits_out);
+
+/* Feed t_new caller-assembled input embeddings [t_new x slow.dim] (f32, row-major) of
+ * sequence 0 through the cached forward at the next positions and return the last
+ * position's logits [vocab] (head bias included; nullable). Replaces
+ * `Qwen2Lm::step_logits_cached(embeds)` (cv2/generate.rs:119-123), whose step-0 input
+ * `build_lm_input` (cv2/generate.rs:92) concatenates rows of several tables (sos / task id,
+ * text embed_tokens, speech_embedding). Later tokens may follow through sx_lm_step_tokens
+ * or sx_decode_greedy, which embed ids from embeddings.weight (the speech table). */
+int sx_lm_step_embeds(sx_session* s, const float* embeds, int32_t t_new, float* logits_out);
 
 /* ---- profiling ------------------------------------------------------------------------ */
 

@@ -20,6 +20,7 @@
 //   drive ................ crates/syrinx-fish/src/common/dualar.rs:161-230
 //   Sampler .............. crates/syrinx-fish/src/common/sampling.rs:19-268
 #include "oracle.h"
+#include "../syrinx_b200/csrc/blob.hpp"
 
 #include <omp.h>
 
@@ -611,6 +612,21 @@ int forward_ids(oc_session* s, const uint32_t* ids, int T, float* logits, float*
   return SX_OK;
 }
 
+// Qwen2Lm::step_logits_cached(embeds) (crates/syrinx-lm/src/cv2/generate.rs:119-123):
+// caller-assembled input embeddings through the cached layers, last-position head.
+int forward_embeds(oc_session* s, const float* embeds, int T, float* logits) {
+  oc_model* m = s->m;
+  if (T <= 0) return fail(SX_E_INVALID, "empty input");
+  if (s->len + T > s->max_ctx) return fail(SX_E_RANGE, "context exceeds session capacity");
+  const int dim = m->d.slow.dim;
+  std::vector<float> x(embeds, embeds + (size_t)T * dim);
+  run_layers(s, false, x.data(), T, s->len);
+  s->len += T;
+  s->last_h.assign(x.end() - dim, x.end());
+  head(s, s->last_h.data(), logits, nullptr);
+  return SX_OK;
+}
+
 uint32_t argmax_allowed(const sx_model_desc& d, const float* logits, bool mask_stop, float* margin) {
   float best = -INFINITY, second = -INFINITY;
   int64_t bi = -1;
@@ -970,6 +986,10 @@ int oc_lm_step_tokens(oc_session* s, const uint32_t* tokens, int32_t t_new, floa
   if (s->m->d.num_codebooks != 0) return fail(SX_E_UNSUPPORTED, "not a plain LM");
   return forward_ids(s, tokens, t_new, logits, nullptr);
 }
+int oc_lm_step_embeds(oc_session* s, const float* embeds, int32_t t_new, float* logits) {
+  if (!s || !embeds) return fail(SX_E_INVALID, "null argument");
+  return forward_embeds(s, embeds, t_new, logits);
+}
 int oc_fast_expand_greedy(oc_session* s, const float* hidden, uint32_t first_code, uint32_t* codes,
                           float* fast_logits) {
   return fast_expand(s, hidden, first_code, codes, fast_logits,
@@ -1054,6 +1074,19 @@ int oc_drive(oc_session* s, const uint32_t* prompt, int32_t T, int32_t max_frame
     pos++;
   }
   *n_out = nf;
+  return SX_OK;
+}
+
+int oc_synth_blob_size(const sx_model_desc* desc, int32_t wtype, size_t* size_out) {
+  if (!desc || !size_out) return fail(SX_E_INVALID, "null argument");
+  std::vector<sx::SynthTensor> ts;
+  size_t header = 0;
+  if (sx::synth_layout(*desc, wtype, &ts, &header, size_out)) return fail(SX_E_UNSUPPORTED, "synthetic blob layout");
+  return SX_OK;
+}
+int oc_synth_blob_write(const sx_model_desc* desc, int32_t wtype, uint64_t seed, void* out, size_t size) {
+  if (!desc || !out) return fail(SX_E_INVALID, "null argument");
+  if (sx::synth_write(*desc, wtype, seed, out, size)) return fail(SX_E_INVALID, "synthetic blob write");
   return SX_OK;
 }
 

@@ -85,6 +85,9 @@ int oc_prefill(oc_session* s, const uint32_t* prompt, int32_t T, float* logits, 
 int oc_slow_step(oc_session* s, const uint32_t* frame, float* logits, float* hidden);
 /* Plain-LM convenience: t_new tokens through the cached forward, last-position logits. */
 int oc_lm_step_tokens(oc_session* s, const uint32_t* tokens, int32_t t_new, float* logits);
+/* Input embeddings [t_new x slow.dim] through the cached forward, last-position logits
+ * (Qwen2Lm::step_logits_cached(embeds), cv2/generate.rs:119-123). */
+int oc_lm_step_embeds(oc_session* s, const float* embeds, int32_t t_new, float* logits);
 /* Greedy fast AR from `hidden`; codes [C]; fast_logits [(C-1) x R] nullable. */
 int oc_fast_expand_greedy(oc_session* s, const float* hidden, uint32_t first_code, uint32_t* codes,
                           float* fast_logits);
@@ -103,6 +106,11 @@ int oc_drive_greedy(oc_session* s, const uint32_t* prompt, int32_t T, int32_t n_
 /* The reference `drive` with the seeded Sampler. codes_out [C x max_frames]. */
 int oc_drive(oc_session* s, const uint32_t* prompt, int32_t T, int32_t max_frames, uint64_t seed,
              const sx_sampling_params* p, uint32_t* codes_out, int32_t* n_out);
+
+/* The seeded synthetic weights of sx_synth_blob_size / sx_synth_blob_write (the same
+ * writer source compiled into this library), so CPU-only callers need not load the product. */
+int oc_synth_blob_size(const sx_model_desc* desc, int32_t wtype, size_t* size_out);
+int oc_synth_blob_write(const sx_model_desc* desc, int32_t wtype, uint64_t seed, void* out, size_t size);
 
 /* Sampler pieces, for unit tests against the reference's own semantics. */
 uint64_t oc_splitmix64_next(uint64_t* state);

@@ -56,12 +56,15 @@ def lib() -> C.CDLL:
             "oc_prefill": (C.c_int, [C.c_void_p, _u32p, C.c_int32, _f32p, _f32p]),
             "oc_slow_step": (C.c_int, [C.c_void_p, _u32p, _f32p, _f32p]),
             "oc_lm_step_tokens": (C.c_int, [C.c_void_p, _u32p, C.c_int32, _f32p]),
+            "oc_lm_step_embeds": (C.c_int, [C.c_void_p, _f32p, C.c_int32, _f32p]),
             "oc_fast_expand_greedy": (C.c_int, [C.c_void_p, _f32p, C.c_uint32, _u32p, _f32p]),
             "oc_first_code": (C.c_uint32, [C.c_void_p, C.c_uint32]),
             "oc_greedy_semantic": (C.c_uint32, [C.c_void_p, _f32p, C.c_int32, _f32p]),
             "oc_drive_greedy": (C.c_int, [C.c_void_p, _u32p, C.c_int32, C.c_int32, C.c_int32, _u32p, _i32p, _f32p]),
             "oc_drive": (C.c_int, [C.c_void_p, _u32p, C.c_int32, C.c_int32, C.c_uint64, C.POINTER(SxSamplingParams), _u32p, _i32p]),
             "oc_splitmix64_next": (C.c_uint64, [C.POINTER(C.c_uint64)]),
+            "oc_synth_blob_size": (C.c_int, [C.POINTER(SxModelDesc), C.c_int32, C.POINTER(C.c_size_t)]),
+            "oc_synth_blob_write": (C.c_int, [C.POINTER(SxModelDesc), C.c_int32, C.c_uint64, C.c_void_p, C.c_size_t]),
             "oc_logits_to_probs": (None, [_f32p, C.c_int32, C.c_float, C.c_float, C.c_int32, _f32p]),
         }
         for name, (res, args) in sig.items():
@@ -79,6 +82,16 @@ def _p(a, ct):
 def _check(rc):
     if rc != 0:
         raise RuntimeError(f"oracle status {rc}: {lib().oc_last_error().decode()}")
+
+
+def synth_blob(cfg: ModelConfig, wtype: int, seed: int) -> np.ndarray:
+    """The seeded synthetic SXW1 blob (byte-identical to syrinx_b200.synth_blob)."""
+    desc = cfg.to_c()
+    size = C.c_size_t()
+    _check(lib().oc_synth_blob_size(C.byref(desc), wtype, C.byref(size)))
+    buf = np.empty(size.value, np.uint8)
+    _check(lib().oc_synth_blob_write(C.byref(desc), wtype, seed, buf.ctypes.data, size.value))
+    return buf
 
 
 # ---- block formats -----------------------------------------------------------------------
@@ -212,6 +225,12 @@ class OracleSession:
         t = np.ascontiguousarray(tokens, np.uint32).reshape(-1)
         logits = np.empty(self.cfg.vocab_size, np.float32)
         _check(lib().oc_lm_step_tokens(self.h, _p(t, C.c_uint32), t.size, _p(logits, C.c_float)))
+        return logits
+
+    def lm_step_embeds(self, embeds):
+        e = np.ascontiguousarray(embeds, np.float32).reshape(-1, self.cfg.slow.dim)
+        logits = np.empty(self.cfg.vocab_size, np.float32)
+        _check(lib().oc_lm_step_embeds(self.h, _p(e, C.c_float), e.shape[0], _p(logits, C.c_float)))
         return logits
 
     def fast_expand_greedy(self, hidden, first_code):

@@ -34,6 +34,7 @@ SIGNATURES = {
     "sx_session_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sx_session_tp_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sx_session_tp_disconnect": (C.c_int, [C.c_void_p]),
+    "sx_session_tp_set_timeout": (C.c_int, [C.c_void_p, C.c_int64]),
     "sx_session_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_uint64]),
     "sx_session_reset": (C.c_int, [C.c_void_p]),
     "sx_session_destroy": (C.c_int, [C.c_void_p]),
@@ -55,6 +56,7 @@ SIGNATURES = {
     "sx_fast_expand_batch_greedy": (C.c_int, [C.c_void_p, _u32p, _u8p, C.c_int32, _u32p]),
     "sx_decode_greedy_batch": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, _u32p, _i32p]),
     "sx_lm_step_tokens": (C.c_int, [C.c_void_p, _u32p, C.c_int32, _f32p]),
+    "sx_lm_step_embeds": (C.c_int, [C.c_void_p, _f32p, C.c_int32, _f32p]),
     "sx_dequantize": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, _f32p, C.c_int32]),
     "sx_dequantize_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, _f32p, C.c_int32]),
 }

@@ -174,6 +174,16 @@ COSYVOICE2_LM = ModelConfig(
     semantic_begin_id=0, semantic_end_id=6560, stop_token_id=6561, num_stop_tokens=3,
     tie_word_embeddings=False, head_bias=True)
 
+# CosyVoice3 LM (cv3/mod.rs:1-69): the same Qwen2 body as CosyVoice2 with a bias-free
+# `llm_decoder` of 6761 rows; every id from speech_token_size (6561) up is one of the 200
+# control ids that stop decoding (cv3/generate.rs:84-88), masked while step < min_len.
+COSYVOICE3_LM = ModelConfig(
+    name="cosyvoice3-qwen2-0.5b",
+    slow=Stack(896, 24, 14, 2, 64, 4864, 1e-6, 1e6, rope_interleaved=False, qkv_bias=True),
+    fast=NO_FAST, vocab_size=6761, num_codebooks=0, codebook_size=0,
+    semantic_begin_id=0, semantic_end_id=6560, stop_token_id=6561, num_stop_tokens=200,
+    tie_word_embeddings=False, head_bias=False)
+
 # Config 2: s1-mini-shaped dual-AR (Llama slow AR, no QK-norm, pre-norm fast hidden).
 S1_MINI = ModelConfig(
     name="s1-mini",
@@ -210,4 +220,4 @@ TINY_S2 = ModelConfig(
     semantic_begin_id=1024, semantic_end_id=1279, stop_token_id=7,
     scale_codebook_embeddings=True, norm_fastlayer_input=True)
 
-PRESETS = {c.name: c for c in (COSYVOICE2_LM, S1_MINI, QWEN3_4B, TINY_S2)}
+PRESETS = {c.name: c for c in (COSYVOICE2_LM, COSYVOICE3_LM, S1_MINI, QWEN3_4B, TINY_S2)}

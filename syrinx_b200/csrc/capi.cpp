@@ -154,6 +154,14 @@ int sx_session_tp_disconnect(sx_session* s) {
   SX_GUARD({ return session_tp_disconnect(s); })
 }
 
+int sx_session_tp_set_timeout(sx_session* s, int64_t timeout_ns) {
+  SX_GUARD({
+    int rc = need_session(s);
+    if (rc) return rc;
+    return session_tp_set_timeout(s, timeout_ns);
+  })
+}
+
 int sx_decode_sample(sx_session* s, int32_t n_frames, uint64_t seed, const sx_sampling_params* params,
                      uint32_t* frames_out, int32_t* n_frames_out) {
   SX_GUARD({
@@ -602,6 +610,20 @@ int sx_lm_step_tokens(sx_session* s, const uint32_t* tokens, int32_t t_new, floa
     } else {
       rc = prefill_seq(s, 0, tokens, t_new);
     }
+    if (rc) return rc;
+    return outputs_single(s, logits_out, nullptr);
+  })
+}
+
+int sx_lm_step_embeds(sx_session* s, const float* embeds, int32_t t_new, float* logits_out) {
+  SX_GUARD({
+    int rc = need_session(s);
+    if (rc) return rc;
+    if (!embeds || t_new <= 0) {
+      set_error("empty embedding input");
+      return SX_E_INVALID;
+    }
+    rc = prefill_seq_embeds(s, 0, embeds, t_new);
     if (rc) return rc;
     return outputs_single(s, logits_out, nullptr);
   })

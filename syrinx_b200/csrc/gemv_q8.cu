@@ -299,12 +299,17 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
 // e % 2: a rank starts exchange e + 2 only after its exchange e + 1 kernel completed, which
 // needed every peer's e + 1 word, which each peer stores only after its exchange e kernel
 // (and with it every read of parity e % 2) completed.
-// After a timeout the session's error flag stays raised until the host reads it, and later
-// exchanges skip their wait, so a lost peer costs one bounded wait, not one per exchange.
-constexpr uint64_t kTpWaitNs = 5000000000ull;
+// A rank whose wait runs out (the session's limit, TpComm::wait_ns) raises the session's
+// error flag (3) and from then on pushes poison words (epoch kTpPoison) instead of row sums,
+// in this exchange and in every later one while the flag stays raised; a receiver that reads
+// a poison word raises its own flag and stops waiting. So a lost or late peer makes every
+// rank fail within one bounded wait, and no rank accepts a value computed from residuals the
+// sender could not update. The host keeps the flag raised (the session refuses to decode)
+// until the group reconnects, which zeroes the receive regions and the slot epochs.
+constexpr uint32_t kTpPoison = 0xffffffffu;
 
 template <int M>
-__global__ void __launch_bounds__(256) k_merge_q8_tp(const GemvArgs a, const Q8Geo g) {
+__global__ void __launch_bounds__(256, 4) k_merge_q8_tp(const GemvArgs a, const Q8Geo g) {
   pdl_launch_dependents();
   pdl_wait();
   const TpComm& tp = a.tp;
@@ -339,25 +344,23 @@ __global__ void __launch_bounds__(256) k_merge_q8_tp(const GemvArgs a, const Q8G
     const uint32_t ep = ld_cg(tp.slot_epochs + idx) + 1;  // only this thread touches slot idx here
     tp.slot_epochs[idx] = ep;
     const size_t par = (size_t)(ep & 1) * kMaxTp;
-    const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(t0);
+    const uint64_t word = ok ? ((uint64_t)ep << 32) | __float_as_uint(t0) : ((uint64_t)kTpPoison << 32);
     for (int p = 0; p < tp.size; p++)
       if (p != tp.rank) st_relaxed_sys_u64(tp.rx[p] + (par + tp.rank) * tp.xb_cap + idx, word);
     float tot = 0.f;
-    for (int q = 0; q < tp.size; q++) {
+    for (int q = 0; q < tp.size && ok; q++) {
       float v = t0;
       if (q != tp.rank) {
         const uint64_t* src = tp.rx[tp.rank] + (par + q) * tp.xb_cap + idx;
         uint64_t w = ld_relaxed_sys_u64(src);
-        if (ok && (uint32_t)(w >> 32) != ep) {
-          const uint64_t t_start = global_ns();
-          do {
-            w = ld_relaxed_sys_u64(src);
-            if (global_ns() - t_start > kTpWaitNs) {
-              ok = false;
-              atomicExch(tp.err, 3);
-              break;
-            }
-          } while ((uint32_t)(w >> 32) != ep);
+        const uint64_t t_start = global_ns();
+        while ((uint32_t)(w >> 32) != ep) {
+          if ((uint32_t)(w >> 32) == kTpPoison || global_ns() - t_start > tp.wait_ns) {
+            ok = false;
+            atomicExch(tp.err, 3);
+            break;
+          }
+          w = ld_relaxed_sys_u64(src);
         }
         v = __uint_as_float((uint32_t)w);
       }
@@ -417,8 +420,14 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, g);
   if (e != cudaSuccess) return e;
   if (epi == EPI_ADD && a.tp.size > 1) {
-    // at most four CTAs per SM (every one co-resident once the GEMV drains)
-    const long long blocks = std::min<long long>(((long long)g.n_vt * 16 * M * 4 + 255) / 256, 4LL * sms);
+    // no more CTAs than can be resident at once (at most four per SM by the launch bounds),
+    // so every CTA of the exchange is co-resident once the GEMV drains
+    int occ = 0;
+    cudaError_t eo = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_merge_q8_tp<M>, 256, 0);
+    if (eo != cudaSuccess) return eo;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    const long long blocks =
+        std::min<long long>(((long long)g.n_vt * 16 * M * 4 + 255) / 256, (long long)std::min(occ, 4) * sms);
     if (a.n_extra != 0 || (long long)M * a.ldy > a.tp.xb_cap) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr2[1];
     cudaLaunchConfig_t cfg2 = launch_cfg(dim3((unsigned)blocks), dim3(256), 0, st, attr2);

@@ -326,9 +326,16 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
     }
   }
   if (d.num_codebooks < 0 || d.num_codebooks > 64 || d.vocab_size <= 0 || d.num_stop_tokens < 0 ||
-      d.num_stop_tokens > 4 || d.semantic_end_id < d.semantic_begin_id) {
+      d.num_stop_tokens > kMaxStops || d.semantic_end_id < d.semantic_begin_id ||
+      (int64_t)d.stop_token_id + d.num_stop_tokens > d.vocab_size) {
     set_error("sx_model_desc: bad vocab / codebook / stop configuration");
     return SX_E_INVALID;
+  }
+  if (d.num_stop_tokens > 4 && !stops_adjacent(d)) {
+    // a wide stop set (CosyVoice3: 200 control ids) must continue the semantic range, so the
+    // head reads it as one widened row range
+    set_error("sx_model_desc: more than 4 stop ids must sit right after (or before) the semantic range");
+    return SX_E_UNSUPPORTED;
   }
   SX_RC(check_tp(d.slow, tp_size, "slow"));
   SX_RC(check_tp(d.fast, tp_size, "fast"));
@@ -545,7 +552,20 @@ int session_tp_handle(sx_session* s, void* out) {
     set_error("sx_session_tp_handle: the model is not tensor-parallel");
     return SX_E_INVALID;
   }
+  if (s->tp_connected) {
+    set_error("sx_session_tp_handle: disconnect first (the handle starts a fresh exchange state)");
+    return SX_E_STATE;
+  }
   SX_CU(cudaSetDevice(s->m->device));
+  // A fresh exchange state: receive region, slot epochs and the error flag at zero. Every rank
+  // does this before the handle exchange, which no rank passes before all have, so no peer
+  // pushes into a region that is still being cleared.
+  SX_CU(cudaStreamSynchronize(s->st));
+  SX_CU(cudaMemset(s->tp_region, 0, s->tp_region_bytes));
+  SX_CU(cudaMemset(s->tp.slot_epochs, 0, (size_t)s->tp.xb_cap * 4));
+  SX_CU(cudaMemset(s->err, 0, 4));
+  SX_CU(cudaDeviceSynchronize());
+  s->tp_failed = false;
   cudaIpcMemHandle_t h;
   SX_CU(cudaIpcGetMemHandle(&h, s->tp_region));
   cudaDeviceProp prop;
@@ -615,6 +635,23 @@ int session_tp_disconnect(sx_session* s) {
   return SX_OK;
 }
 
+int session_tp_set_timeout(sx_session* s, int64_t timeout_ns) {
+  if (!s || timeout_ns <= 0) {
+    set_error("sx_session_tp_set_timeout: null session or non-positive limit");
+    return SX_E_INVALID;
+  }
+  if (s->m->tp_size < 2) {
+    set_error("sx_session_tp_set_timeout: the model is not tensor-parallel");
+    return SX_E_INVALID;
+  }
+  if (!s->graphs.empty()) {
+    set_error("sx_session_tp_set_timeout: set the limit before the first decode loop (its graphs hold the limit)");
+    return SX_E_STATE;
+  }
+  s->tp.wait_ns = (uint64_t)timeout_ns;
+  return SX_OK;
+}
+
 int session_reset(sx_session* s) {
   std::fill(s->len.begin(), s->len.end(), 0);
   std::fill(s->synthetic_len.begin(), s->synthetic_len.end(), 0);
@@ -639,6 +676,11 @@ int gemv(GemvArgs a, Epi epi, sx_session* s) {
     if (!s->tp_connected) {
       set_error("tensor-parallel session: call sx_session_tp_connect before decoding");
       return SX_E_INVALID;
+    }
+    if (s->tp_failed) {
+      set_error("tensor-parallel session: an earlier residual exchange failed; reconnect the group "
+                "(sx_session_tp_disconnect, then handle / connect on every rank) and reset");
+      return SX_E_STATE;
     }
     if (a.w.dtype != SX_DTYPE_Q8_0) {
       set_error("tensor parallelism needs Q8_0 weights");
@@ -743,21 +785,22 @@ int check_err(sx_session* s) {
   int e = 0;
   SX_CU(cudaMemcpyAsync(&e, s->err, 4, cudaMemcpyDeviceToHost, s->st));
   SX_CU(cudaStreamSynchronize(s->st));
-  if (e) {
-    SX_CU(cudaMemsetAsync(s->err, 0, 4, s->st));
-    SX_CU(cudaStreamSynchronize(s->st));
-    if (e == 2) {
-      set_error("a kernel's bounded pipeline wait timed out (device error flag)");
-      return SX_E_DEVICE;
-    }
-    if (e == 3) {
-      set_error("a tensor-parallel peer did not reach the residual exchange within 5 s");
-      return SX_E_DEVICE;
-    }
-    set_error("token id or codebook code out of range");
-    return SX_E_INVALID;
+  if (!e) return SX_OK;
+  if (e == 3) {
+    // The flag stays raised on the device (later exchanges push poison words instead of
+    // values) and the session refuses to decode until the group reconnects.
+    s->tp_failed = true;
+    set_error("a tensor-parallel peer did not complete a residual exchange in time (or reported a failure)");
+    return SX_E_DEVICE;
   }
-  return SX_OK;
+  SX_CU(cudaMemsetAsync(s->err, 0, 4, s->st));
+  SX_CU(cudaStreamSynchronize(s->st));
+  if (e == 2) {
+    set_error("a kernel's bounded pipeline wait timed out (device error flag)");
+    return SX_E_DEVICE;
+  }
+  set_error("token id or codebook code out of range");
+  return SX_E_INVALID;
 }
 
 EmbedArgs embed_args(sx_session* s) {
@@ -870,6 +913,38 @@ int prefill_seq(sx_session* s, int seq, const uint32_t* prompt, int T) {
   return SX_OK;
 }
 
+// Prefill from caller-assembled input embeddings [T][dim] (host f32) instead of ids: the
+// cached forward of `Qwen2Lm::step_logits_cached(embeds)` (cv2/generate.rs:119-123), whose
+// inputs `build_lm_input` (cv2/generate.rs:92) assembles from several tables.
+int prefill_seq_embeds(sx_session* s, int seq, const float* embeds, int T) {
+  const sx_model_desc& d = s->m->d;
+  const int dim = d.slow.dim;
+  if (T <= 0) {
+    set_error("lm_step_embeds: empty input");
+    return SX_E_INVALID;
+  }
+  if (s->len[seq] + T > s->max_ctx) {
+    set_error("lm_step_embeds: input exceeds the session's max_ctx");
+    return SX_E_RANGE;
+  }
+  const int base = s->len[seq];
+  int last_M = 0;
+  for (int c0 = 0; c0 < T; c0 += kMaxPrefillTok) {
+    const int M = std::min(kMaxPrefillTok, T - c0);
+    std::vector<int> ts(M, seq), tp(M);
+    for (int i = 0; i < M; i++) tp[i] = base + c0 + i;
+    SX_RC(upload_tokens(s, s->ptok_seq, s->ptok_pos, ts, tp));
+    SX_CU(cudaMemcpyAsync(s->hp, embeds + (size_t)c0 * dim, (size_t)M * dim * 4, cudaMemcpyHostToDevice, s->st));
+    SX_RC(run_stack(s, false, M, s->hp, s->ptok_seq, s->ptok_pos, 0, false));
+    last_M = M;
+  }
+  SX_CU(cudaMemcpyAsync(s->h + (size_t)seq * dim, s->hp + (size_t)(last_M - 1) * dim, (size_t)dim * 4,
+                        cudaMemcpyDeviceToDevice, s->st));
+  SX_RC(check_err(s));
+  s->len[seq] = base + T;
+  return SX_OK;
+}
+
 int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n) {
   const sx_model_desc& d = s->m->d;
   const int width = 1 + d.num_codebooks;
@@ -905,6 +980,26 @@ int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n
   return SX_OK;
 }
 
+// Rows the greedy / sampled head reads: the semantic range, plus the stop ids unless masked.
+// Stop ids adjacent to the range widen it; others (at most 4) are extra rows.
+void head_rows(const sx_model_desc& d, bool mask_stop, GemvArgs* g) {
+  const uint32_t sem_hi = std::min<uint32_t>(d.semantic_end_id, (uint32_t)d.vocab_size - 1);
+  uint32_t lo = d.semantic_begin_id, hi = sem_hi + 1;
+  g->n_extra = 0;
+  if (!mask_stop && d.num_stop_tokens > 0) {
+    const uint32_t t0 = d.stop_token_id, t1 = d.stop_token_id + (uint32_t)d.num_stop_tokens;
+    if (stops_adjacent(d)) {
+      lo = std::min(lo, t0);
+      hi = std::max(hi, t1);
+    } else {
+      for (uint32_t id = t0; id < t1; id++)
+        if ((id < lo || id >= hi) && id < (uint32_t)d.vocab_size) g->extra[g->n_extra++] = (int)id;
+    }
+  }
+  g->row_base = (int)lo;
+  g->n_range = (int)(hi - lo);
+}
+
 int run_head(sx_session* s, int n, bool want_logits, bool want_argmax, bool mask_stop) {
   sx_model* m = s->m;
   const sx_model_desc& d = m->d;
@@ -921,13 +1016,7 @@ int run_head(sx_session* s, int n, bool want_logits, bool want_argmax, bool mask
     g.ldy = d.vocab_size;
     g.n_range = d.vocab_size;
   } else {
-    g.row_base = (int)d.semantic_begin_id;
-    g.n_range = (int)(sem_hi - d.semantic_begin_id + 1);
-    if (!mask_stop)
-      for (int i = 0; i < d.num_stop_tokens; i++) {
-        const uint32_t id = d.stop_token_id + i;
-        if ((id < d.semantic_begin_id || id > sem_hi) && id < (uint32_t)d.vocab_size) g.extra[g.n_extra++] = (int)id;
-      }
+    head_rows(d, mask_stop, &g);
   }
   if (want_argmax) {
     g.amax = s->amax;
@@ -1133,10 +1222,7 @@ int greedy_frame_front(sx_session* s, int n, int mask_stop, bool sampled) {
     g.M = 1;
     g.y = s->logits;
     g.ldy = d.vocab_size;
-    g.row_base = (int)sa.sem_lo;
-    g.n_range = (int)(sa.sem_hi - sa.sem_lo + 1);
-    for (uint32_t id = sa.stop_lo; id < sa.stop_hi; id++)
-      if (id < sa.sem_lo || id > sa.sem_hi) g.extra[g.n_extra++] = (int)id;
+    head_rows(d, false, &g);
     SX_RC(gemv(g, EPI_STORE, s));
     SX_CU(launch_sample(sa, s->st));
   } else {
@@ -1241,6 +1327,10 @@ int run_frames(sx_session* s, int n, int n_frames, int mask_stop, bool sampled, 
   if (n < 1 || n > s->max_batch || n_frames < 0) {
     set_error("decode_greedy: bad batch or frame count");
     return SX_E_INVALID;
+  }
+  if (s->tp_failed) {
+    set_error("tensor-parallel session: an earlier residual exchange failed; reconnect the group and reset");
+    return SX_E_STATE;
   }
   int max_len = 0;
   for (int i = 0; i < n; i++) {

@@ -78,6 +78,7 @@ struct sx_session {
   void* tp_region = nullptr;
   size_t tp_region_bytes = 0;
   bool tp_connected = false;
+  bool tp_failed = false;  // an exchange timed out or saw a poison word: refuse until reconnect
   std::vector<void*> tp_opened;  // peers' regions opened on this device
   sx::TpComm tp;
   std::vector<int> len;  // host mirror of per-sequence cache lengths
@@ -94,6 +95,7 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
 int session_tp_handle(sx_session* s, void* out);
 int session_tp_connect(sx_session* s, const void* handles);
 int session_tp_disconnect(sx_session* s);
+int session_tp_set_timeout(sx_session* s, int64_t timeout_ns);
 int fill_kv_synthetic(sx_session* s, int seq, int len, uint64_t seed);
 // device-sampled frames of sequence 0 (after prefill): the reference drive loop's draws
 int decode_sample(sx_session* s, int n_frames, uint64_t seed, const sx_sampling_params* p, uint32_t* frames_out,
@@ -106,6 +108,8 @@ int sync_lengths(sx_session* s);
 
 // prefill one sequence; leaves its last residual in s->h[seq]
 int prefill_seq(sx_session* s, int seq, const uint32_t* prompt, int T);
+// prefill one sequence from caller-assembled input embeddings [T][dim] (host f32)
+int prefill_seq_embeds(sx_session* s, int seq, const float* embeds, int T);
 // one slow step for n sequences (frames on the host, [n][1+C]); seqs[i] owns row i of s->h
 int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n);
 // head over h rows [0, n): full logits to s->logits (if want_logits) and/or the greedy

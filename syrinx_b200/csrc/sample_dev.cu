@@ -251,13 +251,11 @@ cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {
   const int n = (int)(a.hi[0] - a.lo[0]) + (a.ranges > 1 ? (int)(a.hi[1] - a.lo[1]) : 0);
   if (n < 1 || n > kSampleMaxIds || a.ranges < 1 || a.ranges > 2) return cudaErrorInvalidValue;
   const size_t smem = sample_smem_bytes(n);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sample_smem_bytes(kSampleMaxIds));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  // the attribute belongs to the current device: set it on every launch (a host-side call,
+  // no device work), so sessions on several devices of one process all get it
+  cudaError_t e = cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sample_smem_bytes(kSampleMaxIds));
+  if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = launch_cfg(dim3(1), dim3(kThreadsS), smem, st, attr);
   return cudaLaunchKernelEx(&cfg, k_sample, a);

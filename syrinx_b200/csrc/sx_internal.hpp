@@ -39,6 +39,14 @@ constexpr int kMaxPrefillTok = 64;  // tokens per prefill chunk (max tokens per 
 constexpr int kAttnThreads = 256;  // 8 warps per attention CTA
 constexpr int kMaxCluster = 8;     // max splits of the attention key axis (one portable cluster)
 constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one CTA
+constexpr int kMaxStops = 256;    // stop ids; more than 4 only right next to the semantic range
+
+// The stop ids [stop_token_id, +num_stop_tokens) continue the semantic range (or end right
+// before it), so one widened row range covers both.
+inline bool stops_adjacent(const sx_model_desc& d) {
+  const uint64_t t0 = d.stop_token_id, t1 = t0 + (uint32_t)d.num_stop_tokens;
+  return t0 == (uint64_t)d.semantic_end_id + 1 || t1 == d.semantic_begin_id;
+}
 
 struct DevMat {
   int dtype = -1;
@@ -91,6 +99,7 @@ struct TpComm {
   uint32_t* slot_epochs = nullptr;    // this rank's per-slot exchange counters [xb_cap]
   int* err = nullptr;                 // this rank's device error flag (3: a peer did not arrive)
   int xb_cap = 0;                     // slots (tokens x rows) per (parity, source rank)
+  uint64_t wait_ns = 5000000000ull;   // longest wait for a peer's word (%globaltimer ns)
 };
 
 struct GemvArgs {

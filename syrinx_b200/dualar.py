@@ -114,6 +114,10 @@ class B200DualAr:
         (as if prefilled); a later prefill appends after them."""
         _lib.check(_lib.lib().sx_session_fill_kv_synthetic(self.handle, seq, length, seed))
 
+    def tp_set_timeout(self, timeout_ns: int) -> None:
+        """Longest wait of a residual exchange for a peer (ns); before the first decode loop."""
+        _lib.check(_lib.lib().sx_session_tp_set_timeout(self.handle, int(timeout_ns)))
+
     def tp_disconnect(self) -> None:
         """Unmap the peers (every rank, before any rank closes its session)."""
         _lib.check(_lib.lib().sx_session_tp_disconnect(self.handle))
@@ -239,6 +243,14 @@ class B200DualAr:
         t = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
         logits = np.empty(self.cfg.vocab_size, np.float32)
         _lib.check(_lib.lib().sx_lm_step_tokens(self.handle, _p(t, C.c_uint32), t.size, _p(logits, C.c_float)))
+        return logits
+
+    def lm_step_embeds(self, embeds: np.ndarray) -> np.ndarray:
+        """`Qwen2Lm::step_logits_cached(embeds)`: [t_new, dim] input embeddings through the
+        cached forward; the last position's logits."""
+        e = np.ascontiguousarray(embeds, dtype=np.float32).reshape(-1, self.cfg.slow.dim)
+        logits = np.empty(self.cfg.vocab_size, np.float32)
+        _lib.check(_lib.lib().sx_lm_step_embeds(self.handle, _p(e, C.c_float), e.shape[0], _p(logits, C.c_float)))
         return logits
 
     def set_stream(self, cuda_stream: int | None) -> None:

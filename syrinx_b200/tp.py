@@ -44,6 +44,17 @@ def connect(session, dist=None) -> None:
     session.tp_connect(handles)
 
 
+def reconnect(session, dist=None) -> None:
+    """Recover a group after a failed residual exchange (collective): every rank unmaps its
+    peers, the ranks meet, and the handle exchange runs again, which clears every rank's
+    exchange state before any rank can push into it. Reset and prefill afterwards."""
+    if dist is None:
+        import torch.distributed as dist
+    session.tp_disconnect()
+    dist.barrier()
+    connect(session, dist)
+
+
 def close(session, model, dist=None) -> None:
     """Tear down a tensor-parallel rank: every rank unmaps its peers before any rank frees
     its own exchange region (collective)."""

@@ -30,3 +30,8 @@ def kats():
 def quant_golden():
     import numpy as np
     return dict(np.load(os.path.join(ROOT, "tests", "golden", "quant_golden.npz")))
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return os.path.join(ROOT, "tests", "golden")

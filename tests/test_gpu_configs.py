@@ -1,12 +1,16 @@
 """Parity at the BASELINE configuration shapes (GPU vs the CPU oracle, through the C ABI),
-plus size-independent properties at full size where the oracle would take minutes.
+plus size-independent properties at full size.
 
   config 1  CosyVoice2-LM-shaped Qwen2, Q8_0, seed 0: prompt 128 ids, 64 greedy steps
             with the stop ids masked (min_len covering the run, cv2/sampling.rs:114-122)
   config 2  s1-mini-shaped dual-AR, Q8_0, seed 1: prompt 256, 128 greedy frames
-  config 3  Qwen3-4B-shaped dual-AR, Q8_0, seed 2: 64 greedy frames token-identical
-            (prompt shortened to 64 positions so the CPU oracle finishes in seconds)
-  config 4  the same architecture in Q4_K, batched utterances of different prompt lengths
+  config 3  Qwen3-4B-shaped dual-AR, Q8_0, seed 2: the BASELINE 512-token prompt (82 text ids
+            + 430 reference-voice positions), step-0 logits and 64 greedy frames against the
+            oracle run live on the host cores
+  config 4  the same architecture in Q4_K at full depth (36 + 4 layers): 8 utterances of
+            prompt lengths in [256, 1024] decoded as one batch of 8 on the paged cache, each
+            against its own oracle run (committed fixtures, tests/golden/config4_q4k.npz,
+            made by tests/golden/make_oracle_fixtures.py: minutes of CPU oracle time)
 """
 import numpy as np
 import pytest
@@ -64,16 +68,43 @@ def test_config2_s1_mini():
     assert_identical(frames, ofr, margins)
 
 
-def test_config3_qwen3_4b_64_frames():
+def test_config3_qwen3_4b_512_prompt_64_frames():
     cfg = sx.QWEN3_4B
-    prompt = dual_ar_prompt(cfg, 64, 54, seed=2)
-    frames, ofr, err0, margins = run_pair(cfg, SX_DTYPE_Q8_0, 2, prompt, 64, 192)
-    print(f"config3 step-0 logits max-abs {err0:.3e}, min margin {margins.min():.3e}")
+    prompt = dual_ar_prompt(cfg, 512, 430, seed=2)
+    frames, ofr, err0, margins = run_pair(cfg, SX_DTYPE_Q8_0, 2, prompt, 64, 600)
+    print(f"config3 (512-token prompt) step-0 logits max-abs {err0:.3e}, min margin {margins.min():.3e}")
     assert err0 <= 2e-2
     assert_identical(frames, ofr, margins)
 
 
-def test_config4_q4k_batched_vs_oracle():
+def test_config4_q4k_full_depth_batch8_vs_oracle(golden_dir):
+    import os
+    import sys
+    sys.path.insert(0, golden_dir)
+    from make_oracle_fixtures import CONFIG4_FRAMES, CONFIG4_SEED, config4_prompts
+
+    fx = np.load(os.path.join(golden_dir, "config4_q4k.npz"))
+    cfg = sx.QWEN3_4B
+    prompts = config4_prompts(cfg)
+    assert [p.shape[1] for p in prompts] == list(fx["lens"])
+    blob = sx.synth_blob(cfg, SX_DTYPE_Q4_K, seed=CONFIG4_SEED)
+    model = sx.Model(cfg, blob)
+    be = sx.B200DualAr(model, max_ctx=max(fx["lens"]) + CONFIG4_FRAMES + 8, max_batch=8)
+    st = be.prefill_batch(prompts)
+    got = be.decode_greedy_batch(8, CONFIG4_FRAMES, mask_stop=True)
+    lo, hi = cfg.semantic_begin_id, cfg.semantic_end_id
+    for i in range(8):
+        sem = np.concatenate([st.semantic_logits[i, lo:hi + 1], st.semantic_logits[i, cfg.stop_token_id:][:1]])
+        err = maxabs(sem, fx["logits0_semantic"][i])
+        print(f"config4 utterance {i} (T={fx['lens'][i]}): step-0 semantic logits max-abs {err:.3e}, "
+              f"min margin {fx['margins'][i].min():.3e}")
+        assert err <= 2e-2
+        assert_identical(got[i], fx["frames"][i], fx["margins"][i])
+    be.close()
+    model.close()
+
+
+def test_q4k_batched_shallow_vs_oracle():
     cfg = shrink(sx.QWEN3_4B, 6, 4, name="qwen3-4b-L6-q4k")
     blob = sx.synth_blob(cfg, SX_DTYPE_Q4_K, seed=3)
     model = sx.Model(cfg, blob)

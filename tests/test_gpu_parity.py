@@ -11,8 +11,8 @@ import pytest
 
 import syrinx_b200 as sx
 from syrinx_b200 import _lib
-from syrinx_b200.configs import SX_DTYPE_Q4_K, SX_DTYPE_Q8_0, TINY_S2
-from syrinx_b200.workloads import prompt_for
+from syrinx_b200.configs import SX_DTYPE_Q4_K, SX_DTYPE_Q8_0, TINY_S2, shrink
+from syrinx_b200.workloads import dual_ar_prompt, prompt_for
 from oracle import oracle as oc
 from tests.toy_lm import TOY_CFG, toy_blob
 
@@ -121,21 +121,46 @@ def test_greedy_decode_repeatable(tiny):
         be.close()
 
 
-def test_bf16_kv_within_tolerance(tiny):
-    cfg, model, om = tiny
-    prompt = prompt_for(cfg, 31, seed=9)
-    be = sx.B200DualAr(model, max_ctx=128, kv_dtype=sx.SX_DTYPE_BF16)
-    os_ = oc.OracleSession(om, 128, kv_bf16=True)
+def bf16_per_step(cfg, model, om, prompt, n):
+    """bf16 KV cache against the oracle rounding K/V to bf16 the same way: teacher-forced on
+    the oracle's own frames, the slow-step logits at every one of n steps within the
+    tolerance; then the free-running greedy token agreement, reported."""
+    be = sx.B200DualAr(model, max_ctx=prompt.shape[1] + n + 8, kv_dtype=sx.SX_DTYPE_BF16)
+    os_ = oc.OracleSession(om, prompt.shape[1] + n + 8, kv_bf16=True)
+    ofr, _ = os_.drive_greedy(prompt, n, mask_stop=True)
+    os_.reset()
     st = be.prefill(prompt)
     ol, _ = os_.prefill(prompt)
-    assert maxabs(st.semantic_logits, ol) <= LOGIT_TOL
-    frames = be.decode_greedy(32, mask_stop=True)
-    os_.reset()
-    ofr, _ = os_.drive_greedy(prompt, 32, mask_stop=True)
+    errs = [maxabs(st.semantic_logits, ol)]
+    pos = prompt.shape[1]
+    for f in range(n - 1):
+        st = be.slow_step(ofr[f], pos + f)
+        ol, _ = os_.slow_step(ofr[f])
+        errs.append(maxabs(st.semantic_logits, ol))
+    be.reset()
+    be.prefill(prompt)
+    frames = be.decode_greedy(n, mask_stop=True)
     agree = float(np.mean(frames == ofr))
-    print(f"bf16 KV: step-0 logits max-abs {maxabs(st.semantic_logits, ol):.2e}, token agreement {agree:.3f}")
-    assert np.array_equal(frames[:, 0][:1], ofr[:, 0][:1])
+    print(f"{cfg.name} bf16 KV: per-step logits max-abs {max(errs):.2e} over {len(errs)} steps, "
+          f"free-running token agreement {agree:.3f}")
     be.close()
+    return max(errs), agree
+
+
+def test_bf16_kv_per_step_logits(tiny):
+    cfg, model, om = tiny
+    err, agree = bf16_per_step(cfg, model, om, prompt_for(cfg, 31, seed=9), 64)
+    assert err <= LOGIT_TOL
+
+
+def test_bf16_kv_per_step_logits_4b_shape():
+    cfg = shrink(sx.QWEN3_4B, 4, 2, name="qwen3-4b-L4")
+    blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=21)
+    model = sx.Model(cfg, blob)
+    om = oc.OracleModel(cfg, blob)
+    err, agree = bf16_per_step(cfg, model, om, dual_ar_prompt(cfg, 96, 80, seed=21), 64)
+    model.close()
+    assert err <= LOGIT_TOL
 
 
 def test_frame_step_and_drive_agree_with_graph_loop(tiny):

@@ -1,8 +1,9 @@
 """The device sampler (sx_decode_sample) against the host-sampled driver loop (sx_drive, the
-restatement of the reference `drive` with `Sampler`): same prompt, seed and parameters give
-the same residual codes, the same frame count and the same stop, over several parameter
-sets (top-k / top-p / temperature / RAS window), on the tiny dual-AR and on a 2-layer
-Qwen3-4B-width model (4096 + 1 allowed semantic ids, 4096 codes)."""
+restatement of the reference `drive` with `Sampler`) and against the CPU oracle's own
+`oc_drive` (the reference `drive` + `Sampler` over the oracle's logits): same prompt, seed
+and parameters give the same residual codes, the same frame count and the same stop, over
+several parameter sets (top-k / top-p / temperature / RAS window), on the tiny dual-AR and
+on a 2-layer Qwen3-4B-width model (4096 + 1 allowed semantic ids, 4096 codes)."""
 import ctypes as C
 
 import numpy as np
@@ -12,6 +13,7 @@ import syrinx_b200 as sx
 from syrinx_b200 import _lib
 from syrinx_b200.configs import SX_DTYPE_Q8_0, TINY_S2, shrink
 from syrinx_b200.workloads import dual_ar_prompt, prompt_for
+from oracle import oracle as oc
 
 pytestmark = pytest.mark.gpu
 
@@ -57,3 +59,31 @@ def test_device_sampler_matches_host_drive_tiny():
 def test_device_sampler_matches_host_drive_4b_width():
     cfg = shrink(sx.QWEN3_4B, 2, 1, name="qwen3-4b-L2")
     check(cfg, 17, dual_ar_prompt(cfg, 24, 18, seed=17), 32)
+
+
+def check_oracle(cfg, blob_seed, prompt, n):
+    blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=blob_seed)
+    model = sx.Model(cfg, blob)
+    max_ctx = prompt.shape[-1] + n + 8
+    be = sx.B200DualAr(model, max_ctx=max_ctx)
+    om = oc.OracleModel(cfg, blob)
+    osess = oc.OracleSession(om, max_ctx, kv_bf16=False)
+    for seed, params in PARAMS:
+        ref = osess.drive(prompt, n, seed, params.to_c())
+        be.reset()
+        be.prefill(prompt)
+        frames = be.decode_sample(n, seed, params)
+        assert frames.shape[0] == ref.shape[1], (seed, frames.shape, ref.shape)
+        bad = np.argwhere(frames[:, 1:].T != ref)
+        assert bad.size == 0, f"seed {seed}: first mismatch (codebook, frame) {bad[0]}"
+    be.close()
+    model.close()
+
+
+def test_device_sampler_matches_oracle_drive_tiny():
+    check_oracle(TINY_S2, 13, prompt_for(TINY_S2, 20, seed=13), 48)
+
+
+def test_device_sampler_matches_oracle_drive_4b_width():
+    cfg = shrink(sx.QWEN3_4B, 2, 1, name="qwen3-4b-L2")
+    check_oracle(cfg, 17, dual_ar_prompt(cfg, 24, 18, seed=17), 32)

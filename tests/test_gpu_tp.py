@@ -2,6 +2,8 @@
 per GPU, against the CPU oracle: step-0 logits within 2e-2 and 32 greedy frames
 token-identical on both ranks. The residual merges after wo and w2 exchange rows over NVLink
 inside the library; the ranks meet on the host only for the handle exchange (gloo).
+A second test makes one rank skip a decode call and checks the bounded wait, the poison
+words, the refusal to decode afterwards and the recovery by reconnecting.
 Skipped when fewer than two GPUs are visible."""
 import datetime
 import os
@@ -15,8 +17,8 @@ import torch.multiprocessing as mp
 
 import syrinx_b200 as sx
 from syrinx_b200 import tp
-from syrinx_b200.configs import SX_DTYPE_Q8_0
-from syrinx_b200.workloads import dual_ar_prompt
+from syrinx_b200.configs import SX_DTYPE_Q8_0, TINY_S2
+from syrinx_b200.workloads import dual_ar_prompt, prompt_for
 from oracle import oracle as oc
 
 pytestmark = pytest.mark.gpu
@@ -83,3 +85,87 @@ def test_tp2_config5_matches_oracle():
     assert err0 <= 2e-2
     bad = np.argwhere(f0 != ofr)
     assert bad.size == 0, f"first mismatch frame {bad[0]}, semantic top-2 margin {margins[bad[0][0]]:.2e}"
+
+
+TIMEOUT_NS = 300_000_000  # 0.3 s of the GPU's global timer
+
+
+def timeout_worker(rank, world, port, q):
+    """Rank 1 skips one decode call between steps (no kernel in flight); rank 0's residual
+    exchange must give up after the short limit with SX_E_DEVICE, rank 1's next call must
+    fail on rank 0's poison words, both sessions must then refuse to decode, and a reconnect
+    must bring back the same frames as before."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180))
+    out = {}
+    try:
+        import time
+
+        cfg = TINY_S2
+        blob = sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=13)
+        model = sx.Model(cfg, blob, device=rank, tp_rank=rank, tp_size=world)
+        be = sx.B200DualAr(model, max_ctx=96)
+        be.tp_set_timeout(TIMEOUT_NS)
+        tp.connect(be, dist)
+        prompt = prompt_for(cfg, 20, seed=13)
+        be.prefill(prompt)
+        out["first"] = be.decode_greedy(3, mask_stop=True)
+        dist.barrier()
+        # rank 1 skips this call; rank 0 waits at most the limit, then fails
+        if rank == 0:
+            t0 = time.time()
+            try:
+                be.decode_greedy(2, mask_stop=True)
+                out["lost_peer"] = ("ok", 0.0)
+            except sx.SyrinxError as e:
+                out["lost_peer"] = (e.code, time.time() - t0)
+        dist.barrier()
+        if rank == 1:
+            t0 = time.time()
+            try:
+                be.decode_greedy(2, mask_stop=True)
+                out["late_peer"] = ("ok", 0.0)
+            except sx.SyrinxError as e:
+                out["late_peer"] = (e.code, time.time() - t0)
+        dist.barrier()
+        try:
+            be.decode_greedy(1, mask_stop=True)
+            out["after"] = "ok"
+        except sx.SyrinxError as e:
+            out["after"] = e.code
+        dist.barrier()
+        tp.reconnect(be, dist)
+        be.reset()
+        be.prefill(prompt)
+        out["again"] = be.decode_greedy(3, mask_stop=True)
+        tp.close(be, model, dist)
+        q.put((rank, out, None))
+    except Exception as e:
+        q.put((rank, out, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp2_lost_peer_times_out_and_recovers():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=timeout_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=600) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+    for rank, _, err in res:
+        assert err is None, f"rank {rank}: {err}"
+    (_, o0, _), (_, o1, _) = res
+    print(f"lost peer: rank 0 {o0['lost_peer']}; late peer: rank 1 {o1['late_peer']}")
+    code, secs = o0["lost_peer"]
+    assert code == -8 and secs < 10.0  # SX_E_DEVICE after the 0.3 s limit, not a hang
+    code, secs = o1["late_peer"]
+    assert code == -8 and secs < 10.0  # the late rank reads poison (or times out): no stale value
+    assert o0["after"] == -5 and o1["after"] == -5  # SX_E_STATE until the group reconnects
+    assert np.array_equal(o0["first"], o1["first"])
+    assert np.array_equal(o0["again"], o0["first"]) and np.array_equal(o1["again"], o1["first"])
