@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <cstdlib>
 
 #include "sx_internal.hpp"
 
@@ -287,6 +288,33 @@ int upload_inv_freq(sx_model* m, const sx_transformer_desc& td, float** out) {
   return SX_OK;
 }
 
+// The persistent decode kernel's per-layer records: only for stacks whose four matrices are
+// all Q8_0 tile records.
+int upload_stack(sx_model* m, const std::vector<DevLayer>& layers, StackLayer** out) {
+  *out = nullptr;
+  if (layers.empty()) return SX_OK;
+  std::vector<StackLayer> h;
+  for (const DevLayer& L : layers) {
+    for (const DevMat* w : {&L.wqkv, &L.wo, &L.w13, &L.w2})
+      if (w->dtype != SX_DTYPE_Q8_0) return SX_OK;
+    StackLayer s;
+    s.wqkv = (const uint8_t*)L.wqkv.q;
+    s.wo = (const uint8_t*)L.wo.q;
+    s.w13 = (const uint8_t*)L.w13.q;
+    s.w2 = (const uint8_t*)L.w2.q;
+    s.attn_norm = L.attn_norm;
+    s.bqkv = L.bqkv;
+    s.qn = L.qn;
+    s.kn = L.kn;
+    s.bo = L.bo;
+    s.ffn_norm = L.ffn_norm;
+    h.push_back(s);
+  }
+  SX_RC(dalloc(m->allocs, out, h.size()));
+  SX_CU(cudaMemcpy(*out, h.data(), h.size() * sizeof(StackLayer), cudaMemcpyHostToDevice));
+  return SX_OK;
+}
+
 }  // namespace
 
 // A transformer stack divides over tp ranks when its heads, kv heads and FFN rows do, and
@@ -386,6 +414,10 @@ int model_create(const sx_model_desc* desc, const void* blob, size_t size, int d
   }
   if ((rc = upload_inv_freq(m, d.slow, &m->inv_slow))) return fail(rc);
   if (d.fast.n_layer > 0 && (rc = upload_inv_freq(m, d.fast, &m->inv_fast))) return fail(rc);
+  if (tp_size == 1) {
+    if ((rc = upload_stack(m, m->slow, &m->slow_stack))) return fail(rc);
+    if ((rc = upload_stack(m, m->fast, &m->fast_stack))) return fail(rc);
+  }
   // every later use sees this rank's geometry
   for (sx_transformer_desc* t : {&m->d.slow, &m->d.fast}) {
     t->n_head /= tp_size;
@@ -502,6 +534,18 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
     for (const DevMat* w : {&m->emb, &m->cb_emb, &m->out_w, &m->fast_out, &m->fast_emb}) need(*w, kMaxTok);
     s->q8_part_cap = cap;
     if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
+  }
+  {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
+    const int hd_max = std::max(sl.head_dim, has_fast ? d.fast.head_dim : 0);
+    if ((rc = dalloc(s->allocs, &s->stack_xb, (size_t)max_batch * dim)) ||
+        (rc = dalloc(s->allocs, &s->stack_attn, stack_attn_part_floats(sms, hd_max))) ||
+        (rc = dalloc(s->allocs, &s->stack_ss, (size_t)2 * kMaxTok * 64)) || (rc = dalloc(s->allocs, &s->stack_bar, 1)))
+      return fail(rc);
+    if (cudaMemset(s->stack_bar, 0, 8) != cudaSuccess) return fail(SX_E_CUDA);
+    const char* env = getenv("SYRINX_STACK");
+    s->stack_enabled = !(env && env[0] == '0');
   }
   if (m->tp_size > 1) {
     // receive region rx [2][kMaxTp][xb_cap] 8-byte words; peers map it by IPC
@@ -692,9 +736,88 @@ int gemv(GemvArgs a, Epi epi, sx_session* s) {
   return SX_OK;
 }
 
+int num_sms_of(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  if (device >= 0 && device < 64) cached[device] = n;
+  return n;
+}
+
+// The persistent decode kernel for a whole stack (stack.cu), when the stack and the launch
+// qualify: Q8_0 matrices, decode (each token appends its own K/V), M <= 8, one GPU.
+// Returns 1 when it launched, 0 when the caller should run the per-kernel chain.
+int try_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos, int const_pos,
+              bool append) {
+  sx_model* m = s->m;
+  const StackLayer* layers = fast ? m->fast_stack : m->slow_stack;
+  if (!s->stack_enabled || !layers || !append || M > kMaxTok || m->tp_size > 1) return 0;
+  const sx_transformer_desc& td = fast ? m->d.fast : m->d.slow;
+  const int sms = num_sms_of(m->device);
+  StackArgs a;
+  a.layers = layers;
+  a.n_layer = td.n_layer;
+  a.dim = td.dim;
+  a.H = td.n_head;
+  a.Hkv = td.n_local_heads;
+  a.hd = td.head_dim;
+  a.F = td.intermediate_size;
+  a.eps = td.norm_eps;
+  a.inv_freq = fast ? m->inv_fast : m->inv_slow;
+  a.interleaved = td.rope_interleaved;
+  a.scale = (float)(1.0 / std::sqrt((double)td.head_dim));
+  a.kv = fast ? s->fkv : s->kv;
+  a.kv_layer_elems = fast ? s->fkv_layer_elems : s->kv_layer_elems;
+  a.kv_f32 = s->kv_f32;
+  a.page_table = fast ? s->fpage_table : s->page_table;
+  a.pt_stride = fast ? 1 : s->pages_per_seq;
+  a.tok_seq = tok_seq;
+  a.tok_pos = tok_pos;
+  a.const_pos = const_pos;
+  a.M = M;
+  const int ctx = fast ? std::max(1, m->d.num_codebooks) : s->max_ctx;
+  a.n_split = std::max(1, std::min(stack_max_splits(sms, M, a.Hkv), (ctx + 31) / 32));
+  a.x = resid;
+  a.xb = s->stack_xb;
+  auto geo = [](int64_t rows, int64_t cols) {
+    StackGeo g;
+    g.K = (int)cols;
+    g.nb = (int)(cols / 32);
+    g.nc = (g.nb + 7) / 8;
+    g.n_vt = (int)q8_tiles(rows);
+    return g;
+  };
+  a.geo[0] = geo((int64_t)(a.H + 2 * a.Hkv) * a.hd, a.dim);
+  a.geo[1] = geo(a.dim, (int64_t)a.H * a.hd);
+  a.geo[2] = geo((int64_t)2 * a.F, a.dim);
+  a.geo[3] = geo(a.dim, a.F);
+  a.nc_dim = a.geo[0].nc;
+  int mt = 1;
+  while (mt < M) mt <<= 1;
+  size_t need = 0;
+  for (int i = 0; i < 4; i++) need = std::max(need, (size_t)a.geo[i].n_vt * a.geo[i].nc * mt * 16);
+  if (2 * need > s->q8_part_cap || !stack_supported(a, sms)) return 0;
+  a.part0 = s->q8_part;
+  a.part1 = s->q8_part + need;
+  a.attn_part = s->stack_attn;
+  a.ss = s->stack_ss;
+  a.bar = s->stack_bar;
+  a.err = s->err;
+  cudaError_t e = launch_stack(a, sms, s->st);
+  if (e != cudaSuccess) {
+    set_error(std::string("persistent decode stack: ") + cudaGetErrorString(e));
+    return -1;
+  }
+  return 1;
+}
+
 // One transformer stack over M tokens. resid [M][dim] is updated in place.
 int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos,
               int const_pos, bool append) {
+  const int ts = try_stack(s, fast, M, resid, tok_seq, tok_pos, const_pos, append);
+  if (ts < 0) return SX_E_CUDA;
+  if (ts > 0) return SX_OK;
   sx_model* m = s->m;
   const sx_transformer_desc& td = fast ? m->d.fast : m->d.slow;
   const std::vector<DevLayer>& layers = fast ? m->fast : m->slow;

@@ -23,6 +23,10 @@ struct sx_model {
   // tensor parallelism: this model holds rank tp_rank's shard of tp_size; d holds the
   // per-rank geometry (n_head, n_local_heads, intermediate_size divided by tp_size)
   int tp_rank = 0, tp_size = 1;
+  // the persistent decode stack's per-layer records (device arrays; null when a stack has a
+  // matrix that is not Q8_0, which then runs the per-kernel chain)
+  sx::StackLayer* slow_stack = nullptr;
+  sx::StackLayer* fast_stack = nullptr;
 };
 
 struct GreedyGraph {
@@ -73,6 +77,13 @@ struct sx_session {
   sx_sampling_params* dparams = nullptr;  // device copy of the sampling parameters
   float* q8_part = nullptr;  // Q8_0 GEMV partial sums [tile][k-chunk][token][16]
   size_t q8_part_cap = 0;    // floats
+  // persistent decode stack scratch: the residual's second buffer, attention split partials,
+  // per-chunk sums of squares and the grid barrier counter
+  float* stack_xb = nullptr;
+  float* stack_attn = nullptr;
+  float* stack_ss = nullptr;
+  unsigned long long* stack_bar = nullptr;
+  bool stack_enabled = true;  // SYRINX_STACK=0 selects the per-kernel chain (for comparison)
   // tensor parallelism: the receive region (rx [2][kMaxTp][xb_cap] 8-byte words) peers map
   // through CUDA IPC, and the communicator the residual merges use
   void* tp_region = nullptr;

@@ -158,6 +158,58 @@ cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st);
 
+// ---- persistent decode stack (stack.cu) ------------------------------------------------
+// One layer's Q8_0 tile records and vectors, as the persistent kernel reads them (device array).
+struct StackLayer {
+  const uint8_t* wqkv = nullptr;
+  const uint8_t* wo = nullptr;
+  const uint8_t* w13 = nullptr;
+  const uint8_t* w2 = nullptr;
+  const float* attn_norm = nullptr;
+  const float* bqkv = nullptr;
+  const float* qn = nullptr;
+  const float* kn = nullptr;
+  const float* bo = nullptr;
+  const float* ffn_norm = nullptr;
+};
+struct StackGeo {
+  int K = 0, nb = 0, nc = 0, n_vt = 0;  // columns, 32-wide blocks, 8-block k chunks, 16-row tiles
+};
+struct StackArgs {
+  const StackLayer* layers = nullptr;  // device [n_layer]
+  int n_layer = 0;
+  int dim = 0, H = 0, Hkv = 0, hd = 0, F = 0;
+  float eps = 0.f;
+  const float* inv_freq = nullptr;
+  int interleaved = 1;
+  float scale = 1.f;
+  uint8_t* kv = nullptr;  // layer l's K pages at kv + l * kv_layer_elems * elem, V half after
+  size_t kv_layer_elems = 0;
+  int kv_f32 = 1;
+  const int* page_table = nullptr;
+  int pt_stride = 0;
+  const int* tok_seq = nullptr;
+  const int* tok_pos = nullptr;  // null: every token at const_pos
+  int const_pos = 0;
+  int M = 1;        // tokens (1..8)
+  int n_split = 1;  // splits of the key axis per (token, kv head)
+  float* x = nullptr;   // [M][dim] residual stream, updated in place
+  float* xb = nullptr;  // [M][dim] scratch
+  float* part0 = nullptr;  // GEMV partials, two alternating buffers
+  float* part1 = nullptr;
+  float* attn_part = nullptr;  // [units][kMaxGroup][hd + 2]
+  float* ss = nullptr;         // sums of squares per k chunk [2][8][64]
+  unsigned long long* bar = nullptr;  // grid barrier counter (monotonic)
+  int* err = nullptr;
+  StackGeo geo[4];  // wqkv, wo, w1|w3, w2
+  int nc_dim = 0;   // k chunks of dim
+  int nslot = 0;    // ring slots (set by the launcher)
+};
+bool stack_supported(const StackArgs& a, int sms);
+size_t stack_attn_part_floats(int sms, int hd);
+int stack_max_splits(int sms, int M, int Hkv);
+cudaError_t launch_stack(const StackArgs& a, int sms, cudaStream_t st);
+
 struct EmbedArgs {
   const int* tok_seq = nullptr;
   const uint32_t* frames = nullptr;  // [batch][1+C] per-sequence current frame
