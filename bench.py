@@ -102,18 +102,19 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def kernels_per_frame(cfg) -> int:
+def kernels_per_frame(cfg, stack: bool = True) -> int:
     """Kernel launches in one greedy frame graph (mirrors the sequence in model.cu). A Q8_0
-    GEMV is two launches: k_gemv_q8 and its k_merge_q8."""
+    GEMV is two launches: k_gemv_q8 and its k_merge_q8. With the persistent decode kernel a
+    whole stack (36 slow layers, or the 4 fast layers of one codebook step) is one launch."""
     gemv = 2
     per_layer = 4 * gemv + 1  # wqkv, wo, w1|w3, w2 + attention
     n = gemv + 1  # semantic head, take_semantic
     if cfg.has_fast:
         C = cfg.num_codebooks
-        n += C * cfg.fast.n_layer * per_layer  # fast steps 0..C-1
+        n += C * (1 if stack else cfg.fast.n_layer * per_layer)  # fast steps 0..C-1
         n += 1  # code-0 embedding (take_code)
         n += (C - 1) * (gemv + 1)  # fast head + take_code
-    n += 1 + cfg.slow.n_layer * per_layer + 1  # embed, slow stack, advance
+    n += 1 + (1 if stack else cfg.slow.n_layer * per_layer) + 1  # embed, slow stack, advance
     return n
 
 
@@ -264,7 +265,7 @@ def bench_device(args):
         "e2e": {"value": round(K_e2e * world / (ms_e2e * 1e-3), 2), "unit": "frames/s",
                 "h2d_bytes_per_step": int(cfg.frame_width * 4), "d2h_bytes_per_step": int(cfg.frame_width * 4),
                 "api": "sx_frame_step_greedy (host frame in, host frame out, per frame)"},
-        "gpu_launches": kernels_per_frame(cfg) * K,
+        "gpu_launches": kernels_per_frame(cfg, os.environ.get("SYRINX_STACK", "1") != "0") * K,
         "clocks": clk.summary(),
         "load_s": round(t_load, 1),
         "prefill_s": round(t_prefill, 3),

@@ -41,6 +41,7 @@ SIGNATURES = {
     "sx_session_len": (C.c_int, [C.c_void_p, C.c_int32, _i32p]),
     "sx_session_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sx_profile_gemv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
+    "sx_profile_stack": (C.c_int, [C.c_void_p, C.c_int32, _f32p]),
     "sx_prefill": (C.c_int, [C.c_void_p, _u32p, C.c_int32, _f32p, _f32p]),
     "sx_slow_step": (C.c_int, [C.c_void_p, _u32p, C.c_int32, _f32p, _f32p]),
     "sx_first_code": (C.c_uint32, [C.c_void_p, C.c_uint32]),

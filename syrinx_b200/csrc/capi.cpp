@@ -262,6 +262,18 @@ int sx_profile_gemv(sx_session* s, int32_t kind, int32_t n_launches) {
   })
 }
 
+int sx_profile_stack(sx_session* s, int32_t fast, float* phase_us_out) {
+  SX_GUARD({
+    int rc = need_session(s);
+    if (rc) return rc;
+    if (!phase_us_out) {
+      set_error("null output");
+      return SX_E_INVALID;
+    }
+    return profile_stack(s, fast, phase_us_out);
+  })
+}
+
 int sx_prefill(sx_session* s, const uint32_t* prompt, int32_t T, float* logits_out, float* hidden_out) {
   SX_GUARD({
     int rc = need_session(s);

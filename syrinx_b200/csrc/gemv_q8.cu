@@ -390,9 +390,18 @@ cudaError_t launch_merge(const GemvArgs& a, const Q8Geo& g, cudaStream_t st) {
 }
 
 template <int M>
+cudaError_t launch_epilogue(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st);
+
+template <int M>
 cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st) {
   constexpr int NP = (M + 1) / 2;
   static const int sms = num_sms();
+  if (M >= 16 && tc_enabled() && a.n_extra == 0 && g.t_first == 0) {
+    // prefill chunks: the same partials from the tensor-core GEMM
+    cudaError_t e = launch_gemm_tc(a, M, g.K, g.nb, g.nc, g.t_first, g.n_vt, sms, st);
+    if (e != cudaSuccess) return e;
+    return launch_epilogue<M>(a, epi, g, st);
+  }
   auto kern = k_gemv_q8<M>;
   const long long I = (long long)g.n_vt * g.nc;
   // persistent grid of up to three CTAs per SM; shared memory holds the limbs of the
@@ -419,6 +428,13 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
   cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kThreads), smem, st, attr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, g);
   if (e != cudaSuccess) return e;
+  return launch_epilogue<M>(a, epi, g, st);
+}
+
+// The merge of the partials with the epilogue (or the tensor-parallel exchange).
+template <int M>
+cudaError_t launch_epilogue(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st) {
+  static const int sms = num_sms();
   if (epi == EPI_ADD && a.tp.size > 1) {
     // no more CTAs than can be resident at once (at most four per SM by the launch bounds),
     // so every CTA of the exchange is co-resident once the GEMV drains

@@ -716,6 +716,7 @@ int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
 int gemv(GemvArgs a, Epi epi, sx_session* s) {
   a.part = s->q8_part;
   a.part_cap = s->q8_part_cap;
+  a.err = s->err;
   if (epi == EPI_ADD && s->m->tp_size > 1) {
     if (!s->tp_connected) {
       set_error("tensor-parallel session: call sx_session_tp_connect before decoding");
@@ -748,11 +749,11 @@ int num_sms_of(int device) {
 // The persistent decode kernel for a whole stack (stack.cu), when the stack and the launch
 // qualify: Q8_0 matrices, decode (each token appends its own K/V), M <= 8, one GPU.
 // Returns 1 when it launched, 0 when the caller should run the per-kernel chain.
-int try_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos, int const_pos,
-              bool append) {
+bool stack_args(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos,
+                int const_pos, StackArgs* out) {
   sx_model* m = s->m;
   const StackLayer* layers = fast ? m->fast_stack : m->slow_stack;
-  if (!s->stack_enabled || !layers || !append || M > kMaxTok || m->tp_size > 1) return 0;
+  if (!layers || M > kMaxTok || m->tp_size > 1) return false;
   const sx_transformer_desc& td = fast ? m->d.fast : m->d.slow;
   const int sms = num_sms_of(m->device);
   StackArgs a;
@@ -797,14 +798,23 @@ int try_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
   while (mt < M) mt <<= 1;
   size_t need = 0;
   for (int i = 0; i < 4; i++) need = std::max(need, (size_t)a.geo[i].n_vt * a.geo[i].nc * mt * 16);
-  if (2 * need > s->q8_part_cap || !stack_supported(a, sms)) return 0;
+  if (2 * need > s->q8_part_cap || !stack_supported(a, sms)) return false;
   a.part0 = s->q8_part;
   a.part1 = s->q8_part + need;
   a.attn_part = s->stack_attn;
   a.ss = s->stack_ss;
   a.bar = s->stack_bar;
   a.err = s->err;
-  cudaError_t e = launch_stack(a, sms, s->st);
+  *out = a;
+  return true;
+}
+
+int try_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos, int const_pos,
+              bool append) {
+  if (!s->stack_enabled || !append) return 0;
+  StackArgs a;
+  if (!stack_args(s, fast, M, resid, tok_seq, tok_pos, const_pos, &a)) return 0;
+  cudaError_t e = launch_stack(a, num_sms_of(s->m->device), s->st);
   if (e != cudaSuccess) {
     set_error(std::string("persistent decode stack: ") + cudaGetErrorString(e));
     return -1;
@@ -1555,6 +1565,50 @@ int profile_gemv(sx_session* s, int kind, int n_launches) {
     SX_RC(gemv(g, epi, s));
   }
   return SX_OK;
+}
+
+// One launch of the persistent stack for sequence 0 at its current position with the phase
+// trace on. out[0] total us; out[1..5] mean us of phases P1..P5 (CTA 0, phase start to the next
+// phase start, averaged over the layers); out[6] the final phase; out[7] setup before P1.
+int profile_stack(sx_session* s, int fast, float* out) {
+  if (s->len[0] <= 0) {
+    set_error("profile_stack: prefill first");
+    return SX_E_STATE;
+  }
+  const std::vector<int> ts{0}, tp{s->len[0]};
+  SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+  StackArgs a;
+  float* resid = fast ? s->fx : s->h;
+  if (!stack_args(s, fast != 0, 1, resid, s->tok_seq, fast ? nullptr : s->tok_pos, 0, &a)) {
+    set_error("profile_stack: this stack does not run on the persistent kernel");
+    return SX_E_UNSUPPORTED;
+  }
+  const int sms = num_sms_of(s->m->device);
+  const size_t per = (size_t)a.n_layer * 5 + 3;
+  unsigned long long* tr = nullptr;
+  SX_CU(cudaMalloc((void**)&tr, per * sms * 8));
+  a.trace = tr;
+  cudaError_t e = launch_stack(a, sms, s->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+  std::vector<unsigned long long> h(per * sms);
+  if (e == cudaSuccess) e = cudaMemcpy(h.data(), tr, h.size() * 8, cudaMemcpyDeviceToHost);
+  cudaFree(tr);
+  if (e != cudaSuccess) {
+    set_error(std::string("profile_stack: ") + cudaGetErrorString(e));
+    return SX_E_CUDA;
+  }
+  const unsigned long long* t = h.data();  // CTA 0
+  const int L = a.n_layer;
+  for (int i = 0; i < 8; i++) out[i] = 0.f;
+  out[0] = (float)((t[2 + L * 5] - t[0]) * 1e-3);
+  for (int l = 0; l < L; l++)
+    for (int p = 0; p < 5; p++) {
+      const unsigned long long t0 = t[1 + l * 5 + p], t1 = t[1 + l * 5 + p + 1];
+      out[1 + p] += (float)((t1 - t0) * 1e-3) / L;
+    }
+  out[6] = (float)((t[2 + L * 5] - t[1 + L * 5]) * 1e-3);
+  out[7] = (float)((t[1] - t[0]) * 1e-3);
+  return check_err(s);
 }
 
 int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, uint32_t* frame_out, int* stopped) {

@@ -133,6 +133,7 @@ int fast_expand_rows(sx_session* s, int n, const int* seqs, bool sampled = false
 int fast_expand_sampled(sx_session* s, uint32_t first_code, sx_sample_fn fn, void* user,
                         uint32_t* codes_out);
 int profile_gemv(sx_session* s, int kind, int n_launches);
+int profile_stack(sx_session* s, int fast, float* out);
 int decode_greedy(sx_session* s, int n, int n_frames, int mask_stop, uint32_t* frames_out,
                   int* n_frames_out);
 int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, uint32_t* frame_out,

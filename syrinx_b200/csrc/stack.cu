@@ -185,13 +185,13 @@ __device__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t* full, uint64
   constexpr int NP = Smem<MT>::NP;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bl = MT == 1 ? (lane & 15) : lane;
-  const long long n = c1 - c0;
-  for (long long j = warp; j < n; j += kCW) {
-    const long long it = c0 + j;
-    const int kc = (int)(it / g.n_vt), vt = (int)(it % g.n_vt);
-    const long long gi = ctr + j;
-    const int slot = (int)(gi % nslot);
-    const uint32_t par = (uint32_t)((gi / nslot) & 1);
+  const int n = (int)(c1 - c0);
+  // this warp's items j = warp, warp + 8, ...: (k chunk, tile) and (slot, round) advance
+  // incrementally, no division per item
+  int kc = (int)((c0 + warp) / g.n_vt), vt = (int)((c0 + warp) % g.n_vt);
+  int slot = (int)((ctr + warp) % nslot), round = (int)((ctr + warp) / nslot);
+  for (int j = warp; j < n; j += kCW) {
+    const uint32_t par = (uint32_t)(round & 1);
     mbar_wait_bounded(&full[slot], par, err);
     const uint8_t* rec = ring + (size_t)slot * kItemBytes;
     float acc[NP][2];
@@ -232,6 +232,10 @@ __device__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t* full, uint64
         __stcg(P + tok * 16 + (lane >> 2) + 8, v1);
       }
     }
+    slot += kCW;
+    if (slot >= nslot) slot -= nslot, round++;
+    vt += kCW;
+    while (vt >= g.n_vt) vt -= g.n_vt, kc++;
   }
   (void)M;
   ctr += n;
@@ -612,7 +616,8 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
   if (threadIdx.x >= kCT) {
     // ---- producer: one lane streams every item of every layer in consumption order ----
     if (threadIdx.x != kCT) return;
-    long long ctr = 0;
+    // incremental slot / round / (k chunk, tile) counters: no division per item
+    int slot = 0, round = 0;
     for (int l = 0; l < a.n_layer; l++) {
       const StackLayer& L = a.layers[l];
       const uint8_t* W[4] = {L.wqkv, L.wo, L.w13, L.w2};
@@ -620,15 +625,16 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
         const MatGeo& g = G4[mi];
         long long c0, c1;
         cta_items(g.n_vt, g.nc, &c0, &c1);
-        for (long long it = c0; it < c1; it++, ctr++) {
-          const int kc = (int)(it / g.n_vt), vt = (int)(it % g.n_vt);
-          const int slot = (int)(ctr % nslot);
-          if (ctr >= nslot) mbar_wait_bounded(&empty[slot], (uint32_t)(((ctr / nslot) - 1) & 1), a.err);
+        int kc = (int)(c0 / g.n_vt), vt = (int)(c0 % g.n_vt);
+        for (int n = (int)(c1 - c0); n > 0; n--) {
+          if (round > 0) mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), a.err);
           const int nrec = min(kIB, g.nb - kc * kIB);
           const uint32_t bytes = (uint32_t)nrec * kQ8Rec;
           mbar_arrive_expect_tx(&full[slot], bytes);
           bulk_g2s(ring + (size_t)slot * kItemBytes, W[mi] + ((size_t)vt * g.nb + (size_t)kc * kIB) * kQ8Rec, bytes,
                    &full[slot]);
+          if (++slot == nslot) slot = 0, round++;
+          if (++vt == g.n_vt) vt = 0, kc++;
         }
       }
     }
@@ -636,6 +642,9 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
   }
 
   // ---- consumers ----
+  // optional phase trace: thread 0 of each CTA stamps %globaltimer at every phase start
+  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * (a.n_layer * 5 + 3) : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = global_ns();
   long long ctr = 0;
   float* xa = a.x;   // the residual stream (in / out)
   float* xb = a.xb;  // the other buffer of the two a residual update alternates between
@@ -646,6 +655,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     int b_lo, b_hi, kc_lo, kc_hi;
     // P1: wqkv (x += previous layer's w2 partials)
     if (l > 0) grid_wait(a, target);
+    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 0] = global_ns();
     cta_items(G4[0].n_vt, G4[0].nc, &c0, &c1);
     resid_prologue<MT>(sm, a, G4[0], c0, c1, xa, xb, l > 0 ? a.part1 : nullptr, G4[3].nc, nullptr, L.attn_norm,
                        a.ss);
@@ -654,10 +664,12 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     target = grid_arrive(a);
     // P2: attention
     grid_wait(a, target);
+    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 1] = global_ns();
     attention_unit<MT, HD, KT>(am, a, L, l, a.part0, G4[0].nc);
     target = grid_arrive(a);
     // P3: wo
     grid_wait(a, target);
+    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 2] = global_ns();
     cta_items(G4[1].n_vt, G4[1].nc, &c0, &c1);
     attn_out_prologue<MT>(sm, a, G4[1], c0, c1);
     k_range(G4[1], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
@@ -665,6 +677,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     target = grid_arrive(a);
     // P4: w1|w3 (x += wo partials + bias)
     grid_wait(a, target);
+    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 3] = global_ns();
     cta_items(G4[2].n_vt, G4[2].nc, &c0, &c1);
     resid_prologue<MT>(sm, a, G4[2], c0, c1, xb, xa, a.part1, G4[1].nc, L.bo, L.ffn_norm, a.ss + (size_t)64 * MT);
     k_range(G4[2], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
@@ -672,6 +685,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     target = grid_arrive(a);
     // P5: w2
     grid_wait(a, target);
+    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 4] = global_ns();
     cta_items(G4[3].n_vt, G4[3].nc, &c0, &c1);
     swiglu_prologue<MT>(sm, a, G4[3], c0, c1, a.part0, G4[2].nc);
     k_range(G4[3], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
@@ -680,10 +694,15 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
   }
   // final: x += last w2 partials, rows spread over the CTAs
   grid_wait(a, target);
+  if (tr && threadIdx.x == 0) tr[1 + a.n_layer * 5] = global_ns();
   const int rows = a.M * a.dim;
   for (int t = blockIdx.x * kCT + threadIdx.x; t < rows; t += gridDim.x * kCT) {
     const int m = t / a.dim, k = t % a.dim;
     xa[t] = __fadd_rn(__ldcg(xa + t), sum_part<MT>(a.part1, G4[3].nc, k, m));
+  }
+  if (tr) {
+    bar_sync_n(1, kCT);
+    if (threadIdx.x == 0) tr[2 + a.n_layer * 5] = global_ns();
   }
 }
 

@@ -260,6 +260,14 @@ class B200DualAr:
     def profile_gemv(self, kind: int, n_launches: int) -> None:
         _lib.check(_lib.lib().sx_profile_gemv(self.handle, kind, n_launches))
 
+    def profile_stack(self, fast: bool = False) -> dict:
+        """Phase timing of one persistent-stack launch (us): total, per-layer mean of each
+        phase, the final phase and the setup."""
+        out = np.zeros(8, np.float32)
+        _lib.check(_lib.lib().sx_profile_stack(self.handle, int(fast), _p(out, C.c_float)))
+        keys = ["total", "wqkv", "attention", "wo", "w13", "w2", "final", "setup"]
+        return {k: float(v) for k, v in zip(keys, out)}
+
     def seq_len(self, seq: int = 0) -> int:
         v = C.c_int32()
         _lib.check(_lib.lib().sx_session_len(self.handle, seq, C.byref(v)))

@@ -4,10 +4,13 @@ Qwen3-4B-shaped model with fewer layers, so an `ncu --set full` capture stays sm
 
   python -m syrinx_b200.profile --what gemv --kind 2 --layers 8 --launches 16
   python -m syrinx_b200.profile --what frames --layers 8 --frames 4 --prompt 512
+  python -m syrinx_b200.profile --what stack --layers 36 --prompt 512   (phase timing, printed)
+  python -m syrinx_b200.profile --what prefill --layers 36 --prompt 512  (prefill time, printed)
 """
 from __future__ import annotations
 
 import argparse
+import time
 
 from . import QWEN3_4B, B200DualAr, Model, shrink, synth_blob
 from .configs import SX_DTYPE_Q4_K, SX_DTYPE_Q8_0
@@ -16,7 +19,7 @@ from .workloads import dual_ar_prompt
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["gemv", "frames"], default="gemv")
+    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill"], default="gemv")
     ap.add_argument("--kind", type=int, default=2, help="0 wqkv, 1 wo, 2 w1|w3, 3 w2")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--launches", type=int, default=16)
@@ -28,8 +31,25 @@ def main():
     wtype = SX_DTYPE_Q4_K if args.q4k else SX_DTYPE_Q8_0
     model = Model(cfg, synth_blob(cfg, wtype, seed=2))
     be = B200DualAr(model, max_ctx=args.prompt + 64 + args.frames)
-    be.prefill(dual_ar_prompt(cfg, args.prompt, max(1, args.prompt * 3 // 4), seed=2))
-    if args.what == "gemv":
+    prompt = dual_ar_prompt(cfg, args.prompt, max(1, args.prompt * 3 // 4), seed=2)
+    t0 = time.perf_counter()
+    be.prefill(prompt)
+    t_prefill = time.perf_counter() - t0
+    if args.what == "prefill":
+        for _ in range(2):
+            be.reset()
+            t0 = time.perf_counter()
+            be.prefill(prompt)
+            t_prefill = min(t_prefill, time.perf_counter() - t0)
+        print(f"prefill of {args.prompt} tokens, {args.layers} layers: {t_prefill * 1e3:.2f} ms")
+    elif args.what == "stack":
+        for fast in (False, True):
+            be.profile_stack(fast)  # warm
+            r = be.profile_stack(fast)
+            print(("fast" if fast else "slow") + " stack phases (us): " +
+                  ", ".join(f"{k} {v:.2f}" for k, v in r.items()))
+        be.decode_greedy(args.frames, mask_stop=True)
+    elif args.what == "gemv":
         be.profile_gemv(args.kind, args.launches)  # close() below synchronizes the stream
     else:
         be.decode_greedy(args.frames, mask_stop=True)

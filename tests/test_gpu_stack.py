@@ -65,3 +65,23 @@ def test_stack_batched_equals_single():
         single.prefill(p)
         assert np.array_equal(got, single.decode_greedy(12, mask_stop=True))
     be.close(); single.close(); model.close()
+
+
+def test_tensor_core_prefill_bit_identical_to_gemv():
+    """The tcgen05 prefill GEMM (gemm_tc.cu) writes the same partials as the mma.sync GEMV:
+    prefill logits and the following decode are bit-identical with SYRINX_TC=0 and =1."""
+    cfg = shrink(sx.QWEN3_4B, 2, 1, name="qwen3-4b-L2")
+    model = sx.Model(cfg, sx.synth_blob(cfg, SX_DTYPE_Q8_0, seed=35))
+    prompt = dual_ar_prompt(cfg, 150, 120, seed=35)  # chunks of 64, 64, 22 tokens
+    out = {}
+    for tc in ("0", "1"):
+        os.environ["SYRINX_TC"] = tc
+        be = sx.B200DualAr(model, max_ctx=200)
+        st = be.prefill(prompt)
+        out[tc] = (st.semantic_logits.copy(), st.hidden.copy(), be.decode_greedy(6, mask_stop=True))
+        be.close()
+    del os.environ["SYRINX_TC"]
+    assert np.array_equal(out["0"][0].view(np.uint32), out["1"][0].view(np.uint32))
+    assert np.array_equal(out["0"][1].view(np.uint32), out["1"][1].view(np.uint32))
+    assert np.array_equal(out["0"][2], out["1"][2])
+    model.close()
