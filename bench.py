@@ -360,7 +360,8 @@ def bench_tp(args):
         "hbm_roofline": {"bytes_per_frame_per_gpu": per_gpu, "frac_of_peak": round(per_gpu * value / (peak * 1e9), 4),
                          "peak_gbs": peak, "peak_kind": peak_kind,
                          "note": "layers and KV divided over the ranks; semantic head and fast_output replicated"},
-        "gpu_launches": kernels_per_frame(cfg) * K, "clocks": clk.summary(), "prefill_s": round(t_prefill, 2),
+        "gpu_launches": kernels_per_frame(cfg, world == 1 and os.environ.get("SYRINX_STACK", "1") != "0") * K,
+        "clocks": clk.summary(), "prefill_s": round(t_prefill, 2),
     }
     if world > 1:
         tp.close(be, model, dist)

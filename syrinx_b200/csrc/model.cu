@@ -785,7 +785,7 @@ bool stack_args(sx_session* s, bool fast, int M, float* resid, const int* tok_se
     StackGeo g;
     g.K = (int)cols;
     g.nb = (int)(cols / 32);
-    g.nc = (g.nb + 7) / 8;
+    g.nc = (g.nb + kStackChunkBlocks - 1) / kStackChunkBlocks;
     g.n_vt = (int)q8_tiles(rows);
     return g;
   };

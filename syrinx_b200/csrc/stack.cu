@@ -47,9 +47,11 @@ namespace {
 constexpr int kCW = 8;                 // consumer warps
 constexpr int kCT = kCW * 32;          // consumer threads
 constexpr int kThreadsStack = kCT + 32;  // + the producer warp
-constexpr int kIB = 8;                 // 32-wide k blocks per item (one k chunk)
-constexpr int kItemBytes = kIB * kQ8Rec;  // 4352
+constexpr int kIB = kStackChunkBlocks;  // 32-wide k blocks per item (one k chunk of 512)
+constexpr int kItemBytes = kIB * kQ8Rec;  // 8704
 constexpr int kSpanBlocks = 32;        // k blocks a CTA's item range may span in one matrix
+constexpr int kNCMax = 20;             // k chunks of any matrix (K <= 10240)
+constexpr int kMaxSplit = 32;          // splits of the key axis (one per lane in the merge)
 constexpr uint64_t kBarWaitNs = 2000000000ull;  // grid / mbarrier wait limit
 
 struct MatGeo {
@@ -106,6 +108,7 @@ __device__ __forceinline__ void mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---- shared memory ----------------------------------------------------------------------
+constexpr int kSpanHeads = 16;  // attention heads a CTA's wo k range may touch (32 blocks / hd 64)
 template <int MT>
 struct Smem {
   static constexpr int NP = (MT + 1) / 2;  // token pairs (tensor-core B columns 0-3 / 4-7)
@@ -114,6 +117,10 @@ struct Smem {
   float sxs[kSpanBlocks][MT];
   float ssb[kSpanBlocks][MT];
   int8_t scr[kCW][4][32];
+  float den[kMaxTok];
+  // attention-split merge weights of the heads in the wo k range [head][token][split]
+  float wts[kSpanHeads][MT][kMaxSplit];
+  float lsum[kSpanHeads][MT];
 };
 template <int HD>
 struct AttnSmem {
@@ -121,7 +128,7 @@ struct AttnSmem {
   float wacc[kCW][kMaxGroup][HD];
   float wm[kCW][kMaxGroup], wl[kCW][kMaxGroup];
   float kbuf[HD], vbuf[HD];
-  float den;
+  float den[kMaxTok];
 };
 
 template <int MT, int HD>
@@ -165,14 +172,34 @@ __device__ __forceinline__ void split_limbs(Smem<MT>& sm, int warp, int lane, in
   __syncwarp();
 }
 
-// Sum of partials of output row `row` (tile row r of virtual tile vt) over the k chunks.
+// Sum of partials of output row `row` (tile row r of virtual tile vt) over the k chunks: every
+// load is issued before the first add (one L2 round trip), the adds run in chunk order.
 template <int MT>
 __device__ __forceinline__ float sum_part(const float* part, int nc, int row, int m) {
   const float* p = part + ((size_t)(row >> 4) * nc * MT + m) * 16 + (row & 15);
+  float v[kNCMax];
+#pragma unroll
+  for (int kc = 0; kc < kNCMax; kc++) v[kc] = kc < nc ? __ldcg(p + (size_t)kc * MT * 16) : 0.f;
   float s = 0.f;
-#pragma unroll 8
-  for (int kc = 0; kc < nc; kc++) s += __ldcg(p + (size_t)kc * MT * 16);
+#pragma unroll
+  for (int kc = 0; kc < kNCMax; kc++)
+    if (kc < nc) s += v[kc];
   return s;
+}
+
+// RMS denominators of the tokens from the per-chunk sums of squares, by warp 0 (one chunk per
+// lane, a butterfly sum that every lane and every CTA evaluates identically) into den[MT].
+template <int MT>
+__device__ __forceinline__ void rms_den_all(const StackArgs& a, const float* ss, float* den) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      const float v = (lane < a.nc_dim && m < a.M) ? __ldcg(ss + (size_t)m * 64 + lane) : 0.f;
+      const float t = warp_sum(v);
+      if (lane == 0) den[m] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)a.dim), a.eps));
+    }
+  }
 }
 
 // ---- GEMV phase ------------------------------------------------------------------------
@@ -294,38 +321,51 @@ __device__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g
   }
 }
 
-// den = sqrt(sum of squares / K + eps), the chunk sums added in order
-__device__ __forceinline__ float rms_den(const float* ss, int m, int nc, int K, float eps) {
-  float t = 0.f;
-  for (int kc = 0; kc < nc; kc++) t += __ldcg(ss + (size_t)m * 64 + kc);
-  return sqrtf(__fadd_rn(__fdiv_rn(t, (float)K), eps));
-}
-
-// ---- P3 prologue: attention output for this CTA's k range (merge of the key-axis splits)
+// ---- P3 prologue: attention output for this CTA's k range (merge of the key-axis splits).
+// First, per (head, token), the splits' weights exp(m_s - max) and the denominator, one split
+// per lane; then per element the weighted sum of the splits' accumulators, every load issued
+// before the first add.
 template <int MT>
 __device__ void attn_out_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g, long long c0, long long c1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b_lo, b_hi, kc_lo, kc_hi;
   k_range(g, c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
   const int G = a.H / a.Hkv, hd = a.hd, ns = a.n_split;
+  const size_t per = (size_t)kMaxGroup * (hd + 2);  // floats per split
+  auto head_base = [&](int m, int h) {  // split 0 of (token m, head h)
+    return a.attn_part + (size_t)((m * a.Hkv + h / G) * ns) * per + (size_t)(h % G) * (hd + 2);
+  };
+  const int h_lo = (b_lo * 32) / hd;
+  const int nh = b_hi > b_lo ? ((b_hi * 32 - 1) / hd) - h_lo + 1 : 0;
+  for (int u = warp; u < nh * MT; u += kCW) {
+    const int hl = u / MT, m = u % MT;
+    float ms = -INFINITY, ls = 0.f;
+    if (m < a.M && lane < ns) {
+      const float* p = head_base(m, h_lo + hl) + (size_t)lane * per;
+      ms = __ldcg(p + hd);
+      ls = __ldcg(p + hd + 1);
+    }
+    const float M_ = warp_max(ms);
+    const float w = ms == -INFINITY ? 0.f : expf(ms - M_);
+    const float L = warp_sum(ls * w);
+    sm.wts[hl][m][lane] = w;
+    if (lane == 0) sm.lsum[hl][m] = L;
+  }
+  bar_sync_n(1, kCT);
   for (int u = warp; u < (b_hi - b_lo) * MT; u += kCW) {
     const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
     float v = 0.f;
     if (m < a.M) {
-      const int h = k / hd, e = k % hd;
-      const int g0 = h / G, i = h % G;
-      const float* base = a.attn_part + ((size_t)((m * a.Hkv + g0) * ns) * kMaxGroup + i) * (hd + 2);
-      const size_t stride = (size_t)kMaxGroup * (hd + 2);
-      float M_ = -INFINITY;
-      for (int s = 0; s < ns; s++) M_ = fmaxf(M_, __ldcg(base + s * stride + hd));
-      float L = 0.f, O = 0.f;
-      for (int s = 0; s < ns; s++) {
-        const float ms = __ldcg(base + s * stride + hd);
-        const float w = ms == -INFINITY ? 0.f : expf(ms - M_);
-        L = fmaf(__ldcg(base + s * stride + hd + 1), w, L);
-        O = fmaf(__ldcg(base + s * stride + e), w, O);
-      }
-      v = __fdiv_rn(O, L);
+      const int h = k / hd, e = k % hd, hl = h - h_lo;
+      const float* p = head_base(m, h) + e;
+      float o[kMaxSplit];
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplit; sp++) o[sp] = sp < ns ? __ldcg(p + (size_t)sp * per) : 0.f;
+      float O = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplit; sp++)
+        if (sp < ns) O = fmaf(o[sp], sm.wts[hl][m][sp], O);
+      v = __fdiv_rn(O, sm.lsum[hl][m]);
     }
     split_limbs<MT>(sm, warp, lane, bi, m, v);
   }
@@ -339,11 +379,13 @@ __device__ void swiglu_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b_lo, b_hi, kc_lo, kc_hi;
   k_range(g, c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
+  rms_den_all<MT>(a, a.ss + (size_t)64 * MT, sm.den);
+  bar_sync_n(1, kCT);
   for (int u = warp; u < (b_hi - b_lo) * MT; u += kCW) {
     const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
     float v = 0.f;
     if (m < a.M) {
-      const float den = rms_den(a.ss + (size_t)64 * MT, m, a.nc_dim, a.dim, a.eps);
+      const float den = sm.den[m];
       // tile j holds gate rows 8j..8j+7 (tile rows 0-7) and up rows 8j..8j+7 (rows 8-15)
       const int row_g = (k >> 3) * 16 + (k & 7);
       const float gt = __fdiv_rn(sum_part<MT>(part13, nc13, row_g, m), den);
@@ -439,26 +481,32 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
 
   // q rows of the group's heads (and, for the split that holds the new position, k and v):
   // merged wqkv partials / den + bias
-  if (threadIdx.x == 0) sm.den = rms_den(a.ss, m, a.nc_dim, a.dim, a.eps);
+  rms_den_all<MT>(a, a.ss, sm.den);
   bar_sync_n(1, kCT);
-  const float den = sm.den;
+  const float den = sm.den[m];
   const int n_rows = G * HD + (own_new ? 2 * HD : 0);
-  for (int t = threadIdx.x; t < n_rows; t += kCT) {
-    int row;
-    float* dst;
-    if (t < G * HD) {
-      row = (g * G + t / HD) * HD + t % HD;
-      dst = &sm.qs[t / HD][t % HD];
-    } else if (t < G * HD + HD) {
-      row = (a.H + g) * HD + (t - G * HD);
-      dst = &sm.kbuf[t - G * HD];
-    } else {
-      row = (a.H + a.Hkv + g) * HD + (t - G * HD - HD);
-      dst = &sm.vbuf[t - G * HD - HD];
+  // up to (8 + 2) * 128 rows over 256 threads: every thread's rows' loads go out together
+  constexpr int kRowsPT = (kMaxGroup + 2) * HD / kCT;
+#pragma unroll
+  for (int rr = 0; rr < kRowsPT; rr++) {
+    const int t = threadIdx.x + rr * kCT;
+    if (t < n_rows) {
+      int row;
+      float* dst;
+      if (t < G * HD) {
+        row = (g * G + t / HD) * HD + t % HD;
+        dst = &sm.qs[t / HD][t % HD];
+      } else if (t < G * HD + HD) {
+        row = (a.H + g) * HD + (t - G * HD);
+        dst = &sm.kbuf[t - G * HD];
+      } else {
+        row = (a.H + a.Hkv + g) * HD + (t - G * HD - HD);
+        dst = &sm.vbuf[t - G * HD - HD];
+      }
+      float v = __fdiv_rn(sum_part<MT>(part_qkv, nc_qkv, row, m), den);
+      if (L.bqkv) v = __fadd_rn(v, L.bqkv[row]);
+      *dst = v;
     }
-    float v = __fdiv_rn(sum_part<MT>(part_qkv, nc_qkv, row, m), den);
-    if (L.bqkv) v = __fadd_rn(v, L.bqkv[row]);
-    *dst = v;
   }
   bar_sync_n(1, kCT);
   for (int i = warp; i < G; i += kCW) norm_rope<HD>(sm.qs[i], L.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
@@ -748,9 +796,12 @@ cudaError_t launch_m(const StackArgs& a, int sms, cudaStream_t st) {
 // ranges per CTA span at most kSpanBlocks k blocks in every matrix.
 bool stack_supported(const StackArgs& a, int sms) {
   if (a.M < 1 || a.M > 8 || (a.hd != 64 && a.hd != 128) || a.H % a.Hkv || a.H / a.Hkv > kMaxGroup) return false;
-  if (a.dim % 32 || a.nc_dim > 64 || a.M * a.Hkv > sms) return false;
+  if (a.dim % 32 || a.nc_dim > 64 || a.M * a.Hkv > sms || a.n_split > kMaxSplit) return false;
+  // a k range is whole 512-wide chunks, so it covers whole heads: at most 1024 / hd of them
+  if (kSpanBlocks * 32 / a.hd > kSpanHeads) return false;
   for (int i = 0; i < 4; i++) {
     const StackGeo& g = a.geo[i];
+    if (g.nc > kNCMax) return false;
     const long long I = (long long)g.n_vt * g.nc;
     const long long ipc = (I + sms - 1) / sms;
     const long long spans = std::min<long long>(g.nc, (ipc + g.n_vt - 1) / g.n_vt + 1);
@@ -761,7 +812,7 @@ bool stack_supported(const StackArgs& a, int sms) {
 
 size_t stack_attn_part_floats(int sms, int hd) { return (size_t)sms * kMaxGroup * (hd + 2); }
 
-int stack_max_splits(int sms, int M, int Hkv) { return std::max(1, sms / (M * Hkv)); }
+int stack_max_splits(int sms, int M, int Hkv) { return std::max(1, std::min(kMaxSplit, sms / (M * Hkv))); }
 
 cudaError_t launch_stack(const StackArgs& a, int sms, cudaStream_t st) {
   if (!stack_supported(a, sms) || a.n_split < 1 || a.M * a.Hkv * a.n_split > sms) return cudaErrorInvalidValue;

@@ -177,8 +177,9 @@ struct StackLayer {
   const float* bo = nullptr;
   const float* ffn_norm = nullptr;
 };
+constexpr int kStackChunkBlocks = 16;  // 32-wide k blocks per weight item of the persistent stack
 struct StackGeo {
-  int K = 0, nb = 0, nc = 0, n_vt = 0;  // columns, 32-wide blocks, 8-block k chunks, 16-row tiles
+  int K = 0, nb = 0, nc = 0, n_vt = 0;  // columns, 32-wide blocks, 16-block k chunks, 16-row tiles
 };
 struct StackArgs {
   const StackLayer* layers = nullptr;  // device [n_layer]

@@ -122,3 +122,27 @@ def test_f16_bf16_conversions():
     bits = np.arange(0, 0x7c00, 7, dtype=np.uint16)
     for b in bits:
         assert oc.lib().oc_f16_to_f32(int(b)) == float(b.view(np.float16))
+
+
+def test_config4_fixture_matches_its_recipe():
+    """tests/golden/config4_q4k.npz holds what make_oracle_fixtures.py describes: 8 prompts of
+    lengths in [256, 1024] from its seeded recipe, 64 frames each, semantic ids in range."""
+    import os
+    import sys
+
+    import numpy as np
+
+    import syrinx_b200 as sx
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, here)
+    from make_oracle_fixtures import CONFIG4_FRAMES, CONFIG4_UTTERANCES, config4_prompts
+
+    fx = np.load(os.path.join(here, "config4_q4k.npz"))
+    cfg = sx.QWEN3_4B
+    lens = [p.shape[1] for p in config4_prompts(cfg)]
+    assert list(fx["lens"]) == lens and all(256 <= T <= 1024 for T in lens)
+    assert fx["frames"].shape == (CONFIG4_UTTERANCES, CONFIG4_FRAMES, cfg.frame_width)
+    sem = fx["frames"][:, :, 0]
+    assert np.all((sem >= cfg.semantic_begin_id) & (sem <= cfg.semantic_end_id))
+    assert np.all(fx["frames"][:, :, 1] == sem - cfg.semantic_begin_id)  # first_code
+    assert fx["logits0_semantic"].shape == (CONFIG4_UTTERANCES, cfg.n_semantic() + 1)
