@@ -486,7 +486,7 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
   const float den = sm.den[m];
   const int n_rows = G * HD + (own_new ? 2 * HD : 0);
   // up to (8 + 2) * 128 rows over 256 threads: every thread's rows' loads go out together
-  constexpr int kRowsPT = (kMaxGroup + 2) * HD / kCT;
+  constexpr int kRowsPT = ((kMaxGroup + 2) * HD + kCT - 1) / kCT;
 #pragma unroll
   for (int rr = 0; rr < kRowsPT; rr++) {
     const int t = threadIdx.x + rr * kCT;
