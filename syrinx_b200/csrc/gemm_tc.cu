@@ -15,14 +15,17 @@
 // and scale per block in f32 in the GEMV's order, while the tensor core already runs the next
 // block's product into the other half of tensor memory.
 //
-// Data flow per CTA (one CTA per SM, a contiguous range of (row group, k chunk) items):
-//   - one lane bulk-copies the 8 tile records of an item (8 x 4352 contiguous bytes) into a
-//     3-stage shared-memory ring (cp.async.bulk, mbarrier completion), an item ahead;
-//   - all warps repack a block's records into the canonical no-swizzle K-major layout of the
-//     A operand (8-row x 16-byte core matrices) and split x into int8 limbs in the same layout
-//     for the B operand (row n = 4 * token + limb), then fence the async proxy;
-//   - one thread issues the MMA and commits it to an mbarrier;
-//   - all warps read back the previous block's sums and accumulate.
+// Data flow:
+//   - k_tc_limbs (one CTA per token) computes the RMSNorm denominator and splits x into int8
+//     limbs, written once per launch as every k block's B operand in the canonical no-swizzle
+//     K-major layout (8-row x 16-byte core matrices; row n = 4 * token + limb);
+//   - k_gemm_tc (one CTA per SM, a contiguous range of (k chunk, 128-row group) items, k-chunk
+//     major so consecutive items share their B operands): one lane bulk-copies an item's 8 tile
+//     records (8 x 4352 contiguous bytes) and, when the chunk changes, the chunk's B operands
+//     into double-buffered shared memory (cp.async.bulk, mbarrier completion), an item ahead;
+//   - per k block all warps repack the 8 records' quants into the canonical A layout and their
+//     row scales, fence the async proxy, one thread issues the MMA and commits it to an
+//     mbarrier, and all warps read back the previous block's sums and accumulate.
 // Every wait is bounded by %globaltimer and raises the session's error flag; tensor memory is
 // freed on every path.
 #include <cuda_runtime.h>
@@ -107,36 +110,108 @@ struct TcGeo {
 };
 
 // element (row n, k) of a canonical K-major operand of 32 bytes of K per row
-__device__ __forceinline__ int canon_off(int n, int k) { return (n >> 3) * 256 + (k >> 4) * 128 + (n & 7) * 16 + (k & 15); }
+__host__ __device__ __forceinline__ int canon_off(int n, int k) {
+  return (n >> 3) * 256 + (k >> 4) * 128 + (n & 7) * 16 + (k & 15);
+}
+
+// ---- the B operand: int8 limbs of x for every k block, in the canonical layout ----------
+// One CTA per token: the RMSNorm denominator exactly as k_gemv_q8 computes it (256 threads,
+// k strided by 256, warp sums added in warp order), then per 32-wide block the limb split of
+// the normed values (exact to 2^-27 of the block max) as rows 4t..4t+3 of that block's
+// operand, and the block's power-of-two scale.
+template <int MT>
+__global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo g, uint8_t* Bg, float* sxg) {
+  __shared__ float red[kTW];
+  __shared__ float den_s;
+  __shared__ __align__(16) int8_t scr[kTW][4][32];
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int N = 4 * MT;
+  pdl_launch_dependents();
+  pdl_wait();
+  const bool live = t < a.M;
+  if (a.norm_w && live) {
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < g.K; k += kTT) {
+      const float v = ld_cg(a.x + (size_t)t * g.K + k);
+      ss = fmaf(v, v, ss);
+    }
+    const float w = warp_sum(ss);
+    if (lane == 0) red[warp] = w;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < kTW; i++) tot += red[i];
+      den_s = sqrtf(__fadd_rn(__fdiv_rn(tot, (float)g.K), a.eps));
+    }
+    __syncthreads();
+  }
+  for (int b = warp; b < g.nb; b += kTW) {
+    const int k = b * 32 + lane;
+    float v = 0.f;
+    if (live) {
+      v = ld_cg(a.x + (size_t)t * g.K + k);
+      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den_s), a.norm_w[k]);
+    }
+    const float mx = warp_max(fabsf(v));
+    const int e = (__float_as_int(mx) >> 23) & 0xff;
+    float sc = 0.f, sx = 0.f;
+    if (e == 255 || __any_sync(0xffffffffu, v != v)) {
+      sx = __int_as_float(0x7fc00000);
+    } else if (e >= 6) {
+      sc = __int_as_float((259 - e) << 23);
+      sx = __int_as_float((e - 5) << 23);
+    }
+    const float sv = v * sc;
+    const float l0 = rintf(sv);
+    float r = (sv - l0) * 128.f;
+    const float l1 = rintf(r);
+    r = (r - l1) * 128.f;
+    const float l2 = rintf(r);
+    r = (r - l2) * 128.f;
+    const float l3 = rintf(r);
+    scr[warp][0][lane] = (int8_t)(int)l0;
+    scr[warp][1][lane] = (int8_t)(int)l1;
+    scr[warp][2][lane] = (int8_t)(int)l2;
+    scr[warp][3][lane] = (int8_t)(int)l3;
+    __syncwarp();
+    const int limb = lane >> 3, kk = 4 * (lane & 7);
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(&scr[warp][limb][kk]);
+    *reinterpret_cast<uint32_t*>(Bg + (size_t)b * N * 32 + canon_off(4 * t + limb, kk)) = word;
+    if (lane == 0) sxg[(size_t)b * MT + t] = sx;
+    __syncwarp();
+  }
+}
 
 template <int MT>
 struct TcSmem {
   static constexpr int N = 4 * MT;
-  uint8_t stage[kStages][kStageBytes];
-  uint8_t A[2][kRows * 32];
-  uint8_t B[2][N * 32];
-  float sxs[2][MT];
-  float den[MT];
-  float red[kTW][MT];
-  int8_t scr[kTW][4][32];
-  uint64_t bar_stage[kStages];
-  uint64_t bar_mma[2];
+  uint8_t stA[2][kStageBytes];              // an item's 8 tile records x 8 blocks
+  uint8_t stB[2][kChunkB * N * 32];         // a k chunk's B operands, canonical
+  float stS[2][kChunkB * MT];               // and its blocks' x scales
+  uint8_t A[2][kRows * 32];                 // one block's A operand, canonical
+  float dsb[2][kRows];                      // its row scales
+  uint64_t bar_a[2], bar_b[2], bar_mma[2];
   uint32_t tmem_base;
 };
 
 template <int MT>
-__global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGeo g) {
+__global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGeo g, const uint8_t* Bg,
+                                                    const float* sxg) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   TcSmem<MT>& sm = *reinterpret_cast<TcSmem<MT>*>(smem_raw);
   constexpr int N = TcSmem<MT>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // items (k chunk, 128-row group), k-chunk-major: consecutive items share the B operand
   const int I = g.n_rg * g.nc;
   const int c0 = (int)((long long)blockIdx.x * I / gridDim.x), c1 = (int)((long long)(blockIdx.x + 1) * I / gridDim.x);
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; i++) mbar_init(&sm.bar_stage[i], 1);
-    for (int i = 0; i < 2; i++) mbar_init(&sm.bar_mma[i], 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&sm.bar_a[i], 1);
+      mbar_init(&sm.bar_b[i], 1);
+      mbar_init(&sm.bar_mma[i], 1);
+    }
     mbar_fence_init();
   }
   if (warp == 0) {  // two accumulators of up to 256 columns
@@ -148,49 +223,28 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  // the item's 8 tile records (weights do not depend on the previous kernel)
-  auto issue_item = [&](int it, int stage) {
-    const int rg = (int)(it / g.nc), kc = (int)(it % g.nc);
-    const int nrec = min(kChunkB, g.nb - kc * kChunkB);
-    int ntiles = 0;
-    for (int t = 0; t < kTiles; t++)
-      if (rg * kTiles + t < g.n_vt) ntiles++;
-    mbar_arrive_expect_tx(&sm.bar_stage[stage], (uint32_t)(ntiles * nrec * kQ8Rec));
+  auto nrec_of = [&](int kc) { return min(kChunkB, g.nb - kc * kChunkB); };
+  // an item's tile records (weights: independent of the previous kernel)
+  auto issue_a = [&](int it, int st) {
+    const int kc = it / g.n_rg, rg = it % g.n_rg;
+    const int nrec = nrec_of(kc);
+    const int ntiles = min(kTiles, g.n_vt - rg * kTiles);
+    mbar_arrive_expect_tx(&sm.bar_a[st], (uint32_t)(ntiles * nrec * kQ8Rec));
     for (int t = 0; t < ntiles; t++)
-      bulk_g2s(sm.stage[stage] + t * kChunkB * kQ8Rec,
-               W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB) * kQ8Rec, (uint32_t)(nrec * kQ8Rec),
-               &sm.bar_stage[stage]);
+      bulk_g2s(sm.stA[st] + t * kChunkB * kQ8Rec, W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB) * kQ8Rec,
+               (uint32_t)(nrec * kQ8Rec), &sm.bar_a[st]);
   };
-  if (threadIdx.x == 0 && c1 > c0) issue_item(c0, 0);
-
+  // a k chunk's B operands and scales (written by k_tc_limbs)
+  auto issue_b = [&](int kc, int st) {
+    const int nrec = nrec_of(kc);
+    mbar_arrive_expect_tx(&sm.bar_b[st], (uint32_t)(nrec * N * 32 + nrec * MT * 4));
+    bulk_g2s(sm.stB[st], Bg + (size_t)kc * kChunkB * N * 32, (uint32_t)(nrec * N * 32), &sm.bar_b[st]);
+    bulk_g2s(sm.stS[st], sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.bar_b[st]);
+  };
+  if (threadIdx.x == 0 && c1 > c0) issue_a(c0, 0);
   pdl_launch_dependents();
-  pdl_wait();
-
-  // RMSNorm denominators of the chunk's tokens over the full K, in the GEMV's order
-  if (a.norm_w) {
-    float ss[MT];
-#pragma unroll
-    for (int m = 0; m < MT; m++) ss[m] = 0.f;
-    for (int k = threadIdx.x; k < g.K; k += kTT)
-#pragma unroll
-      for (int m = 0; m < MT; m++) {
-        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
-        ss[m] = fmaf(v, v, ss[m]);
-      }
-#pragma unroll
-    for (int m = 0; m < MT; m++) {
-      const float t = warp_sum(ss[m]);
-      if (lane == 0) sm.red[warp][m] = t;
-    }
-    __syncthreads();
-    if (threadIdx.x < MT) {
-      float t = 0.f;
-#pragma unroll
-      for (int w = 0; w < kTW; w++) t += sm.red[w][threadIdx.x];
-      sm.den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)g.K), a.eps));
-    }
-    __syncthreads();
-  }
+  pdl_wait();  // the B operands come from the limb kernel
+  if (threadIdx.x == 0 && c1 > c0) issue_b(c0 / g.n_rg, 0);
 
   // epilogue roles: TMEM lane quarter q (rows 32q..32q+31), token half h
   const int q = warp & 3, h = warp >> 2;
@@ -200,132 +254,110 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
 #pragma unroll
   for (int i = 0; i < TPT; i++) acc01[i] = acc23[i] = 0.f;
 
-  int blk = 0;  // blocks processed by this CTA (selects the A/B buffer and TMEM half)
-  int prev_stage = 0, prev_j = 0, prev_rg = 0, prev_kc = 0, prev_nrec = 0;
+  int blk = 0;  // blocks processed by this CTA (selects the A buffer and the TMEM half)
+  int p_sb = 0, p_j = 0, p_rg = 0, p_kc = 0, p_nrec = 0;
   bool have_prev = false;
 
-  // read back block (blk - 1)'s sums and accumulate; at the end of its item, store the partials
+  // read back block (blk - 1)'s sums and accumulate; after its item's last block, the partials
   auto epilogue = [&]() {
-    const int buf = (int)((blk - 1) & 1);
+    const int buf = (blk - 1) & 1;
     tc_wait(&sm.bar_mma[buf], (uint32_t)(((blk - 1) >> 1) & 1), a.err);
     tc_fence_after();
-    const uint8_t* rec = sm.stage[prev_stage] + ((row >> 4) * kChunkB + prev_j) * kQ8Rec;
-    const float ds = __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(row & 15)));
+    const float ds = sm.dsb[buf][row];
+    const float* sxs = sm.stS[p_sb] + p_j * MT + h * TPT;
 #pragma unroll
-    for (int part = 0; part < TPT / 8; part++) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + (h * TPT + part * 8) * 4), r);
+    for (int part = 0; part < TPT / 8; part += 2) {
+      uint32_t r0[32], r1[32];
+      const uint32_t col = (uint32_t)(buf * 256 + (h * TPT + part * 8) * 4);
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col, r0);
+      if (part + 1 < TPT / 8) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col + 32, r1);
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        const int tl = part * 8 + i, t = h * TPT + tl;
-        const float sx = sm.sxs[buf][t];
-        const float dsx = __fmul_rn(ds, sx);
-        const int s01 = (int)r[4 * i] * 128 + (int)r[4 * i + 1];
-        const int s23 = (int)r[4 * i + 2] * 128 + (int)r[4 * i + 3];
-        acc01[tl] = fmaf(dsx, (float)s01, acc01[tl]);
-        acc23[tl] = fmaf(dsx, (float)s23, acc23[tl]);
+        const int tl = part * 8 + i;
+        const float dsx = __fmul_rn(ds, sxs[tl]);
+        acc01[tl] = fmaf(dsx, (float)((int)r0[4 * i] * 128 + (int)r0[4 * i + 1]), acc01[tl]);
+        acc23[tl] = fmaf(dsx, (float)((int)r0[4 * i + 2] * 128 + (int)r0[4 * i + 3]), acc23[tl]);
+      }
+      if (part + 1 < TPT / 8) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const int tl = (part + 1) * 8 + i;
+          const float dsx = __fmul_rn(ds, sxs[tl]);
+          acc01[tl] = fmaf(dsx, (float)((int)r1[4 * i] * 128 + (int)r1[4 * i + 1]), acc01[tl]);
+          acc23[tl] = fmaf(dsx, (float)((int)r1[4 * i + 2] * 128 + (int)r1[4 * i + 3]), acc23[tl]);
+        }
       }
     }
-    if (prev_j == prev_nrec - 1) {
-      const int vt = prev_rg * kTiles + (row >> 4);
+    if (p_j == p_nrec - 1) {
+      const int vt = p_rg * kTiles + (row >> 4);
       if (vt < g.n_vt) {
-        float* P = a.part + ((size_t)vt * g.nc + prev_kc) * MT * 16 + (row & 15);
+        float* P = a.part + ((size_t)vt * g.nc + p_kc) * MT * 16 + (row & 15);
 #pragma unroll
         for (int tl = 0; tl < TPT; tl++) {
           const int t = h * TPT + tl;
           if (t < a.M) __stcg(P + t * 16, acc01[tl] * 0x1p-7f + acc23[tl] * 0x1p-21f);
-          acc01[tl] = acc23[tl] = 0.f;
         }
-      } else {
-#pragma unroll
-        for (int tl = 0; tl < TPT; tl++) acc01[tl] = acc23[tl] = 0.f;
       }
+#pragma unroll
+      for (int tl = 0; tl < TPT; tl++) acc01[tl] = acc23[tl] = 0.f;
     }
   };
 
-  int n_items = 0;
+  int n_items = 0, kc_idx = 0;
   for (int it = c0; it < c1; it++, n_items++) {
-    const int stage = (int)(n_items % kStages);
-    const int rg = (int)(it / g.nc), kc = (int)(it % g.nc);
-    const int nrec = min(kChunkB, g.nb - kc * kChunkB);
-    // the next item's records into the stage an item ahead (its last reader finished two
-    // items ago)
-    if (threadIdx.x == 0 && it + 1 < c1) issue_item(it + 1, (int)((n_items + 1) % kStages));
-    tc_wait(&sm.bar_stage[stage], (uint32_t)((n_items / kStages) & 1), a.err);
+    const int sa = n_items & 1;
+    const int kc = it / g.n_rg, rg = it % g.n_rg;
+    if (it > c0 && kc != (it - 1) / g.n_rg) kc_idx++;
+    const int sb = kc_idx & 1;
+    const int nrec = nrec_of(kc);
+    // prefetch the next item's records (stage sa ^ 1: its last repack finished in the previous
+    // item) and, at a k chunk change, the next chunk's B operand (stage sb ^ 1: unread since
+    // two chunks ago, every MMA reading it has completed)
+    if (threadIdx.x == 0 && it + 1 < c1) {
+      issue_a(it + 1, sa ^ 1);
+      if ((it + 1) / g.n_rg != kc) issue_b((it + 1) / g.n_rg, sb ^ 1);
+    }
+    tc_wait(&sm.bar_a[sa], (uint32_t)((n_items >> 1) & 1), a.err);
+    tc_wait(&sm.bar_b[sb], (uint32_t)((kc_idx >> 1) & 1), a.err);
     for (int j = 0; j < nrec; j++, blk++) {
-      const int buf = (int)(blk & 1);
-      const int b = kc * kChunkB + j;
-      // A: the 8 records' quants into the canonical layout (one 16-byte fragment per thread)
-      {
+      const int buf = blk & 1;
+      {  // A: the 8 records' quants into the canonical layout, and the row scales
         const int t = warp, L = lane;  // tile t, fragment lane L = 4g + c
         const int gg = L >> 2, cc = L & 3;
+        const bool tile_ok = rg * kTiles + t < g.n_vt;
+        const uint8_t* rec = sm.stA[sa] + (t * kChunkB + j) * kQ8Rec;
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (rg * kTiles + t < g.n_vt) v = lds128(sm.stage[stage] + (t * kChunkB + j) * kQ8Rec + L * 16);
+        if (tile_ok) v = lds128(rec + L * 16);
         uint8_t* A = sm.A[buf];
         const int m0 = t * 16 + gg, m1 = m0 + 8;
         *reinterpret_cast<uint32_t*>(A + canon_off(m0, 4 * cc)) = v.x;
         *reinterpret_cast<uint32_t*>(A + canon_off(m1, 4 * cc)) = v.y;
         *reinterpret_cast<uint32_t*>(A + canon_off(m0, 16 + 4 * cc)) = v.z;
         *reinterpret_cast<uint32_t*>(A + canon_off(m1, 16 + 4 * cc)) = v.w;
+        if (L < 16)
+          sm.dsb[buf][t * 16 + L] =
+              tile_ok ? __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(L))) : 0.f;
       }
-      // B: limbs of x (normed) for block b, one warp per token
-      for (int m = warp; m < MT; m += kTW) {
-        const int k = b * 32 + lane;
-        float v = 0.f;
-        if (m < a.M) {
-          v = ld_cg(a.x + (size_t)m * g.K + k);
-          if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, sm.den[m]), a.norm_w[k]);
-        }
-        const float mx = warp_max(fabsf(v));
-        const int e = (__float_as_int(mx) >> 23) & 0xff;
-        float sc = 0.f, sx = 0.f;
-        if (e == 255 || __any_sync(0xffffffffu, v != v)) {
-          sx = __int_as_float(0x7fc00000);
-        } else if (e >= 6) {
-          sc = __int_as_float((259 - e) << 23);
-          sx = __int_as_float((e - 5) << 23);
-        }
-        const float s = v * sc;
-        const float l0 = rintf(s);
-        float r = (s - l0) * 128.f;
-        const float l1 = rintf(r);
-        r = (r - l1) * 128.f;
-        const float l2 = rintf(r);
-        r = (r - l2) * 128.f;
-        const float l3 = rintf(r);
-        sm.scr[warp][0][lane] = (int8_t)(int)l0;
-        sm.scr[warp][1][lane] = (int8_t)(int)l1;
-        sm.scr[warp][2][lane] = (int8_t)(int)l2;
-        sm.scr[warp][3][lane] = (int8_t)(int)l3;
-        __syncwarp();
-        {  // lane L writes limb L/8's bytes k = 4(L%8) .. 4(L%8)+3 as one word
-          const int limb = lane >> 3, kk = 4 * (lane & 7);
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(&sm.scr[warp][limb][kk]);
-          *reinterpret_cast<uint32_t*>(sm.B[buf] + canon_off(4 * m + limb, kk)) = w;
-        }
-        if (lane == 0) sm.sxs[buf][m] = sx;
-        __syncwarp();
-      }
-      fence_async_smem();  // the operands written by threads become visible to the tensor core
+      fence_async_smem();  // the A operand written by threads becomes visible to the tensor core
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
       if (threadIdx.x == 0) {
-        tc_mma(tmem + (uint32_t)(buf * 256), umma_desc(sm.A[buf], 128, 256), umma_desc(sm.B[buf], 128, 256),
-               idesc_i8(kRows, N));
+        tc_mma(tmem + (uint32_t)(buf * 256), umma_desc(sm.A[buf], 128, 256),
+               umma_desc(sm.stB[sb] + j * N * 32, 128, 256), idesc_i8(kRows, N));
         tc_commit(&sm.bar_mma[buf]);
       }
       if (have_prev) epilogue();
-      // the next MMA into this warp's TMEM half must not start before the read-back is done
+      // the next MMA into the other TMEM half must not start before this read-back is done
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
-      prev_stage = stage;
-      prev_j = j;
-      prev_rg = rg;
-      prev_kc = kc;
-      prev_nrec = nrec;
+      p_sb = sb;
+      p_j = j;
+      p_rg = rg;
+      p_kc = kc;
+      p_nrec = nrec;
       have_prev = true;
     }
   }
@@ -336,16 +368,23 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
 }
 
 template <int MT>
-cudaError_t launch_tc_t(const GemvArgs& a, const TcGeo& g, int sms, cudaStream_t st) {
+cudaError_t launch_tc_t(const GemvArgs& a, const TcGeo& g, int sms, uint8_t* scratch, cudaStream_t st) {
+  constexpr int N = 4 * MT;
+  uint8_t* Bg = scratch;
+  float* sxg = reinterpret_cast<float*>(scratch + (size_t)g.nb * N * 32);
+  cudaLaunchAttribute attr0[1];
+  cudaLaunchConfig_t cfg0 = launch_cfg(dim3(MT), dim3(kTT), 0, st, attr0);
+  cudaError_t e = cudaLaunchKernelEx(&cfg0, k_tc_limbs<MT>, a, g, Bg, sxg);
+  if (e != cudaSuccess) return e;
   auto kern = k_gemm_tc<MT>;
   const size_t smem = sizeof(TcSmem<MT>) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const long long I = (long long)g.n_rg * g.nc;
   const int grid = (int)std::max(1LL, std::min<long long>(I, sms));
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kTT), smem, st, attr);
-  return cudaLaunchKernelEx(&cfg, kern, a, g);
+  return cudaLaunchKernelEx(&cfg, kern, a, g, (const uint8_t*)Bg, (const float*)sxg);
 }
 
 }  // namespace
@@ -357,9 +396,12 @@ bool tc_enabled() {
 }
 
 // The partials of a Q8_0 GEMV of 9..64 tokens (Mt = 16, 32 or 64) on the tensor cores.
+size_t gemm_tc_scratch_bytes(int K, int Mt) { return (size_t)(K / 32) * (4 * Mt * 32 + Mt * 4); }
+
 cudaError_t launch_gemm_tc(const GemvArgs& a, int Mt, int K, int nb, int nc, int t_first, int n_vt, int sms,
                            cudaStream_t st) {
-  if (t_first != 0 || a.n_extra != 0 || K % 32) return cudaErrorInvalidValue;
+  if (t_first != 0 || a.n_extra != 0 || K % 32 || !a.tc_scratch || gemm_tc_scratch_bytes(K, Mt) > a.tc_scratch_bytes)
+    return cudaErrorInvalidValue;
   TcGeo g;
   g.K = K;
   g.nb = nb;
@@ -367,9 +409,9 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, int Mt, int K, int nb, int nc, int
   g.n_vt = n_vt;
   g.n_rg = (n_vt + kTiles - 1) / kTiles;
   switch (Mt) {
-    case 16: return launch_tc_t<16>(a, g, sms, st);
-    case 32: return launch_tc_t<32>(a, g, sms, st);
-    case 64: return launch_tc_t<64>(a, g, sms, st);
+    case 16: return launch_tc_t<16>(a, g, sms, a.tc_scratch, st);
+    case 32: return launch_tc_t<32>(a, g, sms, a.tc_scratch, st);
+    case 64: return launch_tc_t<64>(a, g, sms, a.tc_scratch, st);
   }
   return cudaErrorInvalidValue;
 }

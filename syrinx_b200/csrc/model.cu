@@ -533,6 +533,13 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
       }
     for (const DevMat* w : {&m->emb, &m->cb_emb, &m->out_w, &m->fast_out, &m->fast_emb}) need(*w, kMaxTok);
     s->q8_part_cap = cap;
+    // the tensor-core prefill GEMM's B operands at the widest K of any layer matrix
+    size_t kmax = 0;
+    for (const auto* ls : {&m->slow, &m->fast})
+      for (const DevLayer& L : *ls)
+        for (const DevMat* w : {&L.wqkv, &L.wo, &L.w13, &L.w2}) kmax = std::max(kmax, (size_t)w->cols);
+    s->tc_scratch_bytes = gemm_tc_scratch_bytes((int)kmax, kMaxPrefillTok);
+    if ((rc = dalloc(s->allocs, &s->tc_scratch, std::max<size_t>(s->tc_scratch_bytes, 16)))) return fail(rc);
     if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
   }
   {
@@ -717,6 +724,8 @@ int gemv(GemvArgs a, Epi epi, sx_session* s) {
   a.part = s->q8_part;
   a.part_cap = s->q8_part_cap;
   a.err = s->err;
+  a.tc_scratch = s->tc_scratch;
+  a.tc_scratch_bytes = s->tc_scratch_bytes;
   if (epi == EPI_ADD && s->m->tp_size > 1) {
     if (!s->tp_connected) {
       set_error("tensor-parallel session: call sx_session_tp_connect before decoding");
@@ -1568,8 +1577,11 @@ int profile_gemv(sx_session* s, int kind, int n_launches) {
 }
 
 // One launch of the persistent stack for sequence 0 at its current position with the phase
-// trace on. out[0] total us; out[1..5] mean us of phases P1..P5 (CTA 0, phase start to the next
-// phase start, averaged over the layers); out[6] the final phase; out[7] setup before P1.
+// trace on. out[0] total us, out[1] setup before the first phase, out[2] the final phase; then
+// per phase p (wqkv, attention, wo, w1|w3, w2), averaged over the layers, out[3 + 4p + i]:
+// i = 0 the phase (its start to the next phase's start, CTA 0), 1 the slowest CTA's prologue,
+// 2 the slowest CTA's arrival after the phase start, 3 the barrier (the last arrival to the
+// next phase's start on CTA 0).
 int profile_stack(sx_session* s, int fast, float* out) {
   if (s->len[0] <= 0) {
     set_error("profile_stack: prefill first");
@@ -1584,7 +1596,8 @@ int profile_stack(sx_session* s, int fast, float* out) {
     return SX_E_UNSUPPORTED;
   }
   const int sms = num_sms_of(s->m->device);
-  const size_t per = (size_t)a.n_layer * 5 + 3;
+  const int L = a.n_layer;
+  const size_t per = (size_t)L * 15 + 3;
   unsigned long long* tr = nullptr;
   SX_CU(cudaMalloc((void**)&tr, per * sms * 8));
   a.trace = tr;
@@ -1597,17 +1610,27 @@ int profile_stack(sx_session* s, int fast, float* out) {
     set_error(std::string("profile_stack: ") + cudaGetErrorString(e));
     return SX_E_CUDA;
   }
-  const unsigned long long* t = h.data();  // CTA 0
-  const int L = a.n_layer;
-  for (int i = 0; i < 8; i++) out[i] = 0.f;
-  out[0] = (float)((t[2 + L * 5] - t[0]) * 1e-3);
+  auto T = [&](int cta, size_t i) { return (double)h[(size_t)cta * per + i]; };
+  auto at = [&](int l, int p, int k) { return (size_t)1 + ((size_t)l * 5 + p) * 3 + k; };
+  const size_t fin = 1 + (size_t)L * 15, end = 2 + (size_t)L * 15;
+  for (int i = 0; i < 23; i++) out[i] = 0.f;
+  out[0] = (float)((T(0, end) - T(0, 0)) * 1e-3);
+  out[1] = (float)((T(0, at(0, 0, 0)) - T(0, 0)) * 1e-3);
+  out[2] = (float)((T(0, end) - T(0, fin)) * 1e-3);
   for (int l = 0; l < L; l++)
     for (int p = 0; p < 5; p++) {
-      const unsigned long long t0 = t[1 + l * 5 + p], t1 = t[1 + l * 5 + p + 1];
-      out[1 + p] += (float)((t1 - t0) * 1e-3) / L;
+      const double start = T(0, at(l, p, 0));
+      const double next = (l == L - 1 && p == 4) ? T(0, fin) : T(0, p == 4 ? at(l + 1, 0, 0) : at(l, p + 1, 0));
+      double pro = 0, arr = 0;
+      for (int c = 0; c < sms; c++) {
+        pro = std::max(pro, T(c, at(l, p, 1)) - T(c, at(l, p, 0)));
+        arr = std::max(arr, T(c, at(l, p, 2)));
+      }
+      out[3 + 4 * p + 0] += (float)((next - start) * 1e-3 / L);
+      out[3 + 4 * p + 1] += (float)(pro * 1e-3 / L);
+      out[3 + 4 * p + 2] += (float)((arr - start) * 1e-3 / L);
+      out[3 + 4 * p + 3] += (float)((next - arr) * 1e-3 / L);
     }
-  out[6] = (float)((t[2 + L * 5] - t[1 + L * 5]) * 1e-3);
-  out[7] = (float)((t[1] - t[0]) * 1e-3);
   return check_err(s);
 }
 

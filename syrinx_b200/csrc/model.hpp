@@ -79,6 +79,8 @@ struct sx_session {
   size_t q8_part_cap = 0;    // floats
   // persistent decode stack scratch: the residual's second buffer, attention split partials,
   // per-chunk sums of squares and the grid barrier counter
+  uint8_t* tc_scratch = nullptr;  // tensor-core prefill GEMM: B operands of every k block
+  size_t tc_scratch_bytes = 0;
   float* stack_xb = nullptr;
   float* stack_attn = nullptr;
   float* stack_ss = nullptr;

@@ -691,7 +691,12 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
 
   // ---- consumers ----
   // optional phase trace: thread 0 of each CTA stamps %globaltimer at every phase start
-  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * (a.n_layer * 5 + 3) : nullptr;
+  // per CTA: [0] start, [1 + (l * 5 + p) * 3 + {0,1,2}] phase start / prologue end / arrival,
+  // [1 + n_layer * 15] final phase start, [2 + n_layer * 15] end
+  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * (a.n_layer * 15 + 3) : nullptr;
+  auto stamp = [&](int l, int p, int k) {
+    if (tr && threadIdx.x == 0) tr[1 + (l * 5 + p) * 3 + k] = global_ns();
+  };
   if (tr && threadIdx.x == 0) tr[0] = global_ns();
   long long ctr = 0;
   float* xa = a.x;   // the residual stream (in / out)
@@ -703,46 +708,56 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     int b_lo, b_hi, kc_lo, kc_hi;
     // P1: wqkv (x += previous layer's w2 partials)
     if (l > 0) grid_wait(a, target);
-    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 0] = global_ns();
+    stamp(l, 0, 0);
     cta_items(G4[0].n_vt, G4[0].nc, &c0, &c1);
     resid_prologue<MT>(sm, a, G4[0], c0, c1, xa, xb, l > 0 ? a.part1 : nullptr, G4[3].nc, nullptr, L.attn_norm,
                        a.ss);
     k_range(G4[0], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
+    stamp(l, 0, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, G4[0], c0, c1, b_lo, a.M, a.part0, a.err);
+    stamp(l, 0, 2);
     target = grid_arrive(a);
     // P2: attention
     grid_wait(a, target);
-    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 1] = global_ns();
+    stamp(l, 1, 0);
     attention_unit<MT, HD, KT>(am, a, L, l, a.part0, G4[0].nc);
+    stamp(l, 1, 1);
+    stamp(l, 1, 2);
     target = grid_arrive(a);
     // P3: wo
     grid_wait(a, target);
-    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 2] = global_ns();
+    stamp(l, 2, 0);
     cta_items(G4[1].n_vt, G4[1].nc, &c0, &c1);
     attn_out_prologue<MT>(sm, a, G4[1], c0, c1);
     k_range(G4[1], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
+    stamp(l, 2, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, G4[1], c0, c1, b_lo, a.M, a.part1, a.err);
+    stamp(l, 2, 2);
     target = grid_arrive(a);
     // P4: w1|w3 (x += wo partials + bias)
     grid_wait(a, target);
-    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 3] = global_ns();
+    stamp(l, 3, 0);
     cta_items(G4[2].n_vt, G4[2].nc, &c0, &c1);
     resid_prologue<MT>(sm, a, G4[2], c0, c1, xb, xa, a.part1, G4[1].nc, L.bo, L.ffn_norm, a.ss + (size_t)64 * MT);
     k_range(G4[2], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
+    stamp(l, 3, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, G4[2], c0, c1, b_lo, a.M, a.part0, a.err);
+    stamp(l, 3, 2);
     target = grid_arrive(a);
     // P5: w2
     grid_wait(a, target);
-    if (tr && threadIdx.x == 0) tr[1 + l * 5 + 4] = global_ns();
+    stamp(l, 4, 0);
     cta_items(G4[3].n_vt, G4[3].nc, &c0, &c1);
     swiglu_prologue<MT>(sm, a, G4[3], c0, c1, a.part0, G4[2].nc);
     k_range(G4[3], c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
+    stamp(l, 4, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, G4[3], c0, c1, b_lo, a.M, a.part1, a.err);
+    stamp(l, 4, 2);
     target = grid_arrive(a);
   }
   // final: x += last w2 partials, rows spread over the CTAs
   grid_wait(a, target);
-  if (tr && threadIdx.x == 0) tr[1 + a.n_layer * 5] = global_ns();
+  if (tr && threadIdx.x == 0) tr[1 + a.n_layer * 15] = global_ns();
   const int rows = a.M * a.dim;
   for (int t = blockIdx.x * kCT + threadIdx.x; t < rows; t += gridDim.x * kCT) {
     const int m = t / a.dim, k = t % a.dim;
@@ -750,7 +765,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
   }
   if (tr) {
     bar_sync_n(1, kCT);
-    if (threadIdx.x == 0) tr[2 + a.n_layer * 5] = global_ns();
+    if (threadIdx.x == 0) tr[2 + a.n_layer * 15] = global_ns();
   }
 }
 

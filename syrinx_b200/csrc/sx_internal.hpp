@@ -124,6 +124,8 @@ struct GemvArgs {
   // residual add across a tensor-parallel group (EPI_ADD of a K-split matrix, Q8_0 only)
   TpComm tp;
   int* err = nullptr;  // device error flag (bounded pipeline waits of the tensor-core GEMM)
+  uint8_t* tc_scratch = nullptr;  // the tensor-core GEMM's B operands (gemm_tc_scratch_bytes)
+  size_t tc_scratch_bytes = 0;
 };
 // floats of partial sums a Q8_0 GEMV over `w` with `n_rows` logical rows needs at M tokens
 size_t q8_part_floats(const DevMat& w, int64_t n_rows, int M);
@@ -158,6 +160,7 @@ cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st);
 cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st);
 // Q8_0 partials of 9..64 tokens on tcgen05 (gemm_tc.cu); SYRINX_TC=0 keeps them on mma.sync
 bool tc_enabled();
+size_t gemm_tc_scratch_bytes(int K, int Mt);
 cudaError_t launch_gemm_tc(const GemvArgs& a, int Mt, int K, int nb, int nc, int t_first, int n_vt, int sms,
                            cudaStream_t st);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
@@ -210,8 +213,8 @@ struct StackArgs {
   StackGeo geo[4];  // wqkv, wo, w1|w3, w2
   int nc_dim = 0;   // k chunks of dim
   int nslot = 0;    // ring slots (set by the launcher)
-  // profiling: non-null -> per CTA [n_layer * 5 + 3] %globaltimer stamps (start, every phase
-  // start, final phase start, end)
+  // profiling: non-null -> per CTA [n_layer * 15 + 3] %globaltimer stamps (start; per layer
+  // and phase: phase start, prologue end, arrival; final phase start; end)
   unsigned long long* trace = nullptr;
 };
 bool stack_supported(const StackArgs& a, int sms);

@@ -263,10 +263,13 @@ class B200DualAr:
     def profile_stack(self, fast: bool = False) -> dict:
         """Phase timing of one persistent-stack launch (us): total, per-layer mean of each
         phase, the final phase and the setup."""
-        out = np.zeros(8, np.float32)
+        out = np.zeros(23, np.float32)
         _lib.check(_lib.lib().sx_profile_stack(self.handle, int(fast), _p(out, C.c_float)))
-        keys = ["total", "wqkv", "attention", "wo", "w13", "w2", "final", "setup"]
-        return {k: float(v) for k, v in zip(keys, out)}
+        r = {"total": float(out[0]), "setup": float(out[1]), "final": float(out[2])}
+        for p, name in enumerate(["wqkv", "attention", "wo", "w13", "w2"]):
+            r[name] = {k: round(float(out[3 + 4 * p + i]), 2)
+                       for i, k in enumerate(["phase", "prologue", "arrival", "barrier"])}
+        return r
 
     def seq_len(self, seq: int = 0) -> int:
         v = C.c_int32()

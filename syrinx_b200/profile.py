@@ -46,8 +46,10 @@ def main():
         for fast in (False, True):
             be.profile_stack(fast)  # warm
             r = be.profile_stack(fast)
-            print(("fast" if fast else "slow") + " stack phases (us): " +
-                  ", ".join(f"{k} {v:.2f}" for k, v in r.items()))
+            print(("fast" if fast else "slow") + f" stack: total {r['total']:.1f} us, setup {r['setup']:.2f}, "
+                  f"final {r['final']:.2f}")
+            for k in ("wqkv", "attention", "wo", "w13", "w2"):
+                print(f"  {k}: " + ", ".join(f"{n} {v:.2f}" for n, v in r[k].items()))
         be.decode_greedy(args.frames, mask_stop=True)
     elif args.what == "gemv":
         be.profile_gemv(args.kind, args.launches)  # close() below synchronizes the stream
