@@ -52,6 +52,9 @@ constexpr int kItemBytes = kIB * kQ8Rec;  // 8704
 constexpr int kSpanBlocks = 32;        // k blocks a CTA's item range may span in one matrix
 constexpr int kNCMax = 20;             // k chunks of any matrix (K <= 10240)
 constexpr int kMaxSplit = 32;          // splits of the key axis (one per lane in the merge)
+constexpr int kInflight = 10;          // weight items a CTA's producer keeps in flight (87 KB)
+// prologue units (block, token) a warp gathers per batch (register budget: <= ~80 loads)
+constexpr int kUBResid = 3, kUBAttn = 2, kUBSwiglu = 2;
 constexpr uint64_t kBarWaitNs = 2000000000ull;  // grid / mbarrier wait limit
 
 struct MatGeo {
@@ -72,8 +75,10 @@ __device__ __forceinline__ unsigned long long grid_arrive(const StackArgs& a) {
   bar_sync_n(1, kCT);
   unsigned long long target = 0;
   if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned long long old = atomicAdd(a.bar, 1ull);
+    // a release at GPU scope after the CTA barrier: cumulative over the consumer threads'
+    // writes that the named barrier ordered before it (no full fence needed)
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(a.bar) : "memory");
     target = (old / gridDim.x + 1) * gridDim.x;
   }
   return target;
@@ -280,6 +285,7 @@ __device__ __forceinline__ void k_range(const MatGeo& g, long long c0, long long
 
 // ---- residual prologue (P1 and P4): x_new = x + partials (+ bias) for this CTA's k range;
 // the owner of each k chunk writes x_new and the chunk's sum of squares; limbs of x_new * g.
+// A warp's units (block, token) go in batches of kUBResid whose loads are all issued before any use.
 template <int MT>
 __device__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g, long long c0, long long c1,
                                const float* x_in, float* x_out, const float* part, int nc_part,
@@ -287,27 +293,46 @@ __device__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b_lo, b_hi, kc_lo, kc_hi;
   k_range(g, c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
-  const int dim = a.dim;
-  for (int u = warp; u < (b_hi - b_lo) * MT; u += kCW) {
-    const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
-    float v = 0.f;
-    if (m < a.M) {
-      float x = __ldcg(x_in + (size_t)m * dim + k);
-      if (part) {
-        float t = sum_part<MT>(part, nc_part, k, m);
-        if (bias) t = __fadd_rn(t, bias[k]);
-        x = __fadd_rn(x, t);
-      }
-      const int kc = (b_lo + bi) / kIB;
-      const bool owner = (long long)kc * g.n_vt >= c0 && (long long)kc * g.n_vt < c1;
-      if (owner) __stcg(x_out + (size_t)m * dim + k, x);
-      const float sq = warp_sum(x * x);
-      if (lane == 0) sm.ssb[bi][m] = sq;
-      v = __fmul_rn(x, gain[k]);
-    } else if (lane == 0) {
-      sm.ssb[bi][m] = 0.f;
+  const int dim = a.dim, n_units = (b_hi - b_lo) * MT;
+  const int npart = part ? nc_part : 0;
+  for (int u0 = warp; u0 < n_units; u0 += kUBResid * kCW) {
+    float xv[kUBResid], pv[kUBResid][kNCMax];
+#pragma unroll
+    for (int j = 0; j < kUBResid; j++) {
+      const int u = u0 + j * kCW, bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
+      const bool ok = u < n_units && m < a.M;
+      xv[j] = ok ? __ldcg(x_in + (size_t)m * dim + k) : 0.f;
+      const float* p = part + ((size_t)(k >> 4) * nc_part * MT + m) * 16 + (k & 15);
+#pragma unroll
+      for (int kc = 0; kc < kNCMax; kc++) pv[j][kc] = (ok && kc < npart) ? __ldcg(p + (size_t)kc * MT * 16) : 0.f;
     }
-    split_limbs<MT>(sm, warp, lane, bi, m, v);
+#pragma unroll
+    for (int j = 0; j < kUBResid; j++) {
+      const int u = u0 + j * kCW;
+      if (u >= n_units) break;
+      const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
+      float v = 0.f;
+      if (m < a.M) {
+        float x = xv[j];
+        if (npart) {
+          float t = 0.f;
+#pragma unroll
+          for (int kc = 0; kc < kNCMax; kc++)
+            if (kc < npart) t += pv[j][kc];
+          if (bias) t = __fadd_rn(t, bias[k]);
+          x = __fadd_rn(x, t);
+        }
+        const int kc = (b_lo + bi) / kIB;
+        const bool owner = (long long)kc * g.n_vt >= c0 && (long long)kc * g.n_vt < c1;
+        if (owner) __stcg(x_out + (size_t)m * dim + k, x);
+        const float sq = warp_sum(x * x);
+        if (lane == 0) sm.ssb[bi][m] = sq;
+        v = __fmul_rn(x, gain[k]);
+      } else if (lane == 0) {
+        sm.ssb[bi][m] = 0.f;
+      }
+      split_limbs<MT>(sm, warp, lane, bi, m, v);
+    }
   }
   bar_sync_n(1, kCT);
   // owners: the sum of squares of each owned chunk, its blocks added in order
@@ -322,9 +347,9 @@ __device__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g
 }
 
 // ---- P3 prologue: attention output for this CTA's k range (merge of the key-axis splits).
-// First, per (head, token), the splits' weights exp(m_s - max) and the denominator, one split
-// per lane; then per element the weighted sum of the splits' accumulators, every load issued
-// before the first add.
+// Each warp first issues the accumulator loads of its units (one split per register), then
+// computes, one split per lane, the weights exp(m_s - max) and the denominator of the
+// (head, token) pairs it owns; after a CTA barrier the units combine the two.
 template <int MT>
 __device__ void attn_out_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g, long long c0, long long c1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -337,62 +362,103 @@ __device__ void attn_out_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo
   };
   const int h_lo = (b_lo * 32) / hd;
   const int nh = b_hi > b_lo ? ((b_hi * 32 - 1) / hd) - h_lo + 1 : 0;
-  for (int u = warp; u < nh * MT; u += kCW) {
-    const int hl = u / MT, m = u % MT;
-    float ms = -INFINITY, ls = 0.f;
-    if (m < a.M && lane < ns) {
-      const float* p = head_base(m, h_lo + hl) + (size_t)lane * per;
-      ms = __ldcg(p + hd);
-      ls = __ldcg(p + hd + 1);
-    }
-    const float M_ = warp_max(ms);
-    const float w = ms == -INFINITY ? 0.f : expf(ms - M_);
-    const float L = warp_sum(ls * w);
-    sm.wts[hl][m][lane] = w;
-    if (lane == 0) sm.lsum[hl][m] = L;
-  }
-  bar_sync_n(1, kCT);
-  for (int u = warp; u < (b_hi - b_lo) * MT; u += kCW) {
-    const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
-    float v = 0.f;
-    if (m < a.M) {
-      const int h = k / hd, e = k % hd, hl = h - h_lo;
-      const float* p = head_base(m, h) + e;
-      float o[kMaxSplit];
+  const int n_units = (b_hi - b_lo) * MT;
+  for (int u0 = warp; u0 < n_units || u0 == warp; u0 += kUBAttn * kCW) {
+    float o[kUBAttn][kMaxSplit];
 #pragma unroll
-      for (int sp = 0; sp < kMaxSplit; sp++) o[sp] = sp < ns ? __ldcg(p + (size_t)sp * per) : 0.f;
-      float O = 0.f;
+    for (int j = 0; j < kUBAttn; j++) {
+      const int u = u0 + j * kCW, bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
+      const bool ok = u < n_units && m < a.M;
+      const float* p = ok ? head_base(m, k / hd) + k % hd : a.attn_part;
 #pragma unroll
-      for (int sp = 0; sp < kMaxSplit; sp++)
-        if (sp < ns) O = fmaf(o[sp], sm.wts[hl][m][sp], O);
-      v = __fdiv_rn(O, sm.lsum[hl][m]);
+      for (int sp = 0; sp < kMaxSplit; sp++) o[j][sp] = (ok && sp < ns) ? __ldcg(p + (size_t)sp * per) : 0.f;
     }
-    split_limbs<MT>(sm, warp, lane, bi, m, v);
+    if (u0 == warp) {  // the first batch: this warp's (head, token) weights, in the loads' shadow
+      for (int v = warp; v < nh * MT; v += kCW) {
+        const int hl = v / MT, m = v % MT;
+        float ms = -INFINITY, ls = 0.f;
+        if (m < a.M && lane < ns) {
+          const float* p = head_base(m, h_lo + hl) + (size_t)lane * per;
+          ms = __ldcg(p + hd);
+          ls = __ldcg(p + hd + 1);
+        }
+        const float M_ = warp_max(ms);
+        const float w = ms == -INFINITY ? 0.f : expf(ms - M_);
+        const float L = warp_sum(ls * w);
+        sm.wts[hl][m][lane] = w;
+        if (lane == 0) sm.lsum[hl][m] = L;
+      }
+      bar_sync_n(1, kCT);
+    }
+#pragma unroll
+    for (int j = 0; j < kUBAttn; j++) {
+      const int u = u0 + j * kCW;
+      if (u >= n_units) break;
+      const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
+      float v = 0.f;
+      if (m < a.M) {
+        const int hl = k / hd - h_lo;
+        float O = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplit; sp++)
+          if (sp < ns) O = fmaf(o[j][sp], sm.wts[hl][m][sp], O);
+        v = __fdiv_rn(O, sm.lsum[hl][m]);
+      }
+      split_limbs<MT>(sm, warp, lane, bi, m, v);
+    }
   }
   bar_sync_n(1, kCT);
 }
 
-// ---- P5 prologue: act = silu(g / den) * (u / den) for this CTA's k range
+// ---- P5 prologue: act = silu(g / den) * (u / den) for this CTA's k range; the partial loads
+// of a warp's units and warp 0's sum-of-squares loads go out together.
 template <int MT>
 __device__ void swiglu_prologue(Smem<MT>& sm, const StackArgs& a, const MatGeo& g, long long c0, long long c1,
                                 const float* part13, int nc13) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b_lo, b_hi, kc_lo, kc_hi;
   k_range(g, c0, c1, &b_lo, &b_hi, &kc_lo, &kc_hi);
-  rms_den_all<MT>(a, a.ss + (size_t)64 * MT, sm.den);
-  bar_sync_n(1, kCT);
-  for (int u = warp; u < (b_hi - b_lo) * MT; u += kCW) {
-    const int bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
-    float v = 0.f;
-    if (m < a.M) {
-      const float den = sm.den[m];
+  const int n_units = (b_hi - b_lo) * MT;
+  bool first = true;
+  for (int u0 = warp; u0 < n_units || first; u0 += kUBSwiglu * kCW) {
+    float gv[kUBSwiglu][kNCMax], uv[kUBSwiglu][kNCMax];
+#pragma unroll
+    for (int j = 0; j < kUBSwiglu; j++) {
+      const int u = u0 + j * kCW, bi = u / MT, m = u % MT, k = (b_lo + bi) * 32 + lane;
+      const bool ok = u < n_units && m < a.M;
       // tile j holds gate rows 8j..8j+7 (tile rows 0-7) and up rows 8j..8j+7 (rows 8-15)
       const int row_g = (k >> 3) * 16 + (k & 7);
-      const float gt = __fdiv_rn(sum_part<MT>(part13, nc13, row_g, m), den);
-      const float up = __fdiv_rn(sum_part<MT>(part13, nc13, row_g + 8, m), den);
-      v = __fmul_rn(silu_f(gt), up);
+      const float* p = part13 + ((size_t)(row_g >> 4) * nc13 * MT + m) * 16 + (row_g & 15);
+#pragma unroll
+      for (int kc = 0; kc < kNCMax; kc++) {
+        gv[j][kc] = (ok && kc < nc13) ? __ldcg(p + (size_t)kc * MT * 16) : 0.f;
+        uv[j][kc] = (ok && kc < nc13) ? __ldcg(p + (size_t)kc * MT * 16 + 8) : 0.f;
+      }
     }
-    split_limbs<MT>(sm, warp, lane, bi, m, v);
+    if (first) {
+      rms_den_all<MT>(a, a.ss + (size_t)64 * MT, sm.den);
+      bar_sync_n(1, kCT);
+      first = false;
+    }
+#pragma unroll
+    for (int j = 0; j < kUBSwiglu; j++) {
+      const int u = u0 + j * kCW;
+      if (u >= n_units) break;
+      const int bi = u / MT, m = u % MT;
+      float v = 0.f;
+      if (m < a.M) {
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int kc = 0; kc < kNCMax; kc++)
+          if (kc < nc13) {
+            gs += gv[j][kc];
+            us += uv[j][kc];
+          }
+        const float den = sm.den[m];
+        v = __fmul_rn(silu_f(__fdiv_rn(gs, den)), __fdiv_rn(us, den));
+      }
+      split_limbs<MT>(sm, warp, lane, bi, m, v);
+    }
   }
   bar_sync_n(1, kCT);
 }
@@ -479,14 +545,45 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
   KT* kb = reinterpret_cast<KT*>(a.kv + (size_t)layer * a.kv_layer_elems * sizeof(KT));
   KT* vb = kb + a.kv_layer_elems / 2;
 
+  // This warp's first key chunk: its page and K/V rows are requested first, so their latency
+  // overlaps the partial merges below (the new position itself comes from shared memory).
+  float kv0[KC][EPL], vv0[KC][EPL];
+  if (warp < n_chunks) {
+    const int base = t0 + warp * KC;
+    const int page = __ldcg(a.page_table + (size_t)seq * a.pt_stride + base / kPage);
+    const size_t row0 = ((size_t)(page * a.Hkv + g) * kPage + (base % kPage)) * HD + lane * EPL;
+#pragma unroll
+    for (int j = 0; j < KC; j++) {
+      if (base + j < t1 && !(own_new && base + j == pos)) {
+        kv_row<EPL>(kb + row0 + (size_t)j * HD, kv0[j]);
+        kv_row<EPL>(vb + row0 + (size_t)j * HD, vv0[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; e++) kv0[j][e] = vv0[j][e] = 0.f;
+      }
+    }
+  }
   // q rows of the group's heads (and, for the split that holds the new position, k and v):
-  // merged wqkv partials / den + bias
-  rms_den_all<MT>(a, a.ss, sm.den);
-  bar_sync_n(1, kCT);
-  const float den = sm.den[m];
+  // the merged wqkv partials, then / den + bias once warp 0 has the denominators
   const int n_rows = G * HD + (own_new ? 2 * HD : 0);
   // up to (8 + 2) * 128 rows over 256 threads: every thread's rows' loads go out together
   constexpr int kRowsPT = ((kMaxGroup + 2) * HD + kCT - 1) / kCT;
+  float raw[kRowsPT];
+#pragma unroll
+  for (int rr = 0; rr < kRowsPT; rr++) {
+    const int t = threadIdx.x + rr * kCT;
+    int row = 0;
+    if (t < G * HD)
+      row = (g * G + t / HD) * HD + t % HD;
+    else if (t < G * HD + HD)
+      row = (a.H + g) * HD + (t - G * HD);
+    else
+      row = (a.H + a.Hkv + g) * HD + (t - G * HD - HD);
+    raw[rr] = t < n_rows ? sum_part<MT>(part_qkv, nc_qkv, row, m) : 0.f;
+  }
+  rms_den_all<MT>(a, a.ss, sm.den);
+  bar_sync_n(1, kCT);
+  const float den = sm.den[m];
 #pragma unroll
   for (int rr = 0; rr < kRowsPT; rr++) {
     const int t = threadIdx.x + rr * kCT;
@@ -503,7 +600,7 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
         row = (a.H + a.Hkv + g) * HD + (t - G * HD - HD);
         dst = &sm.vbuf[t - G * HD - HD];
       }
-      float v = __fdiv_rn(sum_part<MT>(part_qkv, nc_qkv, row, m), den);
+      float v = __fdiv_rn(raw[rr], den);
       if (L.bqkv) v = __fadd_rn(v, L.bqkv[row]);
       *dst = v;
     }
@@ -538,24 +635,35 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
   }
   for (int c = warp; c < n_chunks; c += kCW) {
     const int base = t0 + c * KC;
-    const int page = __ldcg(a.page_table + (size_t)seq * a.pt_stride + base / kPage);
-    const size_t row0 = ((size_t)(page * a.Hkv + g) * kPage + (base % kPage)) * HD + lane * EPL;
     float kv[KC][EPL], vv[KC][EPL];
+    if (c == warp) {
 #pragma unroll
-    for (int j = 0; j < KC; j++) {
-      if (base + j < t1 && !(own_new && base + j == pos)) {
-        kv_row<EPL>(kb + row0 + (size_t)j * HD, kv[j]);
-        kv_row<EPL>(vb + row0 + (size_t)j * HD, vv[j]);
-      } else if (base + j == pos && own_new) {
+      for (int j = 0; j < KC; j++)
 #pragma unroll
-        for (int e = 0; e < EPL; e++) {
-          kv[j][e] = sm.kbuf[lane * EPL + e];
-          vv[j][e] = sm.vbuf[lane * EPL + e];
+        for (int e = 0; e < EPL; e++) kv[j][e] = kv0[j][e], vv[j][e] = vv0[j][e];
+    } else {
+      const int page = __ldcg(a.page_table + (size_t)seq * a.pt_stride + base / kPage);
+      const size_t row0 = ((size_t)(page * a.Hkv + g) * kPage + (base % kPage)) * HD + lane * EPL;
+#pragma unroll
+      for (int j = 0; j < KC; j++) {
+        if (base + j < t1 && !(own_new && base + j == pos)) {
+          kv_row<EPL>(kb + row0 + (size_t)j * HD, kv[j]);
+          kv_row<EPL>(vb + row0 + (size_t)j * HD, vv[j]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; e++) kv[j][e] = vv[j][e] = 0.f;
         }
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPL; e++) kv[j][e] = vv[j][e] = 0.f;
       }
+    }
+    if (own_new) {
+#pragma unroll
+      for (int j = 0; j < KC; j++)
+        if (base + j == pos)
+#pragma unroll
+          for (int e = 0; e < EPL; e++) {
+            kv[j][e] = sm.kbuf[lane * EPL + e];
+            vv[j][e] = sm.vbuf[lane * EPL + e];
+          }
     }
     float sc[KC][GM];
 #pragma unroll
@@ -665,7 +773,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     // ---- producer: one lane streams every item of every layer in consumption order ----
     if (threadIdx.x != kCT) return;
     // incremental slot / round / (k chunk, tile) counters: no division per item
-    int slot = 0, round = 0;
+    int slot = 0, round = 0, issued = 0;
     for (int l = 0; l < a.n_layer; l++) {
       const StackLayer& L = a.layers[l];
       const uint8_t* W[4] = {L.wqkv, L.wo, L.w13, L.w2};
@@ -676,6 +784,14 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
         int kc = (int)(c0 / g.n_vt), vt = (int)(c0 % g.n_vt);
         for (int n = (int)(c1 - c0); n > 0; n--) {
           if (round > 0) mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), a.err);
+          // at most kInflight items in flight: enough to keep HBM busy (Little's law), few
+          // enough that the phases' small dependent loads do not queue behind the stream
+          if (issued >= kInflight) {
+            int ps = slot - kInflight, pr = round;
+            if (ps < 0) ps += nslot, pr--;
+            mbar_wait_bounded(&full[ps], (uint32_t)(pr & 1), a.err);
+          }
+          issued++;
           const int nrec = min(kIB, g.nb - kc * kIB);
           const uint32_t bytes = (uint32_t)nrec * kQ8Rec;
           mbar_arrive_expect_tx(&full[slot], bytes);
