@@ -307,10 +307,12 @@ int sx_profile_gemv(sx_session* s, int32_t kind, int32_t n_launches);
 
 /* One launch of the persistent decode-stack kernel (the slow stack, or the fast one when
  * `fast`) for sequence 0 at its current position, with %globaltimer stamps in every CTA.
- * Writes phase_us_out[23]: [0] total us, [1] setup, [2] the final residual phase; then for
+ * Writes phase_us_out[28]: [0] total us, [1] setup, [2] the final residual phase; then for
  * each of the five phases p (wqkv, attention, wo, w1|w3, w2), averaged over the layers,
  * [3 + 4p + i]: i = 0 the phase, 1 the slowest CTA's prologue, 2 the slowest CTA's arrival
- * after the phase start, 3 the grid barrier (last arrival to the next phase's start). The
+ * after the phase start, 3 the grid barrier (last arrival to the next phase's start);
+ * [23..27] the attention steps of CTA 0 (merge loads, scaling, QK-norm / RoPE / KV append,
+ * the key loop, the write-out). The
  * step's K/V slot is written as a decode step would write it; the cache length does not
  * advance. */
 int sx_profile_stack(sx_session* s, int32_t fast, float* phase_us_out);

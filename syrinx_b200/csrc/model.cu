@@ -1599,11 +1599,11 @@ int profile_stack(sx_session* s, int fast, float* out) {
   const int L = a.n_layer;
   const size_t per = (size_t)L * 15 + 3;
   unsigned long long* tr = nullptr;
-  SX_CU(cudaMalloc((void**)&tr, per * sms * 8));
+  SX_CU(cudaMalloc((void**)&tr, (per + (size_t)L * 4) * sms * 8));
   a.trace = tr;
   cudaError_t e = launch_stack(a, sms, s->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
-  std::vector<unsigned long long> h(per * sms);
+  std::vector<unsigned long long> h((per + (size_t)L * 4) * sms);
   if (e == cudaSuccess) e = cudaMemcpy(h.data(), tr, h.size() * 8, cudaMemcpyDeviceToHost);
   cudaFree(tr);
   if (e != cudaSuccess) {
@@ -1613,7 +1613,7 @@ int profile_stack(sx_session* s, int fast, float* out) {
   auto T = [&](int cta, size_t i) { return (double)h[(size_t)cta * per + i]; };
   auto at = [&](int l, int p, int k) { return (size_t)1 + ((size_t)l * 5 + p) * 3 + k; };
   const size_t fin = 1 + (size_t)L * 15, end = 2 + (size_t)L * 15;
-  for (int i = 0; i < 23; i++) out[i] = 0.f;
+  for (int i = 0; i < 28; i++) out[i] = 0.f;
   out[0] = (float)((T(0, end) - T(0, 0)) * 1e-3);
   out[1] = (float)((T(0, at(0, 0, 0)) - T(0, 0)) * 1e-3);
   out[2] = (float)((T(0, end) - T(0, fin)) * 1e-3);
@@ -1631,6 +1631,18 @@ int profile_stack(sx_session* s, int fast, float* out) {
       out[3 + 4 * p + 2] += (float)((arr - start) * 1e-3 / L);
       out[3 + 4 * p + 3] += (float)((next - arr) * 1e-3 / L);
     }
+  // attention on CTA 0: merge loads + denominators, scale, norm/rope/append, key loop, write-out
+  const unsigned long long* sub = h.data() + per * sms;
+  for (int l = 0; l < L; l++) {
+    const double st = T(0, at(l, 1, 0)), en = T(0, at(l, 1, 1));
+    const double p0 = (double)sub[l * 4 + 0], p1 = (double)sub[l * 4 + 1], p2 = (double)sub[l * 4 + 2],
+                 p3 = (double)sub[l * 4 + 3];
+    out[23] += (float)((p0 - st) * 1e-3 / L);
+    out[24] += (float)((p1 - p0) * 1e-3 / L);
+    out[25] += (float)((p2 - p1) * 1e-3 / L);
+    out[26] += (float)((p3 - p2) * 1e-3 / L);
+    out[27] += (float)((en - p3) * 1e-3 / L);
+  }
   return check_err(s);
 }
 

@@ -524,7 +524,10 @@ __device__ __forceinline__ void kv_row(const __nv_bfloat16* p, float (&v)[EPL]) 
 
 template <int MT, int HD, typename KT>
 __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const StackLayer& L, int layer,
-                               const float* part_qkv, int nc_qkv) {
+                               const float* part_qkv, int nc_qkv, unsigned long long* sub) {
+  auto substamp = [&](int i) {
+    if (sub && threadIdx.x == 0) sub[i] = global_ns();
+  };
   constexpr int EPL = HD / 32;
   constexpr int GM = kMaxGroup;
   constexpr int KC = 4;
@@ -583,6 +586,7 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
   }
   rms_den_all<MT>(a, a.ss, sm.den);
   bar_sync_n(1, kCT);
+  substamp(0);
   const float den = sm.den[m];
 #pragma unroll
   for (int rr = 0; rr < kRowsPT; rr++) {
@@ -606,6 +610,7 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
     }
   }
   bar_sync_n(1, kCT);
+  substamp(1);
   for (int i = warp; i < G; i += kCW) norm_rope<HD>(sm.qs[i], L.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
   if (own_new && warp == kCW - 1) {
     norm_rope<HD>(sm.kbuf, L.kn, a.eps, a.inv_freq, a.interleaved, pos, lane);
@@ -619,6 +624,7 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
     }
   }
   bar_sync_n(1, kCT);
+  substamp(2);
 
   float qv[GM][EPL];
 #pragma unroll
@@ -706,6 +712,7 @@ __device__ void attention_unit(AttnSmem<HD>& sm, const StackArgs& a, const Stack
       m_w[i] = m_new;
     }
   }
+  substamp(3);
 #pragma unroll
   for (int i = 0; i < GM; i++) {
     if (i >= G) continue;
@@ -836,7 +843,10 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     // P2: attention
     grid_wait(a, target);
     stamp(l, 1, 0);
-    attention_unit<MT, HD, KT>(am, a, L, l, a.part0, G4[0].nc);
+    attention_unit<MT, HD, KT>(am, a, L, l, a.part0, G4[0].nc,
+                               tr ? a.trace + (size_t)gridDim.x * (a.n_layer * 15 + 3) +
+                                        ((size_t)blockIdx.x * a.n_layer + l) * 4
+                                  : nullptr);
     stamp(l, 1, 1);
     stamp(l, 1, 2);
     target = grid_arrive(a);

@@ -263,12 +263,14 @@ class B200DualAr:
     def profile_stack(self, fast: bool = False) -> dict:
         """Phase timing of one persistent-stack launch (us): total, per-layer mean of each
         phase, the final phase and the setup."""
-        out = np.zeros(23, np.float32)
+        out = np.zeros(28, np.float32)
         _lib.check(_lib.lib().sx_profile_stack(self.handle, int(fast), _p(out, C.c_float)))
         r = {"total": float(out[0]), "setup": float(out[1]), "final": float(out[2])}
         for p, name in enumerate(["wqkv", "attention", "wo", "w13", "w2"]):
             r[name] = {k: round(float(out[3 + 4 * p + i]), 2)
                        for i, k in enumerate(["phase", "prologue", "arrival", "barrier"])}
+        r["attention_cta0"] = {k: round(float(out[23 + i]), 2) for i, k in enumerate(
+            ["merge_loads", "scale", "norm_rope_append", "key_loop", "write"])}
         return r
 
     def seq_len(self, seq: int = 0) -> int:

@@ -48,7 +48,7 @@ def main():
             r = be.profile_stack(fast)
             print(("fast" if fast else "slow") + f" stack: total {r['total']:.1f} us, setup {r['setup']:.2f}, "
                   f"final {r['final']:.2f}")
-            for k in ("wqkv", "attention", "wo", "w13", "w2"):
+            for k in ("wqkv", "attention", "wo", "w13", "w2", "attention_cta0"):
                 print(f"  {k}: " + ", ".join(f"{n} {v:.2f}" for n, v in r[k].items()))
         be.decode_greedy(args.frames, mask_stop=True)
     elif args.what == "gemv":
