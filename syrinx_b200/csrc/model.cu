@@ -545,9 +545,11 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
   {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
-    const int hd_max = std::max(sl.head_dim, has_fast ? d.fast.head_dim : 0);
+    (void)sms;
+    size_t attn_floats = stack_attn_part_floats(kMaxTok, sl.n_head, sl.head_dim);
+    if (has_fast) attn_floats = std::max(attn_floats, stack_attn_part_floats(kMaxTok, d.fast.n_head, d.fast.head_dim));
     if ((rc = dalloc(s->allocs, &s->stack_xb, (size_t)max_batch * dim)) ||
-        (rc = dalloc(s->allocs, &s->stack_attn, stack_attn_part_floats(sms, hd_max))) ||
+        (rc = dalloc(s->allocs, &s->stack_attn, attn_floats)) ||
         (rc = dalloc(s->allocs, &s->stack_ss, (size_t)2 * kMaxTok * 64)) || (rc = dalloc(s->allocs, &s->stack_bar, 1)))
       return fail(rc);
     if (cudaMemset(s->stack_bar, 0, 8) != cudaSuccess) return fail(SX_E_CUDA);
@@ -806,7 +808,8 @@ bool stack_args(sx_session* s, bool fast, int M, float* resid, const int* tok_se
   int mt = 1;
   while (mt < M) mt <<= 1;
   size_t need = 0;
-  for (int i = 0; i < 4; i++) need = std::max(need, (size_t)a.geo[i].n_vt * a.geo[i].nc * mt * 16);
+  for (int i = 0; i < 4; i++) need = std::max(need, stack_part_floats(a.geo[i], mt));
+  need = (need + 3) & ~(size_t)3;  // keep the second buffer 16-byte aligned
   if (2 * need > s->q8_part_cap || !stack_supported(a, sms)) return false;
   a.part0 = s->q8_part;
   a.part1 = s->q8_part + need;
@@ -814,6 +817,7 @@ bool stack_args(sx_session* s, bool fast, int M, float* resid, const int* tok_se
   a.ss = s->stack_ss;
   a.bar = s->stack_bar;
   a.err = s->err;
+  if (const char* v = getenv("SYRINX_STACK_INFLIGHT")) a.inflight = atoi(v);  // profiling knob
   *out = a;
   return true;
 }

@@ -204,21 +204,23 @@ struct StackArgs {
   int n_split = 1;  // splits of the key axis per (token, kv head)
   float* x = nullptr;   // [M][dim] residual stream, updated in place
   float* xb = nullptr;  // [M][dim] scratch
-  float* part0 = nullptr;  // GEMV partials, two alternating buffers
+  float* part0 = nullptr;  // GEMV partials [M][rows][k chunks padded to 4], two alternating buffers
   float* part1 = nullptr;
-  float* attn_part = nullptr;  // [units][kMaxGroup][hd + 2]
+  float* attn_part = nullptr;  // [M][H][hd][splits] + [M][H][2][splits], splits padded to 4
   float* ss = nullptr;         // sums of squares per k chunk [2][8][64]
   unsigned long long* bar = nullptr;  // grid barrier counter (monotonic)
   int* err = nullptr;
   StackGeo geo[4];  // wqkv, wo, w1|w3, w2
   int nc_dim = 0;   // k chunks of dim
   int nslot = 0;    // ring slots (set by the launcher)
+  int inflight = 0;  // weight items the producer keeps in flight (0: the default)
   // profiling: non-null -> per CTA [n_layer * 15 + 3] %globaltimer stamps (start; per layer
   // and phase: phase start, prologue end, arrival; final phase start; end)
   unsigned long long* trace = nullptr;
 };
 bool stack_supported(const StackArgs& a, int sms);
-size_t stack_attn_part_floats(int sms, int hd);
+size_t stack_attn_part_floats(int max_tok, int H, int hd);
+size_t stack_part_floats(const StackGeo& g, int M);
 int stack_max_splits(int sms, int M, int Hkv);
 cudaError_t launch_stack(const StackArgs& a, int sms, cudaStream_t st);
 
