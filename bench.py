@@ -265,7 +265,7 @@ def bench_device(args):
         "e2e": {"value": round(K_e2e * world / (ms_e2e * 1e-3), 2), "unit": "frames/s",
                 "h2d_bytes_per_step": int(cfg.frame_width * 4), "d2h_bytes_per_step": int(cfg.frame_width * 4),
                 "api": "sx_frame_step_greedy (host frame in, host frame out, per frame)"},
-        "gpu_launches": kernels_per_frame(cfg, os.environ.get("SYRINX_STACK", "1") != "0") * K,
+        "gpu_launches": kernels_per_frame(cfg, os.environ.get("SYRINX_STACK", "0") == "1") * K,
         "clocks": clk.summary(),
         "load_s": round(t_load, 1),
         "prefill_s": round(t_prefill, 3),
@@ -360,7 +360,7 @@ def bench_tp(args):
         "hbm_roofline": {"bytes_per_frame_per_gpu": per_gpu, "frac_of_peak": round(per_gpu * value / (peak * 1e9), 4),
                          "peak_gbs": peak, "peak_kind": peak_kind,
                          "note": "layers and KV divided over the ranks; semantic head and fast_output replicated"},
-        "gpu_launches": kernels_per_frame(cfg, world == 1 and os.environ.get("SYRINX_STACK", "1") != "0") * K,
+        "gpu_launches": kernels_per_frame(cfg, world == 1 and os.environ.get("SYRINX_STACK", "0") == "1") * K,
         "clocks": clk.summary(), "prefill_s": round(t_prefill, 2),
     }
     if world > 1:

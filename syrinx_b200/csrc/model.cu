@@ -554,7 +554,7 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
       return fail(rc);
     if (cudaMemset(s->stack_bar, 0, 8) != cudaSuccess) return fail(SX_E_CUDA);
     const char* env = getenv("SYRINX_STACK");
-    s->stack_enabled = !(env && env[0] == '0');
+    s->stack_enabled = env && env[0] == '1';
   }
   if (m->tp_size > 1) {
     // receive region rx [2][kMaxTp][xb_cap] 8-byte words; peers map it by IPC

@@ -85,7 +85,7 @@ struct sx_session {
   float* stack_attn = nullptr;
   float* stack_ss = nullptr;
   unsigned long long* stack_bar = nullptr;
-  bool stack_enabled = true;  // SYRINX_STACK=0 selects the per-kernel chain (for comparison)
+  bool stack_enabled = false;  // SYRINX_STACK=1 selects the persistent stack kernel
   // tensor parallelism: the receive region (rx [2][kMaxTp][xb_cap] 8-byte words) peers map
   // through CUDA IPC, and the communicator the residual merges use
   void* tp_region = nullptr;

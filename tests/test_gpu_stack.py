@@ -1,8 +1,9 @@
 """The persistent decode kernel (stack.cu: every layer of a stack in one cooperative launch,
 weights streamed through a shared-memory ring) against the per-kernel chain it replaces and
-against the oracle. SYRINX_STACK=0, read when a session is created, selects the chain. The
-two paths add the same exact block sums in different orders (and apply the RMSNorm after the
-GEMV instead of before), so logits agree to f32 rounding and greedy frames are identical."""
+against the oracle. SYRINX_STACK=1, read when a session is created, selects the persistent
+kernel; the chain is the default. The two paths add the same exact block sums in different
+orders (and apply the RMSNorm after the GEMV instead of before), so logits agree to f32
+rounding and greedy frames are identical."""
 import os
 
 import numpy as np
