@@ -818,6 +818,7 @@ bool stack_args(sx_session* s, bool fast, int M, float* resid, const int* tok_se
   a.bar = s->stack_bar;
   a.err = s->err;
   if (const char* v = getenv("SYRINX_STACK_INFLIGHT")) a.inflight = atoi(v);  // profiling knob
+  if (const char* v = getenv("SYRINX_STACK_L2")) a.l2_ahead = atoi(v);        // profiling knob
   *out = a;
   return true;
 }

@@ -65,6 +65,7 @@ constexpr int kInflight = 10;            // weight items a CTA's producer keeps 
 constexpr int kSpanHeads = 16;           // attention heads a CTA's wo k range may touch
 constexpr int kUB = 2;                   // prologue units (block, token) gathered per batch
 constexpr uint64_t kBarWaitNs = 2000000000ull;  // grid / mbarrier wait limit
+constexpr int kStackMaxLayers = 64;              // layers whose weight pointers the producer keeps
 
 __host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
 
@@ -161,6 +162,7 @@ struct AttnSmem {
 struct Common {  // outside the union of the two
   Plan plan[4];
   float den[kMaxTok];
+  const uint8_t* wptr[kStackMaxLayers][4];  // every layer's wqkv, wo, w1|w3, w2 (for the producer)
 };
 
 template <int MT, int HD>
@@ -224,6 +226,24 @@ __device__ __forceinline__ float sum_row(const float4 (&v)[kNQ], int nc) {
     if (4 * q + 2 < nc) s += v[q].z;
     if (4 * q + 3 < nc) s += v[q].w;
   }
+  return s;
+}
+
+// The same for rows of at most 8 chunks (the matrices whose K is the model width).
+__device__ __forceinline__ void load_row2(const float* p, bool ok, int nq, float4 (&v)[2]) {
+  v[0] = ok ? __ldcg(reinterpret_cast<const float4*>(p)) : float4{0.f, 0.f, 0.f, 0.f};
+  v[1] = (ok && nq > 1) ? __ldcg(reinterpret_cast<const float4*>(p) + 1) : float4{0.f, 0.f, 0.f, 0.f};
+}
+__device__ __forceinline__ float sum_row2(const float4 (&v)[2], int nc) {
+  float s = 0.f;
+  if (nc > 0) s += v[0].x;
+  if (nc > 1) s += v[0].y;
+  if (nc > 2) s += v[0].z;
+  if (nc > 3) s += v[0].w;
+  if (nc > 4) s += v[1].x;
+  if (nc > 5) s += v[1].y;
+  if (nc > 6) s += v[1].z;
+  if (nc > 7) s += v[1].w;
   return s;
 }
 
@@ -308,27 +328,45 @@ __device__ __noinline__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t*
 
 // ---- residual prologue (P1 and P4): x_new = x + partials (+ bias) for this CTA's k range;
 // the owner of each k chunk writes x_new and the chunk's sum of squares; limbs of x_new * g.
-// `pg` is the geometry of the matrix whose partials are added (null: none).
+// `pg` is the geometry of the matrix whose partials are added (null: none). x, the gains and
+// the bias do not depend on the phase that just ended, so the first batch requests them before
+// the grid barrier (`target`, 0: no wait); the partials go out right after it, and at batch 1
+// every unit of this CTA is in one batch, so the prologue costs one round trip to L2.
 template <int MT>
 __device__ __noinline__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, const StackGeo& g, const Plan& p,
                                             const float* x_in, float* x_out, const float* part,
-                                            const StackGeo* pg, const float* bias, const float* gain, float* ss_out) {
+                                            const StackGeo* pg, const float* bias, const float* gain, float* ss_out,
+                                            unsigned long long target, unsigned long long* ts) {
+  constexpr int UB = MT == 1 ? 4 : 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dim = a.dim, n_units = (p.b_hi - p.b_lo) * MT;
   const int nq = pg ? pad4(pg->nc) / 4 : 0, nc = pg ? pg->nc : 0;
+  bool first = true;
 #pragma unroll 1
-  for (int u0 = warp; u0 < n_units; u0 += kUB * kCW) {
-    float xv[kUB];
-    float4 pv[kUB][kNQ];
+  for (int u0 = warp; u0 < n_units || first; u0 += UB * kCW) {
+    float xv[UB], gv[UB], bv[UB];
+    float4 pv[UB][kNQ];
 #pragma unroll
-    for (int j = 0; j < kUB; j++) {  // every load of the batch first
+    for (int j = 0; j < UB; j++) {  // what the ended phase did not write
       const int u = u0 + j * kCW, m = u % MT, k = (p.b_lo + u / MT) * 32 + lane;
       const bool ok = u < n_units && m < a.M;
       xv[j] = ok ? __ldcg(x_in + (size_t)m * dim + k) : 0.f;
+      gv[j] = ok ? gain[k] : 0.f;
+      bv[j] = (ok && bias) ? bias[k] : 0.f;
+    }
+    if (first) {
+      if (target) grid_wait(a, target);
+      if (ts && threadIdx.x == 0) *ts = global_ns();  // profiling: the phase starts here
+      first = false;
+    }
+#pragma unroll
+    for (int j = 0; j < UB; j++) {  // the partials of the ended phase
+      const int u = u0 + j * kCW, m = u % MT, k = (p.b_lo + u / MT) * 32 + lane;
+      const bool ok = u < n_units && m < a.M;
       load_row(pg ? part_row(part, *pg, m, k) : x_in, ok && pg, nq, pv[j]);
     }
 #pragma unroll 1
-    for (int j = 0; j < kUB; j++) {
+    for (int j = 0; j < UB; j++) {
       const int u = u0 + j * kCW;
       if (u >= n_units) break;
       const int bi = u / MT, m = u % MT, k = (p.b_lo + bi) * 32 + lane;
@@ -337,13 +375,13 @@ __device__ __noinline__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, co
         float x = xv[j];
         if (pg) {
           float t = sum_row(pv[j], nc);
-          if (bias) t = __fadd_rn(t, bias[k]);
+          if (bias) t = __fadd_rn(t, bv[j]);
           x = __fadd_rn(x, t);
         }
         if (owns_chunk(p, g, (p.b_lo + bi) / kIB)) __stcg(x_out + (size_t)m * dim + k, x);
         const float sq = warp_sum(x * x);
         if (lane == 0) sm.ssb[bi][m] = sq;
-        v = __fmul_rn(x, gain[k]);
+        v = __fmul_rn(x, gv[j]);
       } else if (lane == 0) {
         sm.ssb[bi][m] = 0.f;
       }
@@ -444,18 +482,19 @@ __device__ __noinline__ void swiglu_prologue(Smem<MT>& sm, Common& cm, const Sta
                                              const float* part13, const StackGeo& g13) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = (p.b_hi - p.b_lo) * MT, nq = pad4(g13.nc) / 4;
+  constexpr int UB = MT == 1 ? 4 : 2;
   bool first = true;
 #pragma unroll 1
-  for (int u0 = warp; u0 < n_units || first; u0 += kUB * kCW) {
-    float4 gv[kUB][kNQ], uv[kUB][kNQ];
+  for (int u0 = warp; u0 < n_units || first; u0 += UB * kCW) {
+    float4 gv[UB][2], uv[UB][2];
 #pragma unroll
-    for (int j = 0; j < kUB; j++) {
+    for (int j = 0; j < UB; j++) {
       const int u = u0 + j * kCW, m = u % MT, k = (p.b_lo + u / MT) * 32 + lane;
       const bool ok = u < n_units && m < a.M;
       // tile j holds gate rows 8j..8j+7 (tile rows 0-7) and up rows 8j..8j+7 (rows 8-15)
       const int row_g = (k >> 3) * 16 + (k & 7);
-      load_row(part_row(part13, g13, m, row_g), ok, nq, gv[j]);
-      load_row(part_row(part13, g13, m, row_g + 8), ok, nq, uv[j]);
+      load_row2(part_row(part13, g13, m, row_g), ok, nq, gv[j]);
+      load_row2(part_row(part13, g13, m, row_g + 8), ok, nq, uv[j]);
     }
     if (first) {
       rms_den_all<MT>(a, a.ss + (size_t)64 * MT, cm.den);
@@ -463,14 +502,14 @@ __device__ __noinline__ void swiglu_prologue(Smem<MT>& sm, Common& cm, const Sta
       first = false;
     }
 #pragma unroll 1
-    for (int j = 0; j < kUB; j++) {
+    for (int j = 0; j < UB; j++) {
       const int u = u0 + j * kCW;
       if (u >= n_units) break;
       const int bi = u / MT, m = u % MT;
       float v = 0.f;
       if (m < a.M) {
         const float den = cm.den[m];
-        v = __fmul_rn(silu_f(__fdiv_rn(sum_row(gv[j], g13.nc), den)), __fdiv_rn(sum_row(uv[j], g13.nc), den));
+        v = __fmul_rn(silu_f(__fdiv_rn(sum_row2(gv[j], g13.nc), den)), __fdiv_rn(sum_row2(uv[j], g13.nc), den));
       }
       split_limbs<MT>(sm, warp, lane, bi, m, v);
     }
@@ -781,33 +820,85 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     mbar_fence_init();
     for (int i = 0; i < 4; i++) cm.plan[i] = make_plan(a.geo[i]);
   }
+  for (int l = threadIdx.x; l < a.n_layer; l += blockDim.x) {
+    const StackLayer& L = a.layers[l];
+    cm.wptr[l][0] = L.wqkv;
+    cm.wptr[l][1] = L.wo;
+    cm.wptr[l][2] = L.w13;
+    cm.wptr[l][3] = L.w2;
+  }
   __syncthreads();
   pdl_launch_dependents();
   pdl_wait();
 
   if (threadIdx.x >= kCT) {
     // ---- producer: one lane streams every item of every layer in consumption order ----
+    // Besides the ring it runs an L2 prefetch cursor up to a.l2_ahead items ahead of the ring
+    // (cp.async.bulk.prefetch.L2 of this GPU's own memory): while the consumers sit in a grid
+    // barrier, a prologue or attention and the ring is full, HBM keeps streaming into L2, and
+    // the ring refills from L2 when they resume.
     if (threadIdx.x != kCT) return;
     int slot = 0, round = 0, issued = 0;
+    int pl = 0, pm = 0, pn = cm.plan[0].n, pkc = cm.plan[0].kc0, pvt = cm.plan[0].vt0, pf = 0;
+    bool pf_done = a.l2_ahead <= 0;
+    // advance the prefetch cursor by one item, prefetching it unless the ring has it already
+    auto pf_one = [&]() {
+      while (pn == 0) {
+        if (++pm == 4) {
+          pm = 0;
+          if (++pl == a.n_layer) {
+            pf_done = true;
+            return;
+          }
+        }
+        pn = cm.plan[pm].n;
+        pkc = cm.plan[pm].kc0;
+        pvt = cm.plan[pm].vt0;
+      }
+      const StackGeo& g = a.geo[pm];
+      if (pf >= issued) {
+        const int nrec = min(kIB, g.nb - pkc * kIB);
+        bulk_prefetch_l2(cm.wptr[pl][pm] + ((size_t)pvt * g.nb + (size_t)pkc * kIB) * kQ8Rec, (uint32_t)nrec * kQ8Rec);
+      }
+      pn--;
+      pf++;
+      if (++pvt == g.n_vt) pvt = 0, pkc++;
+    };
+    // bounded wait on a ring mbarrier that prefetches while it waits
+    auto pwait = [&](uint64_t* bar, uint32_t parity) {
+      if (mbar_try_wait(bar, parity)) return;
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(bar, parity)) {
+        if (!pf_done && pf < issued + a.l2_ahead) {
+          pf_one();
+          continue;
+        }
+        const uint64_t dt = global_ns() - t0;
+        if (dt > 1000000ull && __ldcg(a.err) != 0) return;
+        if (dt > kBarWaitNs) {
+          atomicExch(a.err, 2);
+          return;
+        }
+      }
+    };
     for (int l = 0; l < a.n_layer; l++) {
-      const StackLayer& L = a.layers[l];
-      const uint8_t* W[4] = {L.wqkv, L.wo, L.w13, L.w2};
       for (int mi = 0; mi < 4; mi++) {
         const StackGeo& g = a.geo[mi];
         const Plan& p = cm.plan[mi];
+        const uint8_t* W = cm.wptr[l][mi];
         int kc = p.kc0, vt = p.vt0;
         for (int n = p.n; n > 0; n--) {
-          if (round > 0) mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), a.err);
+          if (round > 0) pwait(&empty[slot], (uint32_t)((round - 1) & 1));
           if (issued >= a.inflight) {  // keep at most `inflight` items in flight
             int ps = slot - a.inflight, pr = round;
             if (ps < 0) ps += nslot, pr--;
-            mbar_wait_bounded(&full[ps], (uint32_t)(pr & 1), a.err);
+            pwait(&full[ps], (uint32_t)(pr & 1));
           }
           issued++;
           const int nrec = min(kIB, g.nb - kc * kIB);
           const uint32_t bytes = (uint32_t)nrec * kQ8Rec;
           mbar_arrive_expect_tx(&full[slot], bytes);
-          bulk_g2s(ring + (size_t)slot * kItemBytes, W[mi] + ((size_t)vt * g.nb + (size_t)kc * kIB) * kQ8Rec, bytes,
+          bulk_g2s(ring + (size_t)slot * kItemBytes, W + ((size_t)vt * g.nb + (size_t)kc * kIB) * kQ8Rec, bytes,
                    &full[slot]);
           if (++slot == nslot) slot = 0, round++;
           if (++vt == g.n_vt) vt = 0, kc++;
@@ -832,11 +923,9 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
   const Plan* P = cm.plan;
   for (int l = 0; l < a.n_layer; l++) {
     const StackLayer& L = a.layers[l];
-    // P1: wqkv (x += previous layer's w2 partials)
-    if (l > 0) grid_wait(a, target);
-    stamp(l, 0, 0);
+    // P1: wqkv (x += previous layer's w2 partials); the grid barrier is inside the prologue
     resid_prologue<MT>(sm, a, a.geo[0], P[0], xa, xb, a.part1, l > 0 ? &a.geo[3] : nullptr, nullptr, L.attn_norm,
-                       a.ss);
+                       a.ss, l > 0 ? target : 0ull, tr ? tr + 1 + (l * 5 + 0) * 3 : nullptr);
     stamp(l, 0, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, a.geo[0], P[0], a.part0, a.err);
     stamp(l, 0, 2);
@@ -859,10 +948,9 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, a.geo[1], P[1], a.part1, a.err);
     stamp(l, 2, 2);
     target = grid_arrive(a);
-    // P4: w1|w3 (x += wo partials + bias)
-    grid_wait(a, target);
-    stamp(l, 3, 0);
-    resid_prologue<MT>(sm, a, a.geo[2], P[2], xb, xa, a.part1, &a.geo[1], L.bo, L.ffn_norm, a.ss + (size_t)64 * MT);
+    // P4: w1|w3 (x += wo partials + bias); the grid barrier is inside the prologue
+    resid_prologue<MT>(sm, a, a.geo[2], P[2], xb, xa, a.part1, &a.geo[1], L.bo, L.ffn_norm, a.ss + (size_t)64 * MT,
+                       target, tr ? tr + 1 + (l * 5 + 3) * 3 : nullptr);
     stamp(l, 3, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, a.geo[2], P[2], a.part0, a.err);
     stamp(l, 3, 2);
@@ -936,6 +1024,7 @@ cudaError_t launch_m(const StackArgs& a, int sms, cudaStream_t st) {
 // ranges per CTA span at most kSpanBlocks k blocks in every matrix.
 bool stack_supported(const StackArgs& a, int sms) {
   if (a.M < 1 || a.M > 8 || (a.hd != 64 && a.hd != 128) || a.H % a.Hkv || a.H / a.Hkv > kMaxGroup) return false;
+  if (a.n_layer < 1 || a.n_layer > kStackMaxLayers) return false;
   if (a.dim % 32 || a.nc_dim > 64 || a.M * a.Hkv > sms || a.n_split > kMaxSplit) return false;
   // a k range is whole 512-wide chunks, so it covers whole heads: at most 1024 / hd of them
   if (kSpanBlocks * 32 / a.hd > kSpanHeads) return false;

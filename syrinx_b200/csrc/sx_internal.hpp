@@ -214,6 +214,7 @@ struct StackArgs {
   int nc_dim = 0;   // k chunks of dim
   int nslot = 0;    // ring slots (set by the launcher)
   int inflight = 0;  // weight items the producer keeps in flight (0: the default)
+  int l2_ahead = 0;  // items the producer's L2 prefetch cursor may run ahead of the ring (0: off)
   // profiling: non-null -> per CTA [n_layer * 15 + 3] %globaltimer stamps (start; per layer
   // and phase: phase start, prologue end, arrival; final phase start; end)
   unsigned long long* trace = nullptr;
