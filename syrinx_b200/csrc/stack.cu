@@ -99,7 +99,7 @@ __device__ __forceinline__ bool owns_chunk(const Plan& p, const StackGeo& g, int
 // ---- grid barrier ---------------------------------------------------------------------
 // Arrive: every consumer thread's writes are ordered by the named barrier, thread 0 counts the
 // CTA in with a release at GPU scope (cumulative over what the named barrier ordered before
-// it). Returns the count that completes the barrier.
+// it). Returns, on thread 0 only, the count that completes the barrier (0 on every other thread).
 __device__ __forceinline__ unsigned long long grid_arrive(const StackArgs& a) {
   bar_sync_n(1, kCT);
   unsigned long long target = 0;
@@ -330,13 +330,13 @@ __device__ __noinline__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t*
 // the owner of each k chunk writes x_new and the chunk's sum of squares; limbs of x_new * g.
 // `pg` is the geometry of the matrix whose partials are added (null: none). x, the gains and
 // the bias do not depend on the phase that just ended, so the first batch requests them before
-// the grid barrier (`target`, 0: no wait); the partials go out right after it, and at batch 1
+// the grid barrier (when `wait`); the partials go out right after it, and at batch 1
 // every unit of this CTA is in one batch, so the prologue costs one round trip to L2.
 template <int MT>
 __device__ __noinline__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, const StackGeo& g, const Plan& p,
                                             const float* x_in, float* x_out, const float* part,
                                             const StackGeo* pg, const float* bias, const float* gain, float* ss_out,
-                                            unsigned long long target, unsigned long long* ts) {
+                                            bool wait, unsigned long long target, unsigned long long* ts) {
   constexpr int UB = MT == 1 ? 4 : 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dim = a.dim, n_units = (p.b_hi - p.b_lo) * MT;
@@ -355,7 +355,7 @@ __device__ __noinline__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, co
       bv[j] = (ok && bias) ? bias[k] : 0.f;
     }
     if (first) {
-      if (target) grid_wait(a, target);
+      if (wait) grid_wait(a, target);  // `wait` is uniform; `target` is thread 0's alone
       if (ts && threadIdx.x == 0) *ts = global_ns();  // profiling: the phase starts here
       first = false;
     }
@@ -925,7 +925,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     const StackLayer& L = a.layers[l];
     // P1: wqkv (x += previous layer's w2 partials); the grid barrier is inside the prologue
     resid_prologue<MT>(sm, a, a.geo[0], P[0], xa, xb, a.part1, l > 0 ? &a.geo[3] : nullptr, nullptr, L.attn_norm,
-                       a.ss, l > 0 ? target : 0ull, tr ? tr + 1 + (l * 5 + 0) * 3 : nullptr);
+                       a.ss, l > 0, target, tr ? tr + 1 + (l * 5 + 0) * 3 : nullptr);
     stamp(l, 0, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, a.geo[0], P[0], a.part0, a.err);
     stamp(l, 0, 2);
@@ -950,7 +950,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
     target = grid_arrive(a);
     // P4: w1|w3 (x += wo partials + bias); the grid barrier is inside the prologue
     resid_prologue<MT>(sm, a, a.geo[2], P[2], xb, xa, a.part1, &a.geo[1], L.bo, L.ffn_norm, a.ss + (size_t)64 * MT,
-                       target, tr ? tr + 1 + (l * 5 + 3) * 3 : nullptr);
+                       true, target, tr ? tr + 1 + (l * 5 + 3) * 3 : nullptr);
     stamp(l, 3, 1);
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, a.geo[2], P[2], a.part0, a.err);
     stamp(l, 3, 2);
