@@ -337,7 +337,7 @@ __device__ __noinline__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, co
                                             const float* x_in, float* x_out, const float* part,
                                             const StackGeo* pg, const float* bias, const float* gain, float* ss_out,
                                             bool wait, unsigned long long target, unsigned long long* ts) {
-  constexpr int UB = MT == 1 ? 4 : 2;
+  constexpr int UB = MT == 1 ? 3 : 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dim = a.dim, n_units = (p.b_hi - p.b_lo) * MT;
   const int nq = pg ? pad4(pg->nc) / 4 : 0, nc = pg ? pg->nc : 0;
@@ -365,7 +365,7 @@ __device__ __noinline__ void resid_prologue(Smem<MT>& sm, const StackArgs& a, co
       const bool ok = u < n_units && m < a.M;
       load_row(pg ? part_row(part, *pg, m, k) : x_in, ok && pg, nq, pv[j]);
     }
-#pragma unroll 1
+#pragma unroll  // constant indices keep the batch in registers (not local memory)
     for (int j = 0; j < UB; j++) {
       const int u = u0 + j * kCW;
       if (u >= n_units) break;
@@ -451,7 +451,7 @@ __device__ __noinline__ void attn_out_prologue(Smem<MT>& sm, const StackArgs& a,
       bar_sync_n(1, kCT);
       first = false;
     }
-#pragma unroll 1
+#pragma unroll  // constant indices keep the batch in registers (not local memory)
     for (int j = 0; j < kUB; j++) {
       const int u = u0 + j * kCW;
       if (u >= n_units) break;
@@ -482,7 +482,7 @@ __device__ __noinline__ void swiglu_prologue(Smem<MT>& sm, Common& cm, const Sta
                                              const float* part13, const StackGeo& g13) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = (p.b_hi - p.b_lo) * MT, nq = pad4(g13.nc) / 4;
-  constexpr int UB = MT == 1 ? 4 : 2;
+  constexpr int UB = MT == 1 ? 3 : 2;
   bool first = true;
 #pragma unroll 1
   for (int u0 = warp; u0 < n_units || first; u0 += UB * kCW) {
@@ -501,7 +501,7 @@ __device__ __noinline__ void swiglu_prologue(Smem<MT>& sm, Common& cm, const Sta
       bar_sync_n(1, kCT);
       first = false;
     }
-#pragma unroll 1
+#pragma unroll  // constant indices keep the batch in registers (not local memory)
     for (int j = 0; j < UB; j++) {
       const int u = u0 + j * kCW;
       if (u >= n_units) break;
@@ -801,7 +801,7 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
 
 // ---- the kernel ------------------------------------------------------------------------
 template <int MT, int HD, typename KT>
-__global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const StackArgs a) {
+__global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constant__ StackArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nslot = a.nslot;
   uint8_t* ring = smem;
