@@ -69,6 +69,11 @@ constexpr int kStackMaxLayers = 64;              // layers whose weight pointers
 
 __host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
 
+// matrix mi (0 wqkv, 1 wo, 2 w1|w3, 3 w2) of a layer
+__device__ __forceinline__ const uint8_t* layer_w(const StackLayer& L, int mi) {
+  return mi == 0 ? L.wqkv : mi == 1 ? L.wo : mi == 2 ? L.w13 : L.w2;
+}
+
 // This CTA's share of one matrix: items [c0, c0 + n) in k-chunk-major order
 struct Plan {
   int c0, n;          // first item, item count
@@ -158,11 +163,17 @@ struct AttnSmem {
   float wacc[kCW][kMaxGroup][HD];
   float wm[kCW][kMaxGroup], wl[kCW][kMaxGroup];
   float kbuf[HD], vbuf[HD];
+  float qn[HD], kn[HD];  // QK-norm weights of the layer
 };
+// Everything the kernel reads more than once that does not change during the launch lives in
+// shared memory: with the ring taking most of the SM's 256 KB, L1 keeps almost nothing, and a
+// miss costs a full L2 round trip.
 struct Common {  // outside the union of the two
+  StackArgs args;                     // the launch arguments
+  StackLayer lay[kStackMaxLayers];    // every layer's weight and vector pointers
+  float inv_freq[64];                 // RoPE inverse frequencies (head_dim / 2 <= 64)
   Plan plan[4];
   float den[kMaxTok];
-  const uint8_t* wptr[kStackMaxLayers][4];  // every layer's wqkv, wo, w1|w3, w2 (for the producer)
 };
 
 template <int MT, int HD>
@@ -579,6 +590,7 @@ __device__ __forceinline__ void kv_row(const __nv_bfloat16* p, float (&v)[EPL]) 
 template <int MT, int HD, typename KT>
 __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const StackArgs& a, const StackLayer& L,
                                             int layer, const float* part_qkv, const StackGeo& gq,
+                                            unsigned long long target, unsigned long long* ts,
                                             unsigned long long* sub) {
   constexpr int EPL = HD / 32;
   constexpr int GQ = 4;  // query heads per compute pass
@@ -589,7 +601,17 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ns = a.n_split;
   const int unit = blockIdx.x;
-  if (unit >= a.M * a.Hkv * ns) return;
+  // The grid barrier that ends the wqkv phase is taken inside (by every consumer thread of
+  // every CTA): what does not depend on that phase (positions, pages, the first keys and values,
+  // norm weights, biases) is requested before it.
+  auto wait_phase = [&]() {
+    grid_wait(a, target);
+    if (ts && threadIdx.x == 0) *ts = global_ns();  // profiling: the phase starts here
+  };
+  if (unit >= a.M * a.Hkv * ns) {
+    wait_phase();
+    return;
+  }
   const int m = unit / (a.Hkv * ns), g = (unit / ns) % a.Hkv, s = unit % ns;
   const int G = a.H / a.Hkv;
   const int seq = a.tok_seq ? __ldcg(a.tok_seq + m) : 0;
@@ -633,6 +655,18 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
     if (t < G * HD + HD) return (a.H + g) * HD + (t - G * HD);
     return (a.H + a.Hkv + g) * HD + (t - G * HD - HD);
   };
+  float bq[kRowsPT];
+#pragma unroll
+  for (int rr = 0; rr < kRowsPT; rr++) {
+    const int t = threadIdx.x + rr * kCT;
+    bq[rr] = (L.bqkv && t < n_rows) ? L.bqkv[row_of(t)] : 0.f;
+  }
+  for (int e = threadIdx.x; e < HD; e += kCT) {
+    if (L.qn) sm.qn[e] = L.qn[e];
+    if (L.kn) sm.kn[e] = L.kn[e];
+  }
+  const int new_page = own_new ? __ldcg(a.page_table + (size_t)seq * a.pt_stride + pos / kPage) : 0;
+  wait_phase();
   float4 pv[kRowsPT][2];  // wqkv has at most 8 k chunks here (gq.nc <= 8, checked on the host)
 #pragma unroll
   for (int rr = 0; rr < kRowsPT; rr++) {
@@ -657,7 +691,7 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
         if (i < gq.nc) raw += c[i];
       const int row = row_of(t);
       float v = __fdiv_rn(raw, den);
-      if (L.bqkv) v = __fadd_rn(v, L.bqkv[row]);
+      if (L.bqkv) v = __fadd_rn(v, bq[rr]);
       float* dst = t < G * HD        ? &sm.qs[t / HD][t % HD]
                    : t < G * HD + HD ? &sm.kbuf[t - G * HD]
                                      : &sm.vbuf[t - G * HD - HD];
@@ -666,11 +700,11 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
   }
   bar_sync_n(1, kCT);
   substamp(1);
-  for (int i = warp; i < G; i += kCW) norm_rope<HD>(sm.qs[i], L.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
+  for (int i = warp; i < G; i += kCW)
+    norm_rope<HD>(sm.qs[i], L.qn ? sm.qn : nullptr, a.eps, cm.inv_freq, a.interleaved, pos, lane);
   if (own_new && warp == kCW - 1) {
-    norm_rope<HD>(sm.kbuf, L.kn, a.eps, a.inv_freq, a.interleaved, pos, lane);
-    const int page = __ldcg(a.page_table + (size_t)seq * a.pt_stride + pos / kPage);
-    const size_t off = ((size_t)(page * a.Hkv + g) * kPage + (pos % kPage)) * HD;
+    norm_rope<HD>(sm.kbuf, L.kn ? sm.kn : nullptr, a.eps, cm.inv_freq, a.interleaved, pos, lane);
+    const size_t off = ((size_t)(new_page * a.Hkv + g) * kPage + (pos % kPage)) * HD;
     for (int e = lane; e < HD; e += 32) {
       kv_put(kb + off + e, sm.kbuf[e]);
       kv_put(vb + off + e, sm.vbuf[e]);
@@ -801,13 +835,14 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
 
 // ---- the kernel ------------------------------------------------------------------------
 template <int MT, int HD, typename KT>
-__global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constant__ StackArgs a) {
+__global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constant__ StackArgs a_in) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int nslot = a.nslot;
+  const int nslot = a_in.nslot;
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nslot * kItemBytes);
   uint64_t* empty = full + nslot;
   Common& cm = *reinterpret_cast<Common*>(empty + nslot);
+  const StackArgs& a = cm.args;
   uint8_t* scratch = reinterpret_cast<uint8_t*>(&cm) + ((sizeof(Common) + 15) & ~(size_t)15);
   Smem<MT>& sm = *reinterpret_cast<Smem<MT>*>(scratch);
   AttnSmem<HD>& am = *reinterpret_cast<AttnSmem<HD>*>(scratch);
@@ -818,15 +853,11 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
       mbar_init(&empty[i], 1);
     }
     mbar_fence_init();
-    for (int i = 0; i < 4; i++) cm.plan[i] = make_plan(a.geo[i]);
+    for (int i = 0; i < 4; i++) cm.plan[i] = make_plan(a_in.geo[i]);
+    cm.args = a_in;
   }
-  for (int l = threadIdx.x; l < a.n_layer; l += blockDim.x) {
-    const StackLayer& L = a.layers[l];
-    cm.wptr[l][0] = L.wqkv;
-    cm.wptr[l][1] = L.wo;
-    cm.wptr[l][2] = L.w13;
-    cm.wptr[l][3] = L.w2;
-  }
+  for (int l = threadIdx.x; l < a_in.n_layer; l += blockDim.x) cm.lay[l] = a_in.layers[l];
+  for (int i = threadIdx.x; i < a_in.hd / 2; i += blockDim.x) cm.inv_freq[i] = a_in.inv_freq[i];
   __syncthreads();
   pdl_launch_dependents();
   pdl_wait();
@@ -858,7 +889,8 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
       const StackGeo& g = a.geo[pm];
       if (pf >= issued) {
         const int nrec = min(kIB, g.nb - pkc * kIB);
-        bulk_prefetch_l2(cm.wptr[pl][pm] + ((size_t)pvt * g.nb + (size_t)pkc * kIB) * kQ8Rec, (uint32_t)nrec * kQ8Rec);
+        bulk_prefetch_l2(layer_w(cm.lay[pl], pm) + ((size_t)pvt * g.nb + (size_t)pkc * kIB) * kQ8Rec,
+                         (uint32_t)nrec * kQ8Rec);
       }
       pn--;
       pf++;
@@ -885,7 +917,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
       for (int mi = 0; mi < 4; mi++) {
         const StackGeo& g = a.geo[mi];
         const Plan& p = cm.plan[mi];
-        const uint8_t* W = cm.wptr[l][mi];
+        const uint8_t* W = layer_w(cm.lay[l], mi);
         int kc = p.kc0, vt = p.vt0;
         for (int n = p.n; n > 0; n--) {
           if (round > 0) pwait(&empty[slot], (uint32_t)((round - 1) & 1));
@@ -922,7 +954,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
   unsigned long long target = 0;
   const Plan* P = cm.plan;
   for (int l = 0; l < a.n_layer; l++) {
-    const StackLayer& L = a.layers[l];
+    const StackLayer& L = cm.lay[l];
     // P1: wqkv (x += previous layer's w2 partials); the grid barrier is inside the prologue
     resid_prologue<MT>(sm, a, a.geo[0], P[0], xa, xb, a.part1, l > 0 ? &a.geo[3] : nullptr, nullptr, L.attn_norm,
                        a.ss, l > 0, target, tr ? tr + 1 + (l * 5 + 0) * 3 : nullptr);
@@ -930,10 +962,8 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
     gemv_consume<MT>(sm, ring, full, empty, nslot, ctr, a.geo[0], P[0], a.part0, a.err);
     stamp(l, 0, 2);
     target = grid_arrive(a);
-    // P2: attention
-    grid_wait(a, target);
-    stamp(l, 1, 0);
-    attention_unit<MT, HD, KT>(am, cm, a, L, l, a.part0, a.geo[0],
+    // P2: attention (the grid barrier is inside)
+    attention_unit<MT, HD, KT>(am, cm, a, L, l, a.part0, a.geo[0], target, tr ? tr + 1 + (l * 5 + 1) * 3 : nullptr,
                                tr ? a.trace + (size_t)gridDim.x * (a.n_layer * 15 + 3) +
                                         ((size_t)blockIdx.x * a.n_layer + l) * 4
                                   : nullptr);
