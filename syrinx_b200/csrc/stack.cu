@@ -65,7 +65,8 @@ constexpr int kInflight = 10;            // weight items a CTA's producer keeps 
 constexpr int kSpanHeads = 16;           // attention heads a CTA's wo k range may touch
 constexpr int kUB = 2;                   // prologue units (block, token) gathered per batch
 constexpr uint64_t kBarWaitNs = 2000000000ull;  // grid / mbarrier wait limit
-constexpr int kStackMaxLayers = 64;              // layers whose weight pointers the producer keeps
+constexpr int kStackMaxLayers = 64;
+constexpr int kKvSeg = 4;  // key-range segments (pages) prefetched per layer              // layers whose weight pointers the producer keeps
 
 __host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
 
@@ -174,6 +175,12 @@ struct Common {  // outside the union of the two
   float inv_freq[64];                 // RoPE inverse frequencies (head_dim / 2 <= 64)
   Plan plan[4];
   float den[kMaxTok];
+  // this CTA's attention key range as contiguous segments of a layer's K (and V) region:
+  // element offset and length per page, recorded by the first layer's attention unit so that
+  // later layers prefetch their keys and values into L2 a phase ahead
+  long long kvp_off[kKvSeg];
+  int kvp_len[kKvSeg];
+  int kvp_n;
 };
 
 template <int MT, int HD>
@@ -624,6 +631,18 @@ __device__ __noinline__ void attention_unit(AttnSmem<HD>& sm, Common& cm, const 
   const bool own_new = pos >= t0 && pos < t1;
   KT* kb = reinterpret_cast<KT*>(a.kv + (size_t)layer * a.kv_layer_elems * sizeof(KT));
   KT* vb = kb + a.kv_layer_elems / 2;
+  if (layer == 0 && threadIdx.x == kCT - 1) {  // the keys [t0, t1) before the new position, per page
+    int n = 0;
+    for (int t = t0; t < min(t1, pos) && n < kKvSeg;) {
+      const int pg = t / kPage, e = min(min(t1, pos), (pg + 1) * kPage);
+      const int page = __ldcg(a.page_table + (size_t)seq * a.pt_stride + pg);
+      cm.kvp_off[n] = ((long long)(page * a.Hkv + g) * kPage + (t % kPage)) * HD;
+      cm.kvp_len[n] = (e - t) * HD;
+      n++;
+      t = e;
+    }
+    cm.kvp_n = n;
+  }
 
   // K/V rows of chunk c (not the new position, which comes from shared memory)
   auto load_chunk = [&](int c, float (&kv)[KC][EPL], float (&vv)[KC][EPL]) {
@@ -855,6 +874,7 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
     mbar_fence_init();
     for (int i = 0; i < 4; i++) cm.plan[i] = make_plan(a_in.geo[i]);
     cm.args = a_in;
+    cm.kvp_n = 0;
   }
   for (int l = threadIdx.x; l < a_in.n_layer; l += blockDim.x) cm.lay[l] = a_in.layers[l];
   for (int i = threadIdx.x; i < a_in.hd / 2; i += blockDim.x) cm.inv_freq[i] = a_in.inv_freq[i];
@@ -955,7 +975,18 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
   const Plan* P = cm.plan;
   for (int l = 0; l < a.n_layer; l++) {
     const StackLayer& L = cm.lay[l];
-    // P1: wqkv (x += previous layer's w2 partials); the grid barrier is inside the prologue
+    // P1: wqkv (x += previous layer's w2 partials); the grid barrier is inside the prologue.
+    // This layer's keys and values for the attention unit go to L2 first (HBM latency under the
+    // weight stream is several microseconds; the attention phase starts one phase later).
+    if (l > 0 && threadIdx.x == 32) {
+      const size_t esz = a.kv_f32 ? 4 : 2;
+      const uint8_t* kb = a.kv + (size_t)l * a.kv_layer_elems * esz;
+      const uint8_t* vb = kb + a.kv_layer_elems / 2 * esz;
+      for (int i = 0; i < cm.kvp_n; i++) {
+        bulk_prefetch_l2(kb + cm.kvp_off[i] * esz, (uint32_t)(cm.kvp_len[i] * esz));
+        bulk_prefetch_l2(vb + cm.kvp_off[i] * esz, (uint32_t)(cm.kvp_len[i] * esz));
+      }
+    }
     resid_prologue<MT>(sm, a, a.geo[0], P[0], xa, xb, a.part1, l > 0 ? &a.geo[3] : nullptr, nullptr, L.attn_norm,
                        a.ss, l > 0, target, tr ? tr + 1 + (l * 5 + 0) * 3 : nullptr);
     stamp(l, 0, 1);
