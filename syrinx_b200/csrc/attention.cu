@@ -353,6 +353,196 @@ __global__ void __launch_bounds__(32) k_kv_append(const AttnArgs a) {
   append_kv<HD, KT>(a, m, seq, pos, g, buf, threadIdx.x);
 }
 
+
+// ---- prefill attention ------------------------------------------------------------------
+// Causal attention of a prompt chunk (M tokens of ONE sequence, consecutive positions) whose
+// K/V k_kv_append has already written. One CTA per (query tile of kPfTq tokens, kv head): its
+// GM x kPfTq query rows (QK-normed and rotated once, in shared memory) share every tile of
+// kPfKeys keys and values staged in shared memory, where the decode kernel re-reads the keys
+// once per token. Per key tile: scores R x kPfKeys (each thread one key for R/4 rows, f32
+// FMAs over the head dimension), an online softmax per row (one warp per row), then
+// O += P.V (each thread R/8 rows x 4 elements). f32 throughout, as the decode path.
+constexpr int kPfTq = 4;     // query tokens per CTA
+constexpr int kPfKeys = 64;  // keys per shared-memory tile (one KV page)
+
+template <int HD, int R>
+struct PfSmem {
+  float q[R][HD];
+  float k[kPfKeys][HD + 4];  // padded rows: a quarter-warp's 16-byte loads hit distinct banks
+  float v[kPfKeys][HD];
+  float p[R][kPfKeys];
+  float m[R], l[R], alpha[R];
+};
+
+template <int HD, typename KT, int GM>
+__global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
+  constexpr int R = GM * kPfTq;   // query rows: row = token * GM + head
+  constexpr int RQ = R / 4;       // rows per thread in the scores (4 row groups of 64 threads)
+  constexpr int RO = R / 8;       // rows per thread in P.V (8 warps)
+  constexpr int EPL = HD / 32;
+  extern __shared__ __align__(16) unsigned char pf_raw[];
+  PfSmem<HD, R>& sm = *reinterpret_cast<PfSmem<HD, R>*>(pf_raw);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tile = blockIdx.x, g = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.H / a.Hkv;
+  const int m0 = tile * kPfTq;
+  const int n_tok = min(kPfTq, a.M - m0);
+  const int seq = ld_cg(a.tok_seq + m0);
+  int qpos[kPfTq];
+  int last = 0;  // the tile's last query position: keys beyond it are never read
+#pragma unroll
+  for (int j = 0; j < kPfTq; j++) {
+    qpos[j] = j < n_tok ? ld_cg(a.tok_pos + m0 + j) : -1;
+    last = max(last, qpos[j]);
+  }
+
+  // query rows: load, QK-norm, RoPE (one warp per row)
+  for (int r = warp; r < R; r += 8) {
+    const int j = r / GM, i = r % GM;
+    if (j < n_tok && i < G) {
+      const float* src = a.qkv + (size_t)(m0 + j) * (a.H + 2 * a.Hkv) * HD + (size_t)(g * G + i) * HD;
+      for (int e = lane; e < HD; e += 32) sm.q[r][e] = ld_cg(src + e);
+      __syncwarp();
+      norm_rope_head<HD>(sm.q[r], a.qn, a.eps, a.inv_freq, a.interleaved, qpos[j], lane);
+    } else {
+      for (int e = lane; e < HD; e += 32) sm.q[r][e] = 0.f;
+    }
+    if (lane == 0) {
+      sm.m[r] = -INFINITY;
+      sm.l[r] = 0.f;
+    }
+  }
+  float acc[RO][4];
+#pragma unroll
+  for (int i = 0; i < RO; i++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[i][e] = 0.f;
+  const KT* kb = static_cast<const KT*>(a.kbase);
+  const KT* vb = static_cast<const KT*>(a.vbase);
+  const int key = threadIdx.x & (kPfKeys - 1), rg = threadIdx.x / kPfKeys;  // scores: key, row group
+  const int d0 = (threadIdx.x & 31) * 4;  // P.V: 4 elements (HD = 128; at HD = 64 half the lanes idle)
+
+  for (int k0 = 0; k0 <= last; k0 += kPfKeys) {
+    __syncthreads();  // the previous tile's readers are done
+    {  // stage the tile's keys and values (one page) as f32
+      const int page = ld_cg(a.page_table + (size_t)seq * a.pt_stride + k0 / kPage);
+      const size_t base = ((size_t)(page * a.Hkv + g) * kPage) * HD;
+      for (int kk = warp; kk < kPfKeys; kk += 8) {
+        float kv[EPL], vv[EPL];
+        if (k0 + kk <= last) {
+          kv_load_row<EPL>(kb + base + (size_t)kk * HD + lane * EPL, kv);
+          kv_load_row<EPL>(vb + base + (size_t)kk * HD + lane * EPL, vv);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; e++) kv[e] = vv[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+          sm.k[kk][lane * EPL + e] = kv[e];
+          sm.v[kk][lane * EPL + e] = vv[e];
+        }
+      }
+    }
+    __syncthreads();
+    {  // scores of this thread's key for rows rg * RQ .. + RQ
+      float sc[RQ];
+#pragma unroll
+      for (int i = 0; i < RQ; i++) sc[i] = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < HD; d += 4) {
+        const float4 kq = *reinterpret_cast<const float4*>(&sm.k[key][d]);
+#pragma unroll
+        for (int i = 0; i < RQ; i++) {
+          const float4 qq = *reinterpret_cast<const float4*>(&sm.q[rg * RQ + i][d]);
+          sc[i] = fmaf(qq.x, kq.x, sc[i]);
+          sc[i] = fmaf(qq.y, kq.y, sc[i]);
+          sc[i] = fmaf(qq.z, kq.z, sc[i]);
+          sc[i] = fmaf(qq.w, kq.w, sc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < RQ; i++) {
+        const int r = rg * RQ + i, j = r / GM;
+        const bool ok = j < n_tok && k0 + key <= qpos[j];
+        sm.p[r][key] = ok ? __fmul_rn(sc[i], a.scale) : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // online softmax per row: one warp per row, two keys per lane
+    for (int r = warp; r < R; r += 8) {
+      const float s0 = sm.p[r][lane], s1 = sm.p[r][lane + 32];
+      const float mx = warp_max(fmaxf(s0, s1));
+      const float m_old = sm.m[r];
+      const float m_new = fmaxf(m_old, mx);
+      const float e0 = m_new == -INFINITY ? 0.f : expf(s0 - m_new);
+      const float e1 = m_new == -INFINITY ? 0.f : expf(s1 - m_new);
+      sm.p[r][lane] = e0;
+      sm.p[r][lane + 32] = e1;
+      const float sum = warp_sum(e0 + e1);
+      if (lane == 0) {
+        const float al = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+        sm.alpha[r] = al;
+        sm.l[r] = __fadd_rn(__fmul_rn(sm.l[r], al), sum);
+        sm.m[r] = m_new;
+      }
+    }
+    __syncthreads();
+    if (d0 < HD) {  // O = O * alpha + P.V for rows warp * RO .. + RO, elements d0 .. d0 + 3
+#pragma unroll
+      for (int i = 0; i < RO; i++) {
+        const float al = sm.alpha[warp * RO + i];
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[i][e] *= al;
+      }
+#pragma unroll 4
+      for (int kk = 0; kk < kPfKeys; kk++) {
+        const float4 vq = *reinterpret_cast<const float4*>(&sm.v[kk][d0]);
+#pragma unroll
+        for (int i = 0; i < RO; i++) {
+          const float pr = sm.p[warp * RO + i][kk];
+          acc[i][0] = fmaf(pr, vq.x, acc[i][0]);
+          acc[i][1] = fmaf(pr, vq.y, acc[i][1]);
+          acc[i][2] = fmaf(pr, vq.z, acc[i][2]);
+          acc[i][3] = fmaf(pr, vq.w, acc[i][3]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (d0 < HD) {
+#pragma unroll
+    for (int i = 0; i < RO; i++) {
+      const int r = warp * RO + i, j = r / GM, h = r % GM;
+      if (j < n_tok && h < G) {
+        float* out = a.out + (size_t)(m0 + j) * a.H * HD + (size_t)(g * G + h) * HD + d0;
+        const float L = sm.l[r];
+#pragma unroll
+        for (int e = 0; e < 4; e++) out[e] = __fdiv_rn(acc[i][e], L);
+      }
+    }
+  }
+}
+
+template <int HD, typename KT, int GM>
+cudaError_t launch_pf_t(const AttnArgs& a, cudaStream_t st) {
+  auto kern = k_attn_prefill<HD, KT, GM>;
+  const size_t smem = sizeof(PfSmem<HD, GM * kPfTq>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_cfg(dim3((a.M + kPfTq - 1) / kPfTq, a.Hkv), dim3(256), smem, st, attr);
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+template <int HD, typename KT>
+cudaError_t launch_pf_hd(const AttnArgs& a, cudaStream_t st) {
+  const int G = a.H / a.Hkv;
+  if (G <= 2) return launch_pf_t<HD, KT, 2>(a, st);
+  if (G <= 4) return launch_pf_t<HD, KT, 4>(a, st);
+  return launch_pf_t<HD, KT, 8>(a, st);
+}
+
 template <int HD, typename KT>
 cudaError_t launch_attention_hd(const AttnArgs& a, cudaLaunchConfig_t& cfg) {
   const int G = a.H / a.Hkv;
@@ -381,6 +571,18 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     case 64: return a.kv_f32 ? launch_attention_hd<64, float>(a, cfg) : launch_attention_hd<64, __nv_bfloat16>(a, cfg);
     case 128:
       return a.kv_f32 ? launch_attention_hd<128, float>(a, cfg) : launch_attention_hd<128, __nv_bfloat16>(a, cfg);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Prefill chunks (append = 0) of one sequence: the tiled kernel above. Its K/V must already be
+// in the cache (launch_kv_append).
+cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t st) {
+  if (a.H % a.Hkv || a.H / a.Hkv > kMaxGroup || a.append || !a.tok_seq || !a.tok_pos || a.M < 1)
+    return cudaErrorInvalidValue;
+  switch (a.hd) {
+    case 64: return a.kv_f32 ? launch_pf_hd<64, float>(a, st) : launch_pf_hd<64, __nv_bfloat16>(a, st);
+    case 128: return a.kv_f32 ? launch_pf_hd<128, float>(a, st) : launch_pf_hd<128, __nv_bfloat16>(a, st);
   }
   return cudaErrorInvalidValue;
 }

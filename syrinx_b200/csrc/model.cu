@@ -886,8 +886,12 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     a.n_split = fast ? 1 : n_split_for(s, M, td.n_local_heads);
     a.append = append ? 1 : 0;
     a.M = M;
-    if (!append) SX_CU(launch_kv_append(a, s->st));
-    SX_CU(launch_attention(a, s->st));
+    if (append) {
+      SX_CU(launch_attention(a, s->st));
+    } else {  // a prompt chunk of one sequence: its K/V first, then the tiled prefill kernel
+      SX_CU(launch_kv_append(a, s->st));
+      SX_CU(launch_attention_prefill(a, s->st));
+    }
 
     GemvArgs o;
     o.w = L.wo;

@@ -165,6 +165,7 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, int Mt, int K, int nb, int nc, int
                            cudaStream_t st);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_kv_append(const AttnArgs& a, cudaStream_t st);
+cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t st);
 
 // ---- persistent decode stack (stack.cu) ------------------------------------------------
 // One layer's Q8_0 tile records and vectors, as the persistent kernel reads them (device array).
