@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
   const KT* kb = static_cast<const KT*>(a.kbase);
   const KT* vb = static_cast<const KT*>(a.vbase);
   const int key = threadIdx.x & (kPfKeys - 1), rg = threadIdx.x / kPfKeys;  // scores: key, row group
-  const int d0 = (threadIdx.x & 31) * 4;  // P.V: 4 elements (HD = 128; at HD = 64 half the lanes idle)
+  const int d0 = (threadIdx.x & 31) * 4;  // P.V: 4 elements (HD = 128; at HD = 64 / 32 lanes past HD idle)
 
   for (int k0 = 0; k0 <= last; k0 += kPfKeys) {
     __syncthreads();  // the previous tile's readers are done
@@ -581,6 +581,7 @@ cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t st) {
   if (a.H % a.Hkv || a.H / a.Hkv > kMaxGroup || a.append || !a.tok_seq || !a.tok_pos || a.M < 1)
     return cudaErrorInvalidValue;
   switch (a.hd) {
+    case 32: return a.kv_f32 ? launch_pf_hd<32, float>(a, st) : launch_pf_hd<32, __nv_bfloat16>(a, st);
     case 64: return a.kv_f32 ? launch_pf_hd<64, float>(a, st) : launch_pf_hd<64, __nv_bfloat16>(a, st);
     case 128: return a.kv_f32 ? launch_pf_hd<128, float>(a, st) : launch_pf_hd<128, __nv_bfloat16>(a, st);
   }
