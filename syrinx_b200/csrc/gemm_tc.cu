@@ -1,4 +1,4 @@
-// gemm_tc.cu — Q8_0 prefill GEMM on the 5th-generation tensor cores (tcgen05, kind::i8).
+// gemm_tc.cu — Q8_0 prefill GEMM on the 5th-generation tensor cores (tcgen05, kind::f16).
 //
 // Replaces the prompt forward's quantized linears (`SlowAr::prefill`,
 // crates/syrinx-fish/src/s2/slow_ar.rs:250-255, M = prompt chunk; `prefill_batch`
@@ -7,25 +7,32 @@
 //
 // It computes exactly what k_gemv_q8<Mt> (gemv_q8.cu) computes and writes the same partial
 // buffer [tile][k chunk][token][16], so the same merge kernels apply the epilogues and a
-// prefill gives bit-identical results either way. The difference is where the products
-// happen: a CTA takes a 128-row group of the weight (8 tile records per 32-wide k block) and
-// all the chunk's tokens, and one tcgen05.mma (M = 128, N = 4 limbs x Mt tokens, K = 32)
-// per k block yields the exact int32 block sums of every row against every limb of every
-// token into tensor memory. The epilogue warps read them back (tcgen05.ld), fold the limbs
-// and scale per block in f32 in the GEMV's order, while the tensor core already runs the next
-// block's product into the other half of tensor memory.
+// prefill gives bit-identical results either way. A CTA takes a 128-row group of the weight
+// (8 tile records per 32-wide k block) and all the chunk's tokens. The operands are small
+// integers: the Q8_0 quants (-128..127) and the four limbs of each token's activations
+// (|limb| <= 128). Both are exact in f16, every product is exact, and every partial sum of a
+// 32-wide block stays below 2^24, so two tcgen05.mma kind::f16 (M = 128, N = 4 limbs x Mt
+// tokens, K = 16) give the exact integer block sums of every row against every limb of every
+// token in f32 in tensor memory, whatever order the tensor core adds them in. The epilogue
+// then needs no integer-to-float conversion (the XU pipe, which bounded the kind::i8 form):
+// per (row, token) one packed fma.rn.f32x2 folds the limb pairs (l0 * 128 + l1 and
+// l2 * 128 + l3, each rounded once, exactly as the GEMV's (float)(int) does) and a second one
+// scales and accumulates them, in the GEMV's order.
 //
 // Data flow:
-//   - k_tc_limbs (one CTA per token) computes the RMSNorm denominator and splits x into int8
-//     limbs, written once per launch as every k block's B operand in the canonical no-swizzle
-//     K-major layout (8-row x 16-byte core matrices; row n = 4 * token + limb);
+//   - k_tc_limbs (one CTA per token) stages the token's row in shared memory (one round trip),
+//     computes the RMSNorm denominator as k_gemv_q8 does (256 threads, k strided by 256, warp
+//     sums added in warp order) and splits the normed values of each 32-wide block into int8
+//     limbs, written once per launch as every block's B operand in the canonical no-swizzle
+//     K-major layout (8-row x 16-byte core matrices), rows n = 4 * token + {l0, l2, l1, l3};
 //   - k_gemm_tc (one CTA per SM, a contiguous range of (k chunk, 128-row group) items, k-chunk
 //     major so consecutive items share their B operands): one lane bulk-copies an item's 8 tile
-//     records (8 x 4352 contiguous bytes) and, when the chunk changes, the chunk's B operands
-//     into double-buffered shared memory (cp.async.bulk, mbarrier completion), an item ahead;
-//   - per k block all warps repack the 8 records' quants into the canonical A layout and their
-//     row scales, fence the async proxy, one thread issues the MMA and commits it to an
-//     mbarrier, and all warps read back the previous block's sums and accumulate.
+//     records (8 x 4352 contiguous bytes) an item ahead and the chunk's B operands when the
+//     chunk changes (cp.async.bulk, mbarrier completion);
+//   - per k block all warps widen the 8 records' quants and the block's limbs to f16 in the
+//     canonical layout (byte-permute into 0x64xx and one packed f16 subtract: exact), fence
+//     the async proxy, one thread issues the two MMAs and commits them to an mbarrier, and all
+//     warps read back the previous block's sums (tcgen05.ld) and accumulate.
 // Every wait is bounded by %globaltimer and raises the session's error flag; tensor memory is
 // freed on every path.
 #include <cuda_runtime.h>
@@ -45,7 +52,6 @@ constexpr int kRows = 128;         // weight rows per CTA tile (8 Q8_0 tiles)
 constexpr int kTiles = kRows / kQ8Tile;
 constexpr int kChunkB = 8;         // blocks per k chunk
 constexpr int kStageBytes = kTiles * kChunkB * kQ8Rec;  // 34816
-constexpr int kStages = 3;
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 __device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -62,7 +68,8 @@ __device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t parity, int* err
 }
 
 // UMMA shared-memory descriptor: canonical K-major layout without swizzle, 8-row x 16-byte
-// core matrices, LBO = distance between the two 16-byte K halves, SBO = between 8-row groups.
+// core matrices, LBO = distance between core matrices adjacent along K, SBO = between 8-row
+// groups.
 __device__ __forceinline__ uint64_t umma_desc(const void* p, uint32_t lbo, uint32_t sbo) {
   const uint32_t a = smem_addr(p);
   uint64_t d = 0;
@@ -72,16 +79,16 @@ __device__ __forceinline__ uint64_t umma_desc(const void* p, uint32_t lbo, uint3
   d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
   return d;                // base offset 0, swizzle none
 }
-// instruction descriptor of kind::i8: s32 accumulator, signed 8-bit A and B, both K-major
-__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// instruction descriptor of kind::f16: f32 accumulator, f16 A and B, both K-major
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc) {
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, 0, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc)
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -105,22 +112,43 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Four signed int8 (one word) -> four exact f16 (two words): bias to 128 + b, place each byte
+// under the f16 exponent of 1024 (0x64xx = 1024 + byte), subtract 1152 in packed f16.
+__device__ __forceinline__ uint2 s8x4_to_f16x4(uint32_t w) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140);
+  const uint32_t hi = __byte_perm(u, 0x64646464u, 0x7362);
+  const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
+  __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo), off);
+  __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi), off);
+  return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
 struct TcGeo {
   int K, nb, nc, n_vt, n_rg;  // columns, blocks, k chunks, tiles, 128-row groups
 };
 
-// element (row n, k) of a canonical K-major operand of 32 bytes of K per row
+// byte offset of element (row n, k) of a canonical K-major operand of 32 int8 per row
 __host__ __device__ __forceinline__ int canon_off(int n, int k) {
   return (n >> 3) * 256 + (k >> 4) * 128 + (n & 7) * 16 + (k & 15);
 }
+// byte offset of element (row n, k) of a canonical K-major operand of 32 f16 per row
+__host__ __device__ __forceinline__ int canon16_off(int n, int k) {
+  return (n >> 3) * 512 + (k >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2;
+}
+// B row of limb l of token t: limbs ordered l0, l2, l1, l3 so that a token's sums read back as
+// the f32 pairs (l0, l2) and (l1, l3)
+__host__ __device__ __forceinline__ int limb_row(int t, int l) { return 4 * t + ((l & 1) << 1) + (l >> 1); }
 
 // ---- the B operand: int8 limbs of x for every k block, in the canonical layout ----------
-// One CTA per token: the RMSNorm denominator exactly as k_gemv_q8 computes it (256 threads,
-// k strided by 256, warp sums added in warp order), then per 32-wide block the limb split of
-// the normed values (exact to 2^-27 of the block max) as rows 4t..4t+3 of that block's
-// operand, and the block's power-of-two scale.
+// One CTA per token: the row into shared memory (every load in flight at once), the RMSNorm
+// denominator exactly as k_gemv_q8 computes it (256 threads, k strided by 256, warp sums added
+// in warp order), then per 32-wide block the limb split of the normed values (exact to 2^-27
+// of the block max) as rows limb_row(t, 0..3) of that block's operand, and the block's
+// power-of-two scale.
 template <int MT>
 __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo g, uint8_t* Bg, float* sxg) {
+  extern __shared__ float xrow[];  // [K]
   __shared__ float red[kTW];
   __shared__ float den_s;
   __shared__ __align__(16) int8_t scr[kTW][4][32];
@@ -129,12 +157,14 @@ __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo 
   pdl_launch_dependents();
   pdl_wait();
   const bool live = t < a.M;
+  if (live) {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)t * g.K);
+    for (int i = threadIdx.x; i < g.K / 4; i += kTT) reinterpret_cast<float4*>(xrow)[i] = __ldcg(src + i);
+  }
+  __syncthreads();
   if (a.norm_w && live) {
     float ss = 0.f;
-    for (int k = threadIdx.x; k < g.K; k += kTT) {
-      const float v = ld_cg(a.x + (size_t)t * g.K + k);
-      ss = fmaf(v, v, ss);
-    }
+    for (int k = threadIdx.x; k < g.K; k += kTT) ss = fmaf(xrow[k], xrow[k], ss);
     const float w = warp_sum(ss);
     if (lane == 0) red[warp] = w;
     __syncthreads();
@@ -149,7 +179,7 @@ __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo 
     const int k = b * 32 + lane;
     float v = 0.f;
     if (live) {
-      v = ld_cg(a.x + (size_t)t * g.K + k);
+      v = xrow[k];
       if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den_s), a.norm_w[k]);
     }
     const float mx = warp_max(fabsf(v));
@@ -176,7 +206,7 @@ __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo 
     __syncwarp();
     const int limb = lane >> 3, kk = 4 * (lane & 7);
     const uint32_t word = *reinterpret_cast<const uint32_t*>(&scr[warp][limb][kk]);
-    *reinterpret_cast<uint32_t*>(Bg + (size_t)b * N * 32 + canon_off(4 * t + limb, kk)) = word;
+    *reinterpret_cast<uint32_t*>(Bg + (size_t)b * N * 32 + canon_off(limb_row(t, limb), kk)) = word;
     if (lane == 0) sxg[(size_t)b * MT + t] = sx;
     __syncwarp();
   }
@@ -186,11 +216,12 @@ template <int MT>
 struct TcSmem {
   static constexpr int N = 4 * MT;
   uint8_t stA[2][kStageBytes];              // an item's 8 tile records x 8 blocks
-  uint8_t stB[2][kChunkB * N * 32];         // a k chunk's B operands, canonical
-  float stS[2][kChunkB * MT];               // and its blocks' x scales
-  uint8_t A[2][kRows * 32];                 // one block's A operand, canonical
-  float dsb[2][kRows];                      // its row scales
-  uint64_t bar_a[2], bar_b[2], bar_mma[2];
+  uint8_t stB[kChunkB * N * 32];            // the k chunk's B operands (int8, canonical)
+  float stS[kChunkB * MT];                  // and its blocks' x scales
+  uint8_t A[2][kRows * 64];                 // one block's A operand, f16 canonical
+  uint8_t B[2][N * 64];                     // one block's B operand, f16 canonical
+  float dsb[2][kRows];                      // the block's row scales
+  uint64_t bar_a[2], bar_b, bar_mma[2];
   uint32_t tmem_base;
 };
 
@@ -209,9 +240,9 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; i++) {
       mbar_init(&sm.bar_a[i], 1);
-      mbar_init(&sm.bar_b[i], 1);
       mbar_init(&sm.bar_mma[i], 1);
     }
+    mbar_init(&sm.bar_b, 1);
     mbar_fence_init();
   }
   if (warp == 0) {  // two accumulators of up to 256 columns
@@ -234,29 +265,32 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
       bulk_g2s(sm.stA[st] + t * kChunkB * kQ8Rec, W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB) * kQ8Rec,
                (uint32_t)(nrec * kQ8Rec), &sm.bar_a[st]);
   };
-  // a k chunk's B operands and scales (written by k_tc_limbs)
-  auto issue_b = [&](int kc, int st) {
+  // a k chunk's B operands and scales (written by k_tc_limbs); the buffer is free: every
+  // block of the previous chunk has been widened (a __syncthreads separates them)
+  auto issue_b = [&](int kc) {
     const int nrec = nrec_of(kc);
-    mbar_arrive_expect_tx(&sm.bar_b[st], (uint32_t)(nrec * N * 32 + nrec * MT * 4));
-    bulk_g2s(sm.stB[st], Bg + (size_t)kc * kChunkB * N * 32, (uint32_t)(nrec * N * 32), &sm.bar_b[st]);
-    bulk_g2s(sm.stS[st], sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.bar_b[st]);
+    mbar_arrive_expect_tx(&sm.bar_b, (uint32_t)(nrec * N * 32 + nrec * MT * 4));
+    bulk_g2s(sm.stB, Bg + (size_t)kc * kChunkB * N * 32, (uint32_t)(nrec * N * 32), &sm.bar_b);
+    bulk_g2s(sm.stS, sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.bar_b);
   };
   if (threadIdx.x == 0 && c1 > c0) issue_a(c0, 0);
   pdl_launch_dependents();
   pdl_wait();  // the B operands come from the limb kernel
-  if (threadIdx.x == 0 && c1 > c0) issue_b(c0 / g.n_rg, 0);
+  if (threadIdx.x == 0 && c1 > c0) issue_b(c0 / g.n_rg);
 
   // epilogue roles: TMEM lane quarter q (rows 32q..32q+31), token half h
   const int q = warp & 3, h = warp >> 2;
   const int row = q * 32 + lane;
   constexpr int TPT = MT / 2;  // tokens per thread
-  float acc01[TPT], acc23[TPT];
+  unsigned long long acc[TPT];  // per token the packed pair {limbs 0/1, limbs 2/3}
 #pragma unroll
-  for (int i = 0; i < TPT; i++) acc01[i] = acc23[i] = 0.f;
+  for (int i = 0; i < TPT; i++) acc[i] = 0ull;
+  const unsigned long long k128 = pack2(128.f, 128.f);
 
-  int blk = 0;  // blocks processed by this CTA (selects the A buffer and the TMEM half)
-  int p_sb = 0, p_j = 0, p_rg = 0, p_kc = 0, p_nrec = 0;
+  int blk = 0;  // blocks processed by this CTA (selects the operand buffer and the TMEM half)
+  int p_j = 0, p_rg = 0, p_kc = 0, p_nrec = 0;
   bool have_prev = false;
+  float sx_prev[TPT];  // the previous block's x scales of this thread's tokens
 
   // read back block (blk - 1)'s sums and accumulate; after its item's last block, the partials
   auto epilogue = [&]() {
@@ -264,29 +298,18 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
     tc_wait(&sm.bar_mma[buf], (uint32_t)(((blk - 1) >> 1) & 1), a.err);
     tc_fence_after();
     const float ds = sm.dsb[buf][row];
-    const float* sxs = sm.stS[p_sb] + p_j * MT + h * TPT;
 #pragma unroll
-    for (int part = 0; part < TPT / 8; part += 2) {
-      uint32_t r0[32], r1[32];
-      const uint32_t col = (uint32_t)(buf * 256 + (h * TPT + part * 8) * 4);
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col, r0);
-      if (part + 1 < TPT / 8) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col + 32, r1);
+    for (int part = 0; part < TPT / 8; part++) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + (h * TPT + part * 8) * 4), r);
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         const int tl = part * 8 + i;
-        const float dsx = __fmul_rn(ds, sxs[tl]);
-        acc01[tl] = fmaf(dsx, (float)((int)r0[4 * i] * 128 + (int)r0[4 * i + 1]), acc01[tl]);
-        acc23[tl] = fmaf(dsx, (float)((int)r0[4 * i + 2] * 128 + (int)r0[4 * i + 3]), acc23[tl]);
-      }
-      if (part + 1 < TPT / 8) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const int tl = (part + 1) * 8 + i;
-          const float dsx = __fmul_rn(ds, sxs[tl]);
-          acc01[tl] = fmaf(dsx, (float)((int)r1[4 * i] * 128 + (int)r1[4 * i + 1]), acc01[tl]);
-          acc23[tl] = fmaf(dsx, (float)((int)r1[4 * i + 2] * 128 + (int)r1[4 * i + 3]), acc23[tl]);
-        }
+        const float dsx = __fmul_rn(ds, sx_prev[tl]);
+        // (S_l0, S_l2) * 128 + (S_l1, S_l3): each sum rounded once, as (float)(int) does
+        const unsigned long long t = fma2(pack2u(r[4 * i], r[4 * i + 1]), k128, pack2u(r[4 * i + 2], r[4 * i + 3]));
+        acc[tl] = fma2(pack2(dsx, dsx), t, acc[tl]);
       }
     }
     if (p_j == p_nrec - 1) {
@@ -296,34 +319,39 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
 #pragma unroll
         for (int tl = 0; tl < TPT; tl++) {
           const int t = h * TPT + tl;
-          if (t < a.M) __stcg(P + t * 16, acc01[tl] * 0x1p-7f + acc23[tl] * 0x1p-21f);
+          float a01, a23;
+          unpack2(acc[tl], a01, a23);
+          if (t < a.M) __stcg(P + t * 16, a01 * 0x1p-7f + a23 * 0x1p-21f);
         }
       }
 #pragma unroll
-      for (int tl = 0; tl < TPT; tl++) acc01[tl] = acc23[tl] = 0.f;
+      for (int tl = 0; tl < TPT; tl++) acc[tl] = 0ull;
     }
   };
 
-  int n_items = 0, kc_idx = 0;
+  int n_items = 0, kc_cur = -1;
   for (int it = c0; it < c1; it++, n_items++) {
     const int sa = n_items & 1;
     const int kc = it / g.n_rg, rg = it % g.n_rg;
-    if (it > c0 && kc != (it - 1) / g.n_rg) kc_idx++;
-    const int sb = kc_idx & 1;
     const int nrec = nrec_of(kc);
-    // prefetch the next item's records (stage sa ^ 1: its last repack finished in the previous
-    // item) and, at a k chunk change, the next chunk's B operand (stage sb ^ 1: unread since
-    // two chunks ago, every MMA reading it has completed)
-    if (threadIdx.x == 0 && it + 1 < c1) {
-      issue_a(it + 1, sa ^ 1);
-      if ((it + 1) / g.n_rg != kc) issue_b((it + 1) / g.n_rg, sb ^ 1);
+    // the next item's records go out an item ahead (stage sa ^ 1: its last widening finished
+    // in the previous item)
+    if (threadIdx.x == 0 && it + 1 < c1) issue_a(it + 1, sa ^ 1);
+    if (kc != kc_cur) {  // a new k chunk: its B operands (the first one was issued above)
+      if (kc_cur >= 0) {
+        __syncthreads();  // every widening of the previous chunk's operands is done
+        if (threadIdx.x == 0) issue_b(kc);
+      }
+      tc_wait(&sm.bar_b, (uint32_t)((kc - c0 / g.n_rg) & 1), a.err);
+      kc_cur = kc;
     }
     tc_wait(&sm.bar_a[sa], (uint32_t)((n_items >> 1) & 1), a.err);
-    tc_wait(&sm.bar_b[sb], (uint32_t)((kc_idx >> 1) & 1), a.err);
     for (int j = 0; j < nrec; j++, blk++) {
       const int buf = blk & 1;
-      {  // A: the 8 records' quants into the canonical layout, and the row scales
-        const int t = warp, L = lane;  // tile t, fragment lane L = 4g + c
+      // the operand buffers `buf` were last read by block blk - 2's MMAs, whose completion the
+      // epilogue of block blk - 2 (in the previous iteration) waited for
+      {  // A: warp t widens tile t's record (lane L = 4g + c holds rows g, g + 8)
+        const int t = warp, L = lane;
         const int gg = L >> 2, cc = L & 3;
         const bool tile_ok = rg * kTiles + t < g.n_vt;
         const uint8_t* rec = sm.stA[sa] + (t * kChunkB + j) * kQ8Rec;
@@ -331,29 +359,43 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
         if (tile_ok) v = lds128(rec + L * 16);
         uint8_t* A = sm.A[buf];
         const int m0 = t * 16 + gg, m1 = m0 + 8;
-        *reinterpret_cast<uint32_t*>(A + canon_off(m0, 4 * cc)) = v.x;
-        *reinterpret_cast<uint32_t*>(A + canon_off(m1, 4 * cc)) = v.y;
-        *reinterpret_cast<uint32_t*>(A + canon_off(m0, 16 + 4 * cc)) = v.z;
-        *reinterpret_cast<uint32_t*>(A + canon_off(m1, 16 + 4 * cc)) = v.w;
+        *reinterpret_cast<uint2*>(A + canon16_off(m0, 4 * cc)) = s8x4_to_f16x4(v.x);
+        *reinterpret_cast<uint2*>(A + canon16_off(m1, 4 * cc)) = s8x4_to_f16x4(v.y);
+        *reinterpret_cast<uint2*>(A + canon16_off(m0, 16 + 4 * cc)) = s8x4_to_f16x4(v.z);
+        *reinterpret_cast<uint2*>(A + canon16_off(m1, 16 + 4 * cc)) = s8x4_to_f16x4(v.w);
         if (L < 16)
           sm.dsb[buf][t * 16 + L] =
               tile_ok ? __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(L))) : 0.f;
       }
-      fence_async_smem();  // the A operand written by threads becomes visible to the tensor core
+      // B: 16-byte pieces (row n, k 16 p .. 16 p + 15) widened to 32 bytes
+      for (int i = threadIdx.x; i < N * 2; i += kTT) {
+        const int n = i >> 1, pk = (i & 1) * 16;
+        const uint4 v = lds128(sm.stB + (size_t)j * N * 32 + canon_off(n, pk));
+        uint8_t* B = sm.B[buf];
+        const uint2 w0 = s8x4_to_f16x4(v.x), w1 = s8x4_to_f16x4(v.y), w2 = s8x4_to_f16x4(v.z),
+                    w3 = s8x4_to_f16x4(v.w);
+        *reinterpret_cast<uint4*>(B + canon16_off(n, pk)) = make_uint4(w0.x, w0.y, w1.x, w1.y);
+        *reinterpret_cast<uint4*>(B + canon16_off(n, pk + 8)) = make_uint4(w2.x, w2.y, w3.x, w3.y);
+      }
+      fence_async_smem();  // the operands written by threads become visible to the tensor core
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
       if (threadIdx.x == 0) {
-        tc_mma(tmem + (uint32_t)(buf * 256), umma_desc(sm.A[buf], 128, 256),
-               umma_desc(sm.stB[sb] + j * N * 32, 128, 256), idesc_i8(kRows, N));
+        const uint32_t d = tmem + (uint32_t)(buf * 256);
+        tc_mma(d, umma_desc(sm.A[buf], 128, 512), umma_desc(sm.B[buf], 128, 512), idesc_f16(kRows, N), 0u);
+        tc_mma(d, umma_desc(sm.A[buf] + 256, 128, 512), umma_desc(sm.B[buf] + 256, 128, 512), idesc_f16(kRows, N), 1u);
         tc_commit(&sm.bar_mma[buf]);
       }
       if (have_prev) epilogue();
+      // this block's x scales for the next epilogue (stS is stable until the chunk changes,
+      // which a __syncthreads precedes)
+#pragma unroll
+      for (int tl = 0; tl < TPT; tl++) sx_prev[tl] = sm.stS[j * MT + h * TPT + tl];
       // the next MMA into the other TMEM half must not start before this read-back is done
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
-      p_sb = sb;
       p_j = j;
       p_rg = rg;
       p_kc = kc;
@@ -372,9 +414,15 @@ cudaError_t launch_tc_t(const GemvArgs& a, const TcGeo& g, int sms, uint8_t* scr
   constexpr int N = 4 * MT;
   uint8_t* Bg = scratch;
   float* sxg = reinterpret_cast<float*>(scratch + (size_t)g.nb * N * 32);
+  const size_t row_bytes = (size_t)g.K * 4;
+  cudaError_t e = cudaSuccess;
+  if (row_bytes > 48 * 1024) {
+    e = cudaFuncSetAttribute(k_tc_limbs<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_bytes);
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchAttribute attr0[1];
-  cudaLaunchConfig_t cfg0 = launch_cfg(dim3(MT), dim3(kTT), 0, st, attr0);
-  cudaError_t e = cudaLaunchKernelEx(&cfg0, k_tc_limbs<MT>, a, g, Bg, sxg);
+  cudaLaunchConfig_t cfg0 = launch_cfg(dim3(MT), dim3(kTT), row_bytes, st, attr0);
+  e = cudaLaunchKernelEx(&cfg0, k_tc_limbs<MT>, a, g, Bg, sxg);
   if (e != cudaSuccess) return e;
   auto kern = k_gemm_tc<MT>;
   const size_t smem = sizeof(TcSmem<MT>) + 1024;
