@@ -23,16 +23,16 @@
 //   - k_tc_limbs (one CTA per token) stages the token's row in shared memory (one round trip),
 //     computes the RMSNorm denominator as k_gemv_q8 does (256 threads, k strided by 256, warp
 //     sums added in warp order) and splits the normed values of each 32-wide block into int8
-//     limbs, written once per launch as every block's B operand in the canonical no-swizzle
-//     K-major layout (8-row x 16-byte core matrices), rows n = 4 * token + {l0, l2, l1, l3};
+//     limbs, written once per launch as every block's f16 B operand in the canonical
+//     no-swizzle K-major layout (8-row x 16-byte core matrices), rows n = 4 * token +
+//     {l0, l2, l1, l3};
 //   - k_gemm_tc (one CTA per SM, a contiguous range of (k chunk, 128-row group) items, k-chunk
-//     major so consecutive items share their B operands): one lane bulk-copies an item's 8 tile
-//     records (8 x 4352 contiguous bytes) an item ahead and the chunk's B operands when the
-//     chunk changes (cp.async.bulk, mbarrier completion);
-//   - per k block all warps widen the 8 records' quants and the block's limbs to f16 in the
-//     canonical layout (byte-permute into 0x64xx and one packed f16 subtract: exact), fence
-//     the async proxy, one thread issues the two MMAs and commits them to an mbarrier, and all
-//     warps read back the previous block's sums (tcgen05.ld) and accumulate.
+//     major so consecutive items share their B operands) runs four warp roles joined by
+//     mbarriers: a copy lane bulk-copies each item's 8 tile records (8 x 4352 contiguous bytes,
+//     two stages) and each chunk's B operands (cp.async.bulk); two warps widen every block's
+//     quants to f16 in the canonical layout (byte-permute into 0x64xx and one packed f16
+//     subtract: exact); one lane issues the block's two MMAs into one of two TMEM accumulators
+//     and commits them; sixteen warps read back each block's sums (tcgen05.ld) and accumulate.
 // Every wait is bounded by %globaltimer and raises the session's error flag; tensor memory is
 // freed on every path.
 #include <cuda_runtime.h>
@@ -46,8 +46,8 @@
 namespace sx {
 namespace {
 
-constexpr int kTW = 8;             // warps
-constexpr int kTT = kTW * 32;      // threads
+constexpr int kTW = 8;             // warps of the limb kernel
+constexpr int kTT = kTW * 32;      // its threads
 constexpr int kRows = 128;         // weight rows per CTA tile (8 Q8_0 tiles)
 constexpr int kTiles = kRows / kQ8Tile;
 constexpr int kChunkB = 8;         // blocks per k chunk
@@ -110,6 +110,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 16 consecutive 32-bit columns of this warp's 32 tensor-memory lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Four signed int8 (one word) -> four exact f16 (two words): bias to 128 + b, place each byte
@@ -140,12 +148,12 @@ __host__ __device__ __forceinline__ int canon16_off(int n, int k) {
 // the f32 pairs (l0, l2) and (l1, l3)
 __host__ __device__ __forceinline__ int limb_row(int t, int l) { return 4 * t + ((l & 1) << 1) + (l >> 1); }
 
-// ---- the B operand: int8 limbs of x for every k block, in the canonical layout ----------
+// ---- the B operand: limbs of x for every k block, f16 in the canonical layout -----------
 // One CTA per token: the row into shared memory (every load in flight at once), the RMSNorm
 // denominator exactly as k_gemv_q8 computes it (256 threads, k strided by 256, warp sums added
 // in warp order), then per 32-wide block the limb split of the normed values (exact to 2^-27
-// of the block max) as rows limb_row(t, 0..3) of that block's operand, and the block's
-// power-of-two scale.
+// of the block max) as rows limb_row(t, 0..3) of that block's f16 operand (exact: |limb| <=
+// 128), and the block's power-of-two scale.
 template <int MT>
 __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo g, uint8_t* Bg, float* sxg) {
   extern __shared__ float xrow[];  // [K]
@@ -206,27 +214,49 @@ __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo 
     __syncwarp();
     const int limb = lane >> 3, kk = 4 * (lane & 7);
     const uint32_t word = *reinterpret_cast<const uint32_t*>(&scr[warp][limb][kk]);
-    *reinterpret_cast<uint32_t*>(Bg + (size_t)b * N * 32 + canon_off(limb_row(t, limb), kk)) = word;
+    *reinterpret_cast<uint2*>(Bg + (size_t)b * N * 64 + canon16_off(limb_row(t, limb), kk)) = s8x4_to_f16x4(word);
     if (lane == 0) sxg[(size_t)b * MT + t] = sx;
     __syncwarp();
   }
 }
 
+// Warp roles of k_gemm_tc (20 warps):
+//   warp 0        one lane bulk-copies the items' tile records (two stages) and each k chunk's
+//                 f16 B operands and x scales (one chunk resident);
+//   warp 1        one lane issues the two MMAs of every block and commits them;
+//   warps 2-3     widen each block's 8 records to the f16 A operand and copy the block's row and
+//                 x scales (two stages, one per TMEM accumulator);
+//   warps 4-19    epilogue: TMEM lane quarter (warp - 4) % 4, token quarter (warp - 4) / 4.
+// Everything between the roles goes through mbarriers, so copies, widening, MMAs and read-backs
+// of different blocks overlap; every wait is bounded.
+constexpr int kGW = 20;            // warps of the GEMM
+constexpr int kGT = kGW * 32;
+constexpr int kWidenW = 2;         // widening warps
+constexpr int kEpiW = 16;          // epilogue warps
+
 template <int MT>
 struct TcSmem {
   static constexpr int N = 4 * MT;
   uint8_t stA[2][kStageBytes];              // an item's 8 tile records x 8 blocks
-  uint8_t stB[kChunkB * N * 32];            // the k chunk's B operands (int8, canonical)
+  uint8_t B16[kChunkB][N * 64];             // the k chunk's B operands, f16 canonical
   float stS[kChunkB * MT];                  // and its blocks' x scales
-  uint8_t A[2][kRows * 64];                 // one block's A operand, f16 canonical
-  uint8_t B[2][N * 64];                     // one block's B operand, f16 canonical
-  float dsb[2][kRows];                      // the block's row scales
-  uint64_t bar_a[2], bar_b, bar_mma[2];
+  uint8_t A16[2][kRows * 64];               // a block's A operand, f16 canonical (per TMEM half)
+  float dsb[2][kRows];                      // its row scales
+  float sxr[2][MT];                         // its x scales
+  uint64_t a_full[2], a_empty[2], b_full, b_empty, w_full[2], t_full[2], t_empty[2];
   uint32_t tmem_base;
 };
 
+// the CTA's items and the chunk bookkeeping every role walks identically
+struct TcWalk {
+  int c0, c1, n_rg;
+  __device__ int kc(int it) const { return it / n_rg; }
+  __device__ bool chunk_starts(int it) const { return it == c0 || kc(it) != kc(it - 1); }
+  __device__ bool chunk_ends(int it) const { return it + 1 == c1 || kc(it + 1) != kc(it); }
+};
+
 template <int MT>
-__global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGeo g, const uint8_t* Bg,
+__global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGeo g, const uint8_t* Bg,
                                                     const float* sxg) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   TcSmem<MT>& sm = *reinterpret_cast<TcSmem<MT>*>(smem_raw);
@@ -234,15 +264,23 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // items (k chunk, 128-row group), k-chunk-major: consecutive items share the B operand
   const int I = g.n_rg * g.nc;
-  const int c0 = (int)((long long)blockIdx.x * I / gridDim.x), c1 = (int)((long long)(blockIdx.x + 1) * I / gridDim.x);
+  TcWalk wk;
+  wk.c0 = (int)((long long)blockIdx.x * I / gridDim.x);
+  wk.c1 = (int)((long long)(blockIdx.x + 1) * I / gridDim.x);
+  wk.n_rg = g.n_rg;
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
+  auto nrec_of = [&](int kc) { return min(kChunkB, g.nb - kc * kChunkB); };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; i++) {
-      mbar_init(&sm.bar_a[i], 1);
-      mbar_init(&sm.bar_mma[i], 1);
+      mbar_init(&sm.a_full[i], 1);
+      mbar_init(&sm.a_empty[i], kWidenW);
+      mbar_init(&sm.w_full[i], kWidenW);
+      mbar_init(&sm.t_full[i], 1);
+      mbar_init(&sm.t_empty[i], kEpiW);
     }
-    mbar_init(&sm.bar_b, 1);
+    mbar_init(&sm.b_full, 1);
+    mbar_init(&sm.b_empty, 1 + kWidenW);  // the chunk's last MMAs (commit) + the widening warps
     mbar_fence_init();
   }
   if (warp == 0) {  // two accumulators of up to 256 columns
@@ -253,159 +291,151 @@ __global__ void __launch_bounds__(kTT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-
-  auto nrec_of = [&](int kc) { return min(kChunkB, g.nb - kc * kChunkB); };
-  // an item's tile records (weights: independent of the previous kernel)
-  auto issue_a = [&](int it, int st) {
-    const int kc = it / g.n_rg, rg = it % g.n_rg;
-    const int nrec = nrec_of(kc);
-    const int ntiles = min(kTiles, g.n_vt - rg * kTiles);
-    mbar_arrive_expect_tx(&sm.bar_a[st], (uint32_t)(ntiles * nrec * kQ8Rec));
-    for (int t = 0; t < ntiles; t++)
-      bulk_g2s(sm.stA[st] + t * kChunkB * kQ8Rec, W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB) * kQ8Rec,
-               (uint32_t)(nrec * kQ8Rec), &sm.bar_a[st]);
-  };
-  // a k chunk's B operands and scales (written by k_tc_limbs); the buffer is free: every
-  // block of the previous chunk has been widened (a __syncthreads separates them)
-  auto issue_b = [&](int kc) {
-    const int nrec = nrec_of(kc);
-    mbar_arrive_expect_tx(&sm.bar_b, (uint32_t)(nrec * N * 32 + nrec * MT * 4));
-    bulk_g2s(sm.stB, Bg + (size_t)kc * kChunkB * N * 32, (uint32_t)(nrec * N * 32), &sm.bar_b);
-    bulk_g2s(sm.stS, sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.bar_b);
-  };
-  if (threadIdx.x == 0 && c1 > c0) issue_a(c0, 0);
   pdl_launch_dependents();
-  pdl_wait();  // the B operands come from the limb kernel
-  if (threadIdx.x == 0 && c1 > c0) issue_b(c0 / g.n_rg);
 
-  // epilogue roles: TMEM lane quarter q (rows 32q..32q+31), token half h
-  const int q = warp & 3, h = warp >> 2;
-  const int row = q * 32 + lane;
-  constexpr int TPT = MT / 2;  // tokens per thread
-  unsigned long long acc[TPT];  // per token the packed pair {limbs 0/1, limbs 2/3}
-#pragma unroll
-  for (int i = 0; i < TPT; i++) acc[i] = 0ull;
-  const unsigned long long k128 = pack2(128.f, 128.f);
-
-  int blk = 0;  // blocks processed by this CTA (selects the operand buffer and the TMEM half)
-  int p_j = 0, p_rg = 0, p_kc = 0, p_nrec = 0;
-  bool have_prev = false;
-  float sx_prev[TPT];  // the previous block's x scales of this thread's tokens
-
-  // read back block (blk - 1)'s sums and accumulate; after its item's last block, the partials
-  auto epilogue = [&]() {
-    const int buf = (blk - 1) & 1;
-    tc_wait(&sm.bar_mma[buf], (uint32_t)(((blk - 1) >> 1) & 1), a.err);
-    tc_fence_after();
-    const float ds = sm.dsb[buf][row];
-#pragma unroll
-    for (int part = 0; part < TPT / 8; part++) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + (h * TPT + part * 8) * 4), r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int tl = part * 8 + i;
-        const float dsx = __fmul_rn(ds, sx_prev[tl]);
-        // (S_l0, S_l2) * 128 + (S_l1, S_l3): each sum rounded once, as (float)(int) does
-        const unsigned long long t = fma2(pack2u(r[4 * i], r[4 * i + 1]), k128, pack2u(r[4 * i + 2], r[4 * i + 3]));
-        acc[tl] = fma2(pack2(dsx, dsx), t, acc[tl]);
-      }
-    }
-    if (p_j == p_nrec - 1) {
-      const int vt = p_rg * kTiles + (row >> 4);
-      if (vt < g.n_vt) {
-        float* P = a.part + ((size_t)vt * g.nc + p_kc) * MT * 16 + (row & 15);
-#pragma unroll
-        for (int tl = 0; tl < TPT; tl++) {
-          const int t = h * TPT + tl;
-          float a01, a23;
-          unpack2(acc[tl], a01, a23);
-          if (t < a.M) __stcg(P + t * 16, a01 * 0x1p-7f + a23 * 0x1p-21f);
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      int n = 0, chunk = 0;
+      for (int it = wk.c0; it < wk.c1; it++, n++) {
+        const int st = n & 1, kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
+        if (n >= 2) tc_wait(&sm.a_empty[st], (uint32_t)(((n - 2) >> 1) & 1), a.err);
+        const int ntiles = min(kTiles, g.n_vt - rg * kTiles);
+        mbar_arrive_expect_tx(&sm.a_full[st], (uint32_t)(ntiles * nrec * kQ8Rec));
+        for (int t = 0; t < ntiles; t++)
+          bulk_g2s(sm.stA[st] + t * kChunkB * kQ8Rec,
+                   W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB) * kQ8Rec, (uint32_t)(nrec * kQ8Rec),
+                   &sm.a_full[st]);
+        if (wk.chunk_starts(it)) {
+          if (chunk == 0) pdl_wait();  // the B operands come from the limb kernel
+          if (chunk > 0) tc_wait(&sm.b_empty, (uint32_t)((chunk - 1) & 1), a.err);
+          mbar_arrive_expect_tx(&sm.b_full, (uint32_t)(nrec * N * 64 + nrec * MT * 4));
+          for (int j = 0; j < nrec; j++)
+            bulk_g2s(sm.B16[j], Bg + ((size_t)kc * kChunkB + j) * N * 64, (uint32_t)(N * 64), &sm.b_full);
+          bulk_g2s(sm.stS, sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.b_full);
+          chunk++;
         }
       }
-#pragma unroll
-      for (int tl = 0; tl < TPT; tl++) acc[tl] = 0ull;
     }
-  };
-
-  int n_items = 0, kc_cur = -1;
-  for (int it = c0; it < c1; it++, n_items++) {
-    const int sa = n_items & 1;
-    const int kc = it / g.n_rg, rg = it % g.n_rg;
-    const int nrec = nrec_of(kc);
-    // the next item's records go out an item ahead (stage sa ^ 1: its last widening finished
-    // in the previous item)
-    if (threadIdx.x == 0 && it + 1 < c1) issue_a(it + 1, sa ^ 1);
-    if (kc != kc_cur) {  // a new k chunk: its B operands (the first one was issued above)
-      if (kc_cur >= 0) {
-        __syncthreads();  // every widening of the previous chunk's operands is done
-        if (threadIdx.x == 0) issue_b(kc);
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      int blk = 0, chunk = 0;
+      for (int it = wk.c0; it < wk.c1; it++) {
+        const int kc = wk.kc(it), nrec = nrec_of(kc);
+        if (wk.chunk_starts(it)) tc_wait(&sm.b_full, (uint32_t)(chunk++ & 1), a.err);
+        for (int j = 0; j < nrec; j++, blk++) {
+          const int s = blk & 1;
+          tc_wait(&sm.w_full[s], (uint32_t)((blk >> 1) & 1), a.err);
+          if (blk >= 2) tc_wait(&sm.t_empty[s], (uint32_t)(((blk - 2) >> 1) & 1), a.err);
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(s * 256);
+          tc_mma(d, umma_desc(sm.A16[s], 128, 512), umma_desc(sm.B16[j], 128, 512), idesc_f16(kRows, N), 0u);
+          tc_mma(d, umma_desc(sm.A16[s] + 256, 128, 512), umma_desc(sm.B16[j] + 256, 128, 512), idesc_f16(kRows, N),
+                 1u);
+          tc_commit(&sm.t_full[s]);
+          if (j == nrec - 1 && wk.chunk_ends(it)) tc_commit(&sm.b_empty);
+        }
       }
-      tc_wait(&sm.bar_b, (uint32_t)((kc - c0 / g.n_rg) & 1), a.err);
-      kc_cur = kc;
     }
-    tc_wait(&sm.bar_a[sa], (uint32_t)((n_items >> 1) & 1), a.err);
-    for (int j = 0; j < nrec; j++, blk++) {
-      const int buf = blk & 1;
-      // the operand buffers `buf` were last read by block blk - 2's MMAs, whose completion the
-      // epilogue of block blk - 2 (in the previous iteration) waited for
-      {  // A: warp t widens tile t's record (lane L = 4g + c holds rows g, g + 8)
-        const int t = warp, L = lane;
-        const int gg = L >> 2, cc = L & 3;
-        const bool tile_ok = rg * kTiles + t < g.n_vt;
-        const uint8_t* rec = sm.stA[sa] + (t * kChunkB + j) * kQ8Rec;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (tile_ok) v = lds128(rec + L * 16);
-        uint8_t* A = sm.A[buf];
-        const int m0 = t * 16 + gg, m1 = m0 + 8;
-        *reinterpret_cast<uint2*>(A + canon16_off(m0, 4 * cc)) = s8x4_to_f16x4(v.x);
-        *reinterpret_cast<uint2*>(A + canon16_off(m1, 4 * cc)) = s8x4_to_f16x4(v.y);
-        *reinterpret_cast<uint2*>(A + canon16_off(m0, 16 + 4 * cc)) = s8x4_to_f16x4(v.z);
-        *reinterpret_cast<uint2*>(A + canon16_off(m1, 16 + 4 * cc)) = s8x4_to_f16x4(v.w);
-        if (L < 16)
-          sm.dsb[buf][t * 16 + L] =
-              tile_ok ? __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(L))) : 0.f;
+  } else if (warp < 2 + kWidenW) {
+    // ---- widening: warp w widens tiles w - 2, w, w + 2, ... of each block ----
+    const int ww = warp - 2;
+    int blk = 0, n = 0, chunk = 0;
+    for (int it = wk.c0; it < wk.c1; it++, n++) {
+      const int st = n & 1, kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
+      if (wk.chunk_starts(it)) tc_wait(&sm.b_full, (uint32_t)(chunk++ & 1), a.err);
+      tc_wait(&sm.a_full[st], (uint32_t)((n >> 1) & 1), a.err);
+      for (int j = 0; j < nrec; j++, blk++) {
+        const int s = blk & 1;
+        // A16[s], dsb[s], sxr[s] were last read for block blk - 2 (its MMAs and read-back)
+        if (blk >= 2) tc_wait(&sm.t_empty[s], (uint32_t)(((blk - 2) >> 1) & 1), a.err);
+        const int gg = lane >> 2, cc = lane & 3;
+        for (int t = ww; t < kTiles; t += kWidenW) {
+          const bool tile_ok = rg * kTiles + t < g.n_vt;
+          const uint8_t* rec = sm.stA[st] + (t * kChunkB + j) * kQ8Rec;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (tile_ok) v = lds128(rec + lane * 16);
+          uint8_t* A = sm.A16[s];
+          const int m0 = t * 16 + gg, m1 = m0 + 8;
+          *reinterpret_cast<uint2*>(A + canon16_off(m0, 4 * cc)) = s8x4_to_f16x4(v.x);
+          *reinterpret_cast<uint2*>(A + canon16_off(m1, 4 * cc)) = s8x4_to_f16x4(v.y);
+          *reinterpret_cast<uint2*>(A + canon16_off(m0, 16 + 4 * cc)) = s8x4_to_f16x4(v.z);
+          *reinterpret_cast<uint2*>(A + canon16_off(m1, 16 + 4 * cc)) = s8x4_to_f16x4(v.w);
+          if (lane < 16)
+            sm.dsb[s][t * 16 + lane] =
+                tile_ok ? __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(lane))) : 0.f;
+        }
+        for (int i = ww * 32 + lane; i < MT; i += kWidenW * 32) sm.sxr[s][i] = sm.stS[j * MT + i];
+        fence_async_smem();  // the A operand written by threads becomes visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.w_full[s]);
       }
-      // B: 16-byte pieces (row n, k 16 p .. 16 p + 15) widened to 32 bytes
-      for (int i = threadIdx.x; i < N * 2; i += kTT) {
-        const int n = i >> 1, pk = (i & 1) * 16;
-        const uint4 v = lds128(sm.stB + (size_t)j * N * 32 + canon_off(n, pk));
-        uint8_t* B = sm.B[buf];
-        const uint2 w0 = s8x4_to_f16x4(v.x), w1 = s8x4_to_f16x4(v.y), w2 = s8x4_to_f16x4(v.z),
-                    w3 = s8x4_to_f16x4(v.w);
-        *reinterpret_cast<uint4*>(B + canon16_off(n, pk)) = make_uint4(w0.x, w0.y, w1.x, w1.y);
-        *reinterpret_cast<uint4*>(B + canon16_off(n, pk + 8)) = make_uint4(w2.x, w2.y, w3.x, w3.y);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.a_empty[st]);
+        if (wk.chunk_ends(it)) mbar_arrive(&sm.b_empty);  // stS of this chunk is no longer read
       }
-      fence_async_smem();  // the operands written by threads become visible to the tensor core
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      if (threadIdx.x == 0) {
-        const uint32_t d = tmem + (uint32_t)(buf * 256);
-        tc_mma(d, umma_desc(sm.A[buf], 128, 512), umma_desc(sm.B[buf], 128, 512), idesc_f16(kRows, N), 0u);
-        tc_mma(d, umma_desc(sm.A[buf] + 256, 128, 512), umma_desc(sm.B[buf] + 256, 128, 512), idesc_f16(kRows, N), 1u);
-        tc_commit(&sm.bar_mma[buf]);
-      }
-      if (have_prev) epilogue();
-      // this block's x scales for the next epilogue (stS is stable until the chunk changes,
-      // which a __syncthreads precedes)
+    }
+  } else {
+    // ---- epilogue ----
+    const int e = warp - 2 - kWidenW, q = e & 3, h = e >> 2;
+    const int row = q * 32 + lane;
+    constexpr int TPT = MT / 4;  // tokens per thread
+    unsigned long long acc[TPT];  // per token the packed pair {limbs 0/1, limbs 2/3}
 #pragma unroll
-      for (int tl = 0; tl < TPT; tl++) sx_prev[tl] = sm.stS[j * MT + h * TPT + tl];
-      // the next MMA into the other TMEM half must not start before this read-back is done
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      p_j = j;
-      p_rg = rg;
-      p_kc = kc;
-      p_nrec = nrec;
-      have_prev = true;
+    for (int i = 0; i < TPT; i++) acc[i] = 0ull;
+    const unsigned long long k128 = pack2(128.f, 128.f);
+    int blk = 0;
+    for (int it = wk.c0; it < wk.c1; it++) {
+      const int kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
+      for (int j = 0; j < nrec; j++, blk++) {
+        const int s = blk & 1;
+        tc_wait(&sm.w_full[s], (uint32_t)((blk >> 1) & 1), a.err);  // acquires dsb[s], sxr[s]
+        tc_wait(&sm.t_full[s], (uint32_t)((blk >> 1) & 1), a.err);
+        tc_fence_after();
+        const float ds = sm.dsb[s][row];
+#pragma unroll
+        for (int part = 0; part < TPT / 4; part++) {
+          uint32_t r[16];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * 256 + (h * TPT + part * 4) * 4), r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const int tl = part * 4 + i;
+            const float dsx = __fmul_rn(ds, sm.sxr[s][h * TPT + tl]);
+            // (S_l0, S_l2) * 128 + (S_l1, S_l3): each sum rounded once, as (float)(int) does
+            const unsigned long long t = fma2(pack2u(r[4 * i], r[4 * i + 1]), k128, pack2u(r[4 * i + 2], r[4 * i + 3]));
+            acc[tl] = fma2(pack2(dsx, dsx), t, acc[tl]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.t_empty[s]);
+        if (j == nrec - 1) {
+          const int vt = rg * kTiles + (row >> 4);
+          if (vt < g.n_vt) {
+            float* P = a.part + ((size_t)vt * g.nc + kc) * MT * 16 + (row & 15);
+#pragma unroll
+            for (int tl = 0; tl < TPT; tl++) {
+              const int t = h * TPT + tl;
+              float a01, a23;
+              unpack2(acc[tl], a01, a23);
+              if (t < a.M) __stcg(P + t * 16, a01 * 0x1p-7f + a23 * 0x1p-21f);
+            }
+          }
+#pragma unroll
+          for (int tl = 0; tl < TPT; tl++) acc[tl] = 0ull;
+        }
+      }
     }
   }
-  if (have_prev) epilogue();  // the last block (blk - 1)
+  // every role is done: the epilogue waited for every MMA and read back every accumulator.
+  // Every thread also waits for the prerequisite grid, so this grid never completes before it.
+  pdl_wait();
   tc_fence_before();
   __syncthreads();
+  tc_fence_after();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
 
@@ -413,7 +443,7 @@ template <int MT>
 cudaError_t launch_tc_t(const GemvArgs& a, const TcGeo& g, int sms, uint8_t* scratch, cudaStream_t st) {
   constexpr int N = 4 * MT;
   uint8_t* Bg = scratch;
-  float* sxg = reinterpret_cast<float*>(scratch + (size_t)g.nb * N * 32);
+  float* sxg = reinterpret_cast<float*>(scratch + (size_t)g.nb * N * 64);
   const size_t row_bytes = (size_t)g.K * 4;
   cudaError_t e = cudaSuccess;
   if (row_bytes > 48 * 1024) {
@@ -431,7 +461,7 @@ cudaError_t launch_tc_t(const GemvArgs& a, const TcGeo& g, int sms, uint8_t* scr
   const long long I = (long long)g.n_rg * g.nc;
   const int grid = (int)std::max(1LL, std::min<long long>(I, sms));
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kTT), smem, st, attr);
+  cudaLaunchConfig_t cfg = launch_cfg(dim3(grid), dim3(kGT), smem, st, attr);
   return cudaLaunchKernelEx(&cfg, kern, a, g, (const uint8_t*)Bg, (const float*)sxg);
 }
 
@@ -444,7 +474,7 @@ bool tc_enabled() {
 }
 
 // The partials of a Q8_0 GEMV of 9..64 tokens (Mt = 16, 32 or 64) on the tensor cores.
-size_t gemm_tc_scratch_bytes(int K, int Mt) { return (size_t)(K / 32) * (4 * Mt * 32 + Mt * 4); }
+size_t gemm_tc_scratch_bytes(int K, int Mt) { return (size_t)(K / 32) * (4 * Mt * 64 + Mt * 4); }
 
 cudaError_t launch_gemm_tc(const GemvArgs& a, int Mt, int K, int nb, int nc, int t_first, int n_vt, int sms,
                            cudaStream_t st) {
