@@ -24,12 +24,12 @@
 //     computes the RMSNorm denominator as k_gemv_q8 does (256 threads, k strided by 256, warp
 //     sums added in warp order) and splits the normed values of each 32-wide block into int8
 //     limbs, written once per launch as every block's f16 B operand in the canonical
-//     no-swizzle K-major layout (8-row x 16-byte core matrices), rows n = 4 * token +
-//     {l0, l2, l1, l3};
+//     no-swizzle K-major layout (8-row x 16-byte core matrices), rows grouped by token pairs
+//     (limb_row);
 //   - k_gemm_tc (one CTA per SM, a contiguous range of (k chunk, 128-row group) items, k-chunk
 //     major so consecutive items share their B operands) runs four warp roles joined by
-//     mbarriers: a copy lane bulk-copies each item's 8 tile records (8 x 4352 contiguous bytes,
-//     two stages) and each chunk's B operands (cp.async.bulk); two warps widen every block's
+//     mbarriers: a copy lane bulk-copies each half item's 8 x 4 tile records (three stages) and
+//     each chunk's B operands (cp.async.bulk); two warps widen every block's
 //     quants to f16 in the canonical layout (byte-permute into 0x64xx and one packed f16
 //     subtract: exact); one lane issues the block's two MMAs into one of two TMEM accumulators
 //     and commits them; sixteen warps read back each block's sums (tcgen05.ld) and accumulate.
@@ -99,17 +99,6 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 32 consecutive 32-bit columns of this warp's 32 tensor-memory lanes
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
 // 16 consecutive 32-bit columns of this warp's 32 tensor-memory lanes
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -136,17 +125,13 @@ struct TcGeo {
   int K, nb, nc, n_vt, n_rg;  // columns, blocks, k chunks, tiles, 128-row groups
 };
 
-// byte offset of element (row n, k) of a canonical K-major operand of 32 int8 per row
-__host__ __device__ __forceinline__ int canon_off(int n, int k) {
-  return (n >> 3) * 256 + (k >> 4) * 128 + (n & 7) * 16 + (k & 15);
-}
 // byte offset of element (row n, k) of a canonical K-major operand of 32 f16 per row
 __host__ __device__ __forceinline__ int canon16_off(int n, int k) {
   return (n >> 3) * 512 + (k >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2;
 }
-// B row of limb l of token t: limbs ordered l0, l2, l1, l3 so that a token's sums read back as
-// the f32 pairs (l0, l2) and (l1, l3)
-__host__ __device__ __forceinline__ int limb_row(int t, int l) { return 4 * t + ((l & 1) << 1) + (l >> 1); }
+// B row of limb l of token t: tokens in pairs, each limb's two tokens adjacent
+// (S_l0[t], S_l0[t+1], S_l1[t], S_l1[t+1], ...), so a pair's sums read back as f32x2 operands
+__host__ __device__ __forceinline__ int limb_row(int t, int l) { return 8 * (t >> 1) + 2 * l + (t & 1); }
 
 // ---- the B operand: limbs of x for every k block, f16 in the canonical layout -----------
 // One CTA per token: the row into shared memory (every load in flight at once), the RMSNorm
@@ -221,29 +206,34 @@ __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo 
 }
 
 // Warp roles of k_gemm_tc (20 warps):
-//   warp 0        one lane bulk-copies the items' tile records (two stages) and each k chunk's
-//                 f16 B operands and x scales (one chunk resident);
+//   warp 0        one lane bulk-copies the tile records of each half item (4 blocks, three
+//                 stages) and each k chunk's f16 B operands and x scales (one chunk resident);
 //   warp 1        one lane issues the two MMAs of every block and commits them;
 //   warps 2-3     widen each block's 8 records to the f16 A operand and copy the block's row and
-//                 x scales (two stages, one per TMEM accumulator);
-//   warps 4-19    epilogue: TMEM lane quarter (warp - 4) % 4, token quarter (warp - 4) / 4.
+//                 x scales into a ring of four stages, so they run up to four blocks ahead;
+//   warps 4-19    read-back: TMEM lane quarter (warp - 4) % 4, token quarter (warp - 4) / 4.
 // Everything between the roles goes through mbarriers, so copies, widening, MMAs and read-backs
-// of different blocks overlap; every wait is bounded.
+// of different blocks overlap: with the operands ahead, a block costs the larger of its MMAs
+// and its read-back, which alternate between two TMEM accumulators. Every wait is bounded.
 constexpr int kGW = 20;            // warps of the GEMM
 constexpr int kGT = kGW * 32;
 constexpr int kWidenW = 2;         // widening warps
-constexpr int kEpiW = 16;          // epilogue warps
+constexpr int kEpiW = 16;          // read-back warps
+constexpr int kHalfB = kChunkB / 2;  // blocks per staged half item
+constexpr int kAStages = 3;        // staged half items
+constexpr int kWStages = 4;        // widened blocks
 
 template <int MT>
 struct TcSmem {
   static constexpr int N = 4 * MT;
-  uint8_t stA[2][kStageBytes];              // an item's 8 tile records x 8 blocks
-  uint8_t B16[kChunkB][N * 64];             // the k chunk's B operands, f16 canonical
-  float stS[kChunkB * MT];                  // and its blocks' x scales
-  uint8_t A16[2][kRows * 64];               // a block's A operand, f16 canonical (per TMEM half)
-  float dsb[2][kRows];                      // its row scales
-  float sxr[2][MT];                         // its x scales
-  uint64_t a_full[2], a_empty[2], b_full, b_empty, w_full[2], t_full[2], t_empty[2];
+  uint8_t stA[kAStages][kTiles * kHalfB * kQ8Rec];  // a half item: 8 tiles x 4 records
+  uint8_t B16[kChunkB][N * 64];                     // the k chunk's B operands, f16 canonical
+  float stS[kChunkB * MT];                          // and its blocks' x scales
+  uint8_t A16[kWStages][kRows * 64];                // a block's A operand, f16 canonical
+  float dsb[kWStages][kRows];                       // its row scales
+  float sxr[kWStages][MT];                          // its x scales
+  uint64_t a_full[kAStages], a_empty[kAStages], b_full, b_empty, w_full[kWStages], w_empty[kWStages], t_full[2],
+      t_empty[2];
   uint32_t tmem_base;
 };
 
@@ -270,12 +260,18 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   wk.n_rg = g.n_rg;
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
   auto nrec_of = [&](int kc) { return min(kChunkB, g.nb - kc * kChunkB); };
+  auto half_blocks = [&](int nrec, int hf) { return min(kHalfB, nrec - hf * kHalfB); };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kAStages; i++) {
       mbar_init(&sm.a_full[i], 1);
       mbar_init(&sm.a_empty[i], kWidenW);
+    }
+    for (int i = 0; i < kWStages; i++) {
       mbar_init(&sm.w_full[i], kWidenW);
+      mbar_init(&sm.w_empty[i], 1 + kEpiW);  // the block's MMAs (commit) + the read-back warps
+    }
+    for (int i = 0; i < 2; i++) {
       mbar_init(&sm.t_full[i], 1);
       mbar_init(&sm.t_empty[i], kEpiW);
     }
@@ -294,46 +290,53 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   pdl_launch_dependents();
 
   if (warp == 0) {
-    // ---- producer ----
+    // ---- copy lane ----
     if (lane == 0) {
-      int n = 0, chunk = 0;
-      for (int it = wk.c0; it < wk.c1; it++, n++) {
-        const int st = n & 1, kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
-        if (n >= 2) tc_wait(&sm.a_empty[st], (uint32_t)(((n - 2) >> 1) & 1), a.err);
+      int ns = 0, chunk = 0;
+      for (int it = wk.c0; it < wk.c1; it++) {
+        const int kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
         const int ntiles = min(kTiles, g.n_vt - rg * kTiles);
-        mbar_arrive_expect_tx(&sm.a_full[st], (uint32_t)(ntiles * nrec * kQ8Rec));
-        for (int t = 0; t < ntiles; t++)
-          bulk_g2s(sm.stA[st] + t * kChunkB * kQ8Rec,
-                   W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB) * kQ8Rec, (uint32_t)(nrec * kQ8Rec),
-                   &sm.a_full[st]);
-        if (wk.chunk_starts(it)) {
-          if (chunk == 0) pdl_wait();  // the B operands come from the limb kernel
-          if (chunk > 0) tc_wait(&sm.b_empty, (uint32_t)((chunk - 1) & 1), a.err);
-          mbar_arrive_expect_tx(&sm.b_full, (uint32_t)(nrec * N * 64 + nrec * MT * 4));
-          for (int j = 0; j < nrec; j++)
-            bulk_g2s(sm.B16[j], Bg + ((size_t)kc * kChunkB + j) * N * 64, (uint32_t)(N * 64), &sm.b_full);
-          bulk_g2s(sm.stS, sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.b_full);
-          chunk++;
+        for (int hf = 0; hf < 2; hf++) {
+          const int nbh = half_blocks(nrec, hf);
+          if (nbh <= 0) break;
+          const int st = ns % kAStages;
+          if (ns >= kAStages) tc_wait(&sm.a_empty[st], (uint32_t)(((ns - kAStages) / kAStages) & 1), a.err);
+          mbar_arrive_expect_tx(&sm.a_full[st], (uint32_t)(ntiles * nbh * kQ8Rec));
+          for (int t = 0; t < ntiles; t++)
+            bulk_g2s(sm.stA[st] + t * kHalfB * kQ8Rec,
+                     W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB + hf * kHalfB) * kQ8Rec,
+                     (uint32_t)(nbh * kQ8Rec), &sm.a_full[st]);
+          ns++;
+          if (hf == 0 && wk.chunk_starts(it)) {
+            if (chunk == 0) pdl_wait();  // the B operands come from the limb kernel
+            if (chunk > 0) tc_wait(&sm.b_empty, (uint32_t)((chunk - 1) & 1), a.err);
+            mbar_arrive_expect_tx(&sm.b_full, (uint32_t)(nrec * N * 64 + nrec * MT * 4));
+            for (int j = 0; j < nrec; j++)
+              bulk_g2s(sm.B16[j], Bg + ((size_t)kc * kChunkB + j) * N * 64, (uint32_t)(N * 64), &sm.b_full);
+            bulk_g2s(sm.stS, sxg + (size_t)kc * kChunkB * MT, (uint32_t)(nrec * MT * 4), &sm.b_full);
+            chunk++;
+          }
         }
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
+    // ---- MMA lane ----
     if (lane == 0) {
       int blk = 0, chunk = 0;
       for (int it = wk.c0; it < wk.c1; it++) {
         const int kc = wk.kc(it), nrec = nrec_of(kc);
         if (wk.chunk_starts(it)) tc_wait(&sm.b_full, (uint32_t)(chunk++ & 1), a.err);
         for (int j = 0; j < nrec; j++, blk++) {
-          const int s = blk & 1;
-          tc_wait(&sm.w_full[s], (uint32_t)((blk >> 1) & 1), a.err);
+          const int r = blk % kWStages, s = blk & 1;
+          tc_wait(&sm.w_full[r], (uint32_t)((blk / kWStages) & 1), a.err);
           if (blk >= 2) tc_wait(&sm.t_empty[s], (uint32_t)(((blk - 2) >> 1) & 1), a.err);
           tc_fence_after();
           const uint32_t d = tmem + (uint32_t)(s * 256);
-          tc_mma(d, umma_desc(sm.A16[s], 128, 512), umma_desc(sm.B16[j], 128, 512), idesc_f16(kRows, N), 0u);
-          tc_mma(d, umma_desc(sm.A16[s] + 256, 128, 512), umma_desc(sm.B16[j] + 256, 128, 512), idesc_f16(kRows, N),
+          tc_mma(d, umma_desc(sm.A16[r], 128, 512), umma_desc(sm.B16[j], 128, 512), idesc_f16(kRows, N), 0u);
+          tc_mma(d, umma_desc(sm.A16[r] + 256, 128, 512), umma_desc(sm.B16[j] + 256, 128, 512), idesc_f16(kRows, N),
                  1u);
           tc_commit(&sm.t_full[s]);
+          tc_commit(&sm.w_empty[r]);
           if (j == nrec - 1 && wk.chunk_ends(it)) tc_commit(&sm.b_empty);
         }
       }
@@ -341,96 +344,111 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
   } else if (warp < 2 + kWidenW) {
     // ---- widening: warp w widens tiles w - 2, w, w + 2, ... of each block ----
     const int ww = warp - 2;
-    int blk = 0, n = 0, chunk = 0;
-    for (int it = wk.c0; it < wk.c1; it++, n++) {
-      const int st = n & 1, kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
-      if (wk.chunk_starts(it)) tc_wait(&sm.b_full, (uint32_t)(chunk++ & 1), a.err);
-      tc_wait(&sm.a_full[st], (uint32_t)((n >> 1) & 1), a.err);
-      for (int j = 0; j < nrec; j++, blk++) {
-        const int s = blk & 1;
-        // A16[s], dsb[s], sxr[s] were last read for block blk - 2 (its MMAs and read-back)
-        if (blk >= 2) tc_wait(&sm.t_empty[s], (uint32_t)(((blk - 2) >> 1) & 1), a.err);
-        const int gg = lane >> 2, cc = lane & 3;
-        for (int t = ww; t < kTiles; t += kWidenW) {
-          const bool tile_ok = rg * kTiles + t < g.n_vt;
-          const uint8_t* rec = sm.stA[st] + (t * kChunkB + j) * kQ8Rec;
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (tile_ok) v = lds128(rec + lane * 16);
-          uint8_t* A = sm.A16[s];
-          const int m0 = t * 16 + gg, m1 = m0 + 8;
-          *reinterpret_cast<uint2*>(A + canon16_off(m0, 4 * cc)) = s8x4_to_f16x4(v.x);
-          *reinterpret_cast<uint2*>(A + canon16_off(m1, 4 * cc)) = s8x4_to_f16x4(v.y);
-          *reinterpret_cast<uint2*>(A + canon16_off(m0, 16 + 4 * cc)) = s8x4_to_f16x4(v.z);
-          *reinterpret_cast<uint2*>(A + canon16_off(m1, 16 + 4 * cc)) = s8x4_to_f16x4(v.w);
-          if (lane < 16)
-            sm.dsb[s][t * 16 + lane] =
-                tile_ok ? __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(lane))) : 0.f;
+    const int gg = lane >> 2, cc = lane & 3;
+    int blk = 0, ns = 0, chunk = 0;
+    for (int it = wk.c0; it < wk.c1; it++) {
+      const int kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
+      if (wk.chunk_starts(it)) tc_wait(&sm.b_full, (uint32_t)(chunk++ & 1), a.err);  // stS
+      for (int hf = 0; hf < 2; hf++) {
+        const int nbh = half_blocks(nrec, hf);
+        if (nbh <= 0) break;
+        const int st = ns % kAStages;
+        tc_wait(&sm.a_full[st], (uint32_t)((ns / kAStages) & 1), a.err);
+        for (int jj = 0; jj < nbh; jj++, blk++) {
+          const int j = hf * kHalfB + jj, r = blk % kWStages;
+          // ring stage r was last used by block blk - 4 (its MMAs and its read-back)
+          if (blk >= kWStages) tc_wait(&sm.w_empty[r], (uint32_t)(((blk - kWStages) / kWStages) & 1), a.err);
+          uint8_t* A = sm.A16[r];
+          for (int t = ww; t < kTiles; t += kWidenW) {
+            const bool tile_ok = rg * kTiles + t < g.n_vt;
+            const uint8_t* rec = sm.stA[st] + (t * kHalfB + jj) * kQ8Rec;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (tile_ok) v = lds128(rec + lane * 16);
+            const int m0 = t * 16 + gg, m1 = m0 + 8;
+            *reinterpret_cast<uint2*>(A + canon16_off(m0, 4 * cc)) = s8x4_to_f16x4(v.x);
+            *reinterpret_cast<uint2*>(A + canon16_off(m1, 4 * cc)) = s8x4_to_f16x4(v.y);
+            *reinterpret_cast<uint2*>(A + canon16_off(m0, 16 + 4 * cc)) = s8x4_to_f16x4(v.z);
+            *reinterpret_cast<uint2*>(A + canon16_off(m1, 16 + 4 * cc)) = s8x4_to_f16x4(v.w);
+            if (lane < 16)
+              sm.dsb[r][t * 16 + lane] =
+                  tile_ok ? __half2float(*reinterpret_cast<const __half*>(rec + q8_scale_off(lane))) : 0.f;
+          }
+          for (int i = ww * 32 + lane; i < MT; i += kWidenW * 32) sm.sxr[r][i] = sm.stS[j * MT + i];
+          fence_async_smem();  // the A operand written by threads becomes visible to the tensor core
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.w_full[r]);
         }
-        for (int i = ww * 32 + lane; i < MT; i += kWidenW * 32) sm.sxr[s][i] = sm.stS[j * MT + i];
-        fence_async_smem();  // the A operand written by threads becomes visible to the tensor core
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.w_full[s]);
+        if (lane == 0) mbar_arrive(&sm.a_empty[st]);
+        ns++;
       }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sm.a_empty[st]);
-        if (wk.chunk_ends(it)) mbar_arrive(&sm.b_empty);  // stS of this chunk is no longer read
-      }
+      if (lane == 0 && wk.chunk_ends(it)) mbar_arrive(&sm.b_empty);  // stS of this chunk is no longer read
     }
   } else {
-    // ---- epilogue ----
+    // ---- read-back ----
     const int e = warp - 2 - kWidenW, q = e & 3, h = e >> 2;
     const int row = q * 32 + lane;
-    constexpr int TPT = MT / 4;  // tokens per thread
-    unsigned long long acc[TPT];  // per token the packed pair {limbs 0/1, limbs 2/3}
+    constexpr int TPT = MT / 4;   // tokens per thread
+    constexpr int NPR = TPT / 2;  // token pairs per thread
+    unsigned long long acc01[NPR], acc23[NPR];  // per token pair the packed {limbs 0/1} and {limbs 2/3}
 #pragma unroll
-    for (int i = 0; i < TPT; i++) acc[i] = 0ull;
+    for (int i = 0; i < NPR; i++) acc01[i] = acc23[i] = 0ull;
     const unsigned long long k128 = pack2(128.f, 128.f);
     int blk = 0;
     for (int it = wk.c0; it < wk.c1; it++) {
       const int kc = wk.kc(it), rg = it % g.n_rg, nrec = nrec_of(kc);
       for (int j = 0; j < nrec; j++, blk++) {
-        const int s = blk & 1;
-        tc_wait(&sm.w_full[s], (uint32_t)((blk >> 1) & 1), a.err);  // acquires dsb[s], sxr[s]
+        const int r = blk % kWStages, s = blk & 1;
+        tc_wait(&sm.w_full[r], (uint32_t)((blk / kWStages) & 1), a.err);  // acquires dsb[r], sxr[r]
         tc_wait(&sm.t_full[s], (uint32_t)((blk >> 1) & 1), a.err);
         tc_fence_after();
-        const float ds = sm.dsb[s][row];
+        const unsigned long long ds2 = pack2(sm.dsb[r][row], sm.dsb[r][row]);
 #pragma unroll
-        for (int part = 0; part < TPT / 4; part++) {
-          uint32_t r[16];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * 256 + (h * TPT + part * 4) * 4), r);
+        for (int ld = 0; ld < NPR / 2; ld++) {
+          uint32_t v[16];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * 256 + 4 * h * TPT + 16 * ld), v);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const int tl = part * 4 + i;
-            const float dsx = __fmul_rn(ds, sm.sxr[s][h * TPT + tl]);
-            // (S_l0, S_l2) * 128 + (S_l1, S_l3): each sum rounded once, as (float)(int) does
-            const unsigned long long t = fma2(pack2u(r[4 * i], r[4 * i + 1]), k128, pack2u(r[4 * i + 2], r[4 * i + 3]));
-            acc[tl] = fma2(pack2(dsx, dsx), t, acc[tl]);
+          for (int i = 0; i < 2; i++) {
+            const int p = 2 * ld + i;
+            const float2 sx = *reinterpret_cast<const float2*>(&sm.sxr[r][h * TPT + 2 * p]);
+            const unsigned long long dsx = mul2(ds2, pack2(sx.x, sx.y));
+            // per token: S_l0 * 128 + S_l1 and S_l2 * 128 + S_l3, each rounded once as
+            // (float)(int) rounds the GEMV's integer sums
+            const uint32_t* w = v + 8 * i;
+            const unsigned long long t01 = fma2(pack2u(w[0], w[1]), k128, pack2u(w[2], w[3]));
+            const unsigned long long t23 = fma2(pack2u(w[4], w[5]), k128, pack2u(w[6], w[7]));
+            acc01[p] = fma2(dsx, t01, acc01[p]);
+            acc23[p] = fma2(dsx, t23, acc23[p]);
           }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.t_empty[s]);
+        if (lane == 0) {
+          mbar_arrive(&sm.t_empty[s]);
+          mbar_arrive(&sm.w_empty[r]);
+        }
         if (j == nrec - 1) {
           const int vt = rg * kTiles + (row >> 4);
           if (vt < g.n_vt) {
             float* P = a.part + ((size_t)vt * g.nc + kc) * MT * 16 + (row & 15);
 #pragma unroll
-            for (int tl = 0; tl < TPT; tl++) {
-              const int t = h * TPT + tl;
-              float a01, a23;
-              unpack2(acc[tl], a01, a23);
-              if (t < a.M) __stcg(P + t * 16, a01 * 0x1p-7f + a23 * 0x1p-21f);
+            for (int p = 0; p < NPR; p++) {
+              const int t = h * TPT + 2 * p;
+              float x0, x1, y0, y1;
+              unpack2(acc01[p], x0, x1);
+              unpack2(acc23[p], y0, y1);
+              if (t < a.M) __stcg(P + t * 16, x0 * 0x1p-7f + y0 * 0x1p-21f);
+              if (t + 1 < a.M) __stcg(P + (t + 1) * 16, x1 * 0x1p-7f + y1 * 0x1p-21f);
             }
           }
 #pragma unroll
-          for (int tl = 0; tl < TPT; tl++) acc[tl] = 0ull;
+          for (int p = 0; p < NPR; p++) acc01[p] = acc23[p] = 0ull;
         }
       }
     }
   }
-  // every role is done: the epilogue waited for every MMA and read back every accumulator.
+  // every role is done: the read-back waited for every MMA and read every accumulator.
   // Every thread also waits for the prerequisite grid, so this grid never completes before it.
   pdl_wait();
   tc_fence_before();

@@ -60,6 +60,11 @@ __device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigne
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
                                                    unsigned long long c) {
   unsigned long long d;
