@@ -57,7 +57,7 @@ constexpr uint64_t kTcWaitNs = 2000000000ull;
 __device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_wait_sleep(bar, parity)) {
     const uint64_t dt = global_ns() - t0;
     if (dt > 1000000ull && err && __ldcg(err) != 0) return;
     if (dt > kTcWaitNs) {

@@ -135,7 +135,7 @@ __device__ __noinline__ void grid_wait(const StackArgs& a, unsigned long long ta
 __device__ __noinline__ void mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_wait_sleep(bar, parity)) {
     const uint64_t dt = global_ns() - t0;
     if (dt > 1000000ull && __ldcg(err) != 0) return;
     if (dt > kBarWaitNs) {
@@ -920,8 +920,10 @@ __global__ void __launch_bounds__(kThreadsStack, 1) k_stack(const __grid_constan
     auto pwait = [&](uint64_t* bar, uint32_t parity) {
       if (mbar_try_wait(bar, parity)) return;
       const uint64_t t0 = global_ns();
-      while (!mbar_try_wait(bar, parity)) {
-        if (!pf_done && pf < issued + a.l2_ahead) {
+      for (;;) {
+        const bool more = !pf_done && pf < issued + a.l2_ahead;  // prefetch work while waiting
+        if (more ? mbar_try_wait(bar, parity) : mbar_wait_sleep(bar, parity)) return;
+        if (more) {
           pf_one();
           continue;
         }

@@ -161,6 +161,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same, but the thread may sleep until the phase completes (at most `ns` nanoseconds)
+// instead of returning at once: waiting warps then take no issue slots from working ones.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns = 100000) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // `bytes` (a multiple of 16) from global `src` (16-byte aligned) into shared `dst` (16-byte
 // aligned); completion is counted on `bar` as transaction bytes. A plain bulk copy: no tensor
 // map and no multicast.
