@@ -205,19 +205,19 @@ __global__ void __launch_bounds__(kTT) k_tc_limbs(const GemvArgs a, const TcGeo 
   }
 }
 
-// Warp roles of k_gemm_tc (20 warps):
+// Warp roles of k_gemm_tc (22 warps):
 //   warp 0        one lane bulk-copies the tile records of each half item (4 blocks, three
 //                 stages) and each k chunk's f16 B operands and x scales (one chunk resident);
 //   warp 1        one lane issues the two MMAs of every block and commits them;
-//   warps 2-3     widen each block's 8 records to the f16 A operand and copy the block's row and
-//                 x scales into a ring of four stages, so they run up to four blocks ahead;
-//   warps 4-19    read-back: TMEM lane quarter (warp - 4) % 4, token quarter (warp - 4) / 4.
+//   warps 2-5     widen each block's 8 records (two tiles each) to the f16 A operand and copy the
+//                 block's row and x scales into a ring of four stages, up to four blocks ahead;
+//   warps 6-21    read-back: TMEM lane quarter warp % 4, token quarter (warp - 6) / 4.
 // Everything between the roles goes through mbarriers, so copies, widening, MMAs and read-backs
 // of different blocks overlap: with the operands ahead, a block costs the larger of its MMAs
 // and its read-back, which alternate between two TMEM accumulators. Every wait is bounded.
-constexpr int kGW = 20;            // warps of the GEMM
+constexpr int kGW = 22;            // warps of the GEMM
 constexpr int kGT = kGW * 32;
-constexpr int kWidenW = 2;         // widening warps
+constexpr int kWidenW = 4;         // widening warps (two tiles each)
 constexpr int kEpiW = 16;          // read-back warps
 constexpr int kHalfB = kChunkB / 2;  // blocks per staged half item
 constexpr int kAStages = 3;        // staged half items
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
       }
     }
   } else if (warp < 2 + kWidenW) {
-    // ---- widening: warp w widens tiles w - 2, w, w + 2, ... of each block ----
+    // ---- widening: warp w widens tiles w - 2 and w + 2 of each block ----
     const int ww = warp - 2;
     const int gg = lane >> 2, cc = lane & 3;
     int blk = 0, ns = 0, chunk = 0;
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
     }
   } else {
     // ---- read-back ----
-    const int e = warp - 2 - kWidenW, q = e & 3, h = e >> 2;
+    const int e = warp - 2 - kWidenW, q = warp & 3, h = e >> 2;  // a warp reads TMEM lanes 32 (warp % 4)..
     const int row = q * 32 + lane;
     constexpr int TPT = MT / 4;   // tokens per thread
     constexpr int NPR = TPT / 2;  // token pairs per thread
@@ -403,14 +403,17 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
         tc_wait(&sm.t_full[s], (uint32_t)((blk >> 1) & 1), a.err);
         tc_fence_after();
         const unsigned long long ds2 = pack2(sm.dsb[r][row], sm.dsb[r][row]);
+        constexpr int LDP = NPR >= 4 ? 4 : NPR;  // token pairs per batch of loads (two per load)
 #pragma unroll
-        for (int ld = 0; ld < NPR / 2; ld++) {
-          uint32_t v[16];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * 256 + 4 * h * TPT + 16 * ld), v);
+        for (int ld = 0; ld < NPR / LDP; ld++) {  // up to two loads of 16 columns in flight
+          uint32_t v[8 * LDP];
+          const uint32_t col = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s * 256 + 4 * h * TPT + 8 * LDP * ld);
+#pragma unroll
+          for (int k = 0; k < LDP / 2; k++) tmem_ld16(col + 16 * k, *reinterpret_cast<uint32_t(*)[16]>(v + 16 * k));
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 2; i++) {
-            const int p = 2 * ld + i;
+          for (int i = 0; i < LDP; i++) {
+            const int p = LDP * ld + i;
             const float2 sx = *reinterpret_cast<const float2*>(&sm.sxr[r][h * TPT + 2 * p]);
             const unsigned long long dsx = mul2(ds2, pack2(sx.x, sx.y));
             // per token: S_l0 * 128 + S_l1 and S_l2 * 128 + S_l3, each rounded once as
