@@ -24,15 +24,15 @@
 //     computes the RMSNorm denominator as k_gemv_q8 does (256 threads, k strided by 256, warp
 //     sums added in warp order) and splits the normed values of each 32-wide block into int8
 //     limbs, written once per launch as every block's f16 B operand in the canonical
-//     no-swizzle K-major layout (8-row x 16-byte core matrices), rows grouped by token pairs
-//     (limb_row);
+//     K-major layout with the 64-byte swizzle, rows grouped by token pairs (limb_row);
 //   - k_gemm_tc (one CTA per SM, a contiguous range of (k chunk, 128-row group) items, k-chunk
 //     major so consecutive items share their B operands) runs four warp roles joined by
 //     mbarriers: a copy lane bulk-copies each half item's 8 x 4 tile records (three stages) and
-//     each chunk's B operands (cp.async.bulk); two warps widen every block's
-//     quants to f16 in the canonical layout (byte-permute into 0x64xx and one packed f16
-//     subtract: exact); one lane issues the block's two MMAs into one of two TMEM accumulators
-//     and commits them; sixteen warps read back each block's sums (tcgen05.ld) and accumulate.
+//     each chunk's B operands (cp.async.bulk), after prefetching all the CTA's records into L2;
+//     four warps widen every block's quants to f16 in the swizzled layout (byte-permute into
+//     0x64xx and one packed f16 subtract: exact); one lane issues the block's two MMAs into
+//     one of two TMEM accumulators and commits them; sixteen warps read back each block's sums
+//     (tcgen05.ld) and accumulate.
 // Every wait is bounded by %globaltimer and raises the session's error flag; tensor memory is
 // freed on every path.
 #include <cuda_runtime.h>
@@ -51,7 +51,6 @@ constexpr int kTT = kTW * 32;      // its threads
 constexpr int kRows = 128;         // weight rows per CTA tile (8 Q8_0 tiles)
 constexpr int kTiles = kRows / kQ8Tile;
 constexpr int kChunkB = 8;         // blocks per k chunk
-constexpr int kStageBytes = kTiles * kChunkB * kQ8Rec;  // 34816
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 __device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -67,17 +66,18 @@ __device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t parity, int* err
   }
 }
 
-// UMMA shared-memory descriptor: canonical K-major layout without swizzle, 8-row x 16-byte
-// core matrices, LBO = distance between core matrices adjacent along K, SBO = between 8-row
-// groups.
-__device__ __forceinline__ uint64_t umma_desc(const void* p, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptor of the canonical K-major layout with the 64-byte swizzle (one
+// 32-wide block of f16 per row): 8-row atoms of 512 bytes (SBO), the leading offset field 1 as the swizzled K-major
+// form requires, layout type 4. The second MMA of a block starts 32 bytes further.
+__device__ __forceinline__ uint64_t umma_desc_sw64(const void* p) {
   const uint32_t a = smem_addr(p);
   uint64_t d = 0;
   d |= (uint64_t)((a >> 4) & 0x3fff);
-  d |= (uint64_t)((lbo >> 4) & 0x3fff) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3fff) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
-  return d;                // base offset 0, swizzle none
+  d |= (uint64_t)1 << 16;           // leading byte offset (16 B units): 1
+  d |= (uint64_t)(512 >> 4) << 32;  // stride byte offset: 512
+  d |= (uint64_t)1 << 46;           // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;           // SWIZZLE_64B
+  return d;
 }
 // instruction descriptor of kind::f16: f32 accumulator, f16 A and B, both K-major
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
@@ -125,15 +125,18 @@ struct TcGeo {
   int K, nb, nc, n_vt, n_rg;  // columns, blocks, k chunks, tiles, 128-row groups
 };
 
-// byte offset of element (row n, k) of a canonical K-major operand of 32 f16 per row
+// byte offset of element (row n, k < 32) of a K-major f16 operand, 64-byte swizzle: rows of 64
+// bytes, 8-row atoms of 512 bytes, 16-byte chunk c of row r stored at chunk c ^ ((r & 7) >> 1)
+// (address bits 4-5 ^= bits 7-8). Pieces of 4 elements (k % 4 == 0) stay contiguous.
 __host__ __device__ __forceinline__ int canon16_off(int n, int k) {
-  return (n >> 3) * 512 + (k >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2;
+  const int o = (n >> 3) * 512 + (n & 7) * 64 + k * 2;
+  return o ^ (((o >> 7) & 3) << 4);
 }
 // B row of limb l of token t: tokens in pairs, each limb's two tokens adjacent
 // (S_l0[t], S_l0[t+1], S_l1[t], S_l1[t+1], ...), so a pair's sums read back as f32x2 operands
 __host__ __device__ __forceinline__ int limb_row(int t, int l) { return 8 * (t >> 1) + 2 * l + (t & 1); }
 
-// ---- the B operand: limbs of x for every k block, f16 in the canonical layout -----------
+// ---- the B operand: limbs of x for every k block, f16 in the swizzled layout -----------
 // One CTA per token: the row into shared memory (every load in flight at once), the RMSNorm
 // denominator exactly as k_gemv_q8 computes it (256 threads, k strided by 256, warp sums added
 // in warp order), then per 32-wide block the limb split of the normed values (exact to 2^-27
@@ -227,9 +230,9 @@ template <int MT>
 struct TcSmem {
   static constexpr int N = 4 * MT;
   uint8_t stA[kAStages][kTiles * kHalfB * kQ8Rec];  // a half item: 8 tiles x 4 records
-  uint8_t B16[kChunkB][N * 64];                     // the k chunk's B operands, f16 canonical
+  alignas(512) uint8_t B16[kChunkB][N * 64];        // the k chunk's B operands, f16 swizzled
   float stS[kChunkB * MT];                          // and its blocks' x scales
-  uint8_t A16[kWStages][kRows * 64];                // a block's A operand, f16 canonical
+  alignas(512) uint8_t A16[kWStages][kRows * 64];   // a block's A operand, f16 swizzled
   float dsb[kWStages][kRows];                       // its row scales
   float sxr[kWStages][MT];                          // its x scales
   uint64_t a_full[kAStages], a_empty[kAStages], b_full, b_empty, w_full[kWStages], w_empty[kWStages], t_full[2],
@@ -307,6 +310,15 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
                      W + ((size_t)(rg * kTiles + t) * g.nb + (size_t)kc * kChunkB + hf * kHalfB) * kQ8Rec,
                      (uint32_t)(nbh * kQ8Rec), &sm.a_full[st]);
           ns++;
+          if (ns == 1) {  // every later record of this CTA into L2 now: the copies then hit L2
+            for (int i2 = it; i2 < wk.c1; i2++) {
+              const int kc2 = wk.kc(i2), rg2 = i2 % g.n_rg, nr2 = nrec_of(kc2);
+              const int nt2 = min(kTiles, g.n_vt - rg2 * kTiles);
+              for (int t = 0; t < nt2; t++)
+                bulk_prefetch_l2(W + ((size_t)(rg2 * kTiles + t) * g.nb + (size_t)kc2 * kChunkB) * kQ8Rec,
+                                 (uint32_t)(nr2 * kQ8Rec));
+            }
+          }
           if (hf == 0 && wk.chunk_starts(it)) {
             if (chunk == 0) pdl_wait();  // the B operands come from the limb kernel
             if (chunk > 0) tc_wait(&sm.b_empty, (uint32_t)((chunk - 1) & 1), a.err);
@@ -332,9 +344,8 @@ __global__ void __launch_bounds__(kGT, 1) k_gemm_tc(const GemvArgs a, const TcGe
           if (blk >= 2) tc_wait(&sm.t_empty[s], (uint32_t)(((blk - 2) >> 1) & 1), a.err);
           tc_fence_after();
           const uint32_t d = tmem + (uint32_t)(s * 256);
-          tc_mma(d, umma_desc(sm.A16[r], 128, 512), umma_desc(sm.B16[j], 128, 512), idesc_f16(kRows, N), 0u);
-          tc_mma(d, umma_desc(sm.A16[r] + 256, 128, 512), umma_desc(sm.B16[j] + 256, 128, 512), idesc_f16(kRows, N),
-                 1u);
+          tc_mma(d, umma_desc_sw64(sm.A16[r]), umma_desc_sw64(sm.B16[j]), idesc_f16(kRows, N), 0u);
+          tc_mma(d, umma_desc_sw64(sm.A16[r] + 32), umma_desc_sw64(sm.B16[j] + 32), idesc_f16(kRows, N), 1u);
           tc_commit(&sm.t_full[s]);
           tc_commit(&sm.w_empty[r]);
           if (j == nrec - 1 && wk.chunk_ends(it)) tc_commit(&sm.b_empty);
