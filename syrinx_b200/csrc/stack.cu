@@ -282,21 +282,7 @@ __device__ __forceinline__ void rms_den_all(const StackArgs& a, const float* ss,
 
 // ---- GEMV phase ------------------------------------------------------------------------
 // Consumes this CTA's items of one matrix from the ring (item j of the phase by warp j % 8)
-// and writes each item's 16 row sums per token into the row-major partials. A warp takes its
-// items two at a time (j and j + 8), interleaving their block products, so that with only eight
-// consumer warps per SM twice as many independent tensor-core products are in flight.
-template <int MT>
-struct ItemPos {
-  int slot, round, vt, kc;
-};
-template <int MT>
-__device__ __forceinline__ void item_advance(ItemPos<MT>& it, int n, int nslot, const StackGeo& g) {
-  it.slot += n;
-  while (it.slot >= nslot) it.slot -= nslot, it.round++;
-  it.vt += n;
-  while (it.vt >= g.n_vt) it.vt -= g.n_vt, it.kc++;
-}
-
+// and writes each item's 16 row sums per token into the row-major partials.
 template <int MT>
 __device__ __noinline__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t* full, uint64_t* empty, int nslot,
                                           int& ctr, const StackGeo& g, const Plan& p, float* part, int* err) {
@@ -304,37 +290,39 @@ __device__ __noinline__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t*
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bl = MT == 1 ? (lane & 15) : lane;
   const int ncp = pad4(g.nc), NR = g.n_vt * 16;
-  // this warp's first item j = warp: (slot, round) and (tile, k chunk) advance incrementally
-  ItemPos<MT> a0;
-  a0.slot = ctr % nslot;
-  a0.round = ctr / nslot;
-  a0.vt = p.vt0;
-  a0.kc = p.kc0;
-  item_advance<MT>(a0, warp, nslot, g);
-  // the products of one block of one item into acc
-  auto block = [&](const uint8_t* rec, int kc, int i, float (&acc)[NP][2]) {
-    const int b = kc * kIB + i;
-    if (b < g.nb) {
-      const uint4 qv = lds128(rec + i * kQ8Rec + lane * 16);
-      const uint32_t sw = lds32(rec + i * kQ8Rec + 512 + (lane >> 2) * 4);
-      const float2 ds = __half22float2(*reinterpret_cast<const __half2*>(&sw));
-      const int bi = b - p.b_lo;
+  // this warp's items j = warp, warp + 8, ...: (k chunk, tile) and (slot, round) advance
+  // incrementally
+  int vt = p.vt0 + warp, kc = p.kc0;
+  while (vt >= g.n_vt) vt -= g.n_vt, kc++;
+  int slot = (ctr + warp) % nslot, round = (ctr + warp) / nslot;
+  for (int j = warp; j < p.n; j += kCW) {
+    mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), err);
+    const uint8_t* rec = ring + (size_t)slot * kItemBytes;
+    float acc[NP][2];
 #pragma unroll
-      for (int q = 0; q < NP; q++) {
-        const uint2 bf = sm.bfr[bi][q][bl];
-        const int tok = MT == 1 ? 0 : 2 * q + ((lane >> 1) & 1);
-        const float sx = sm.sxs[bi][tok < MT ? tok : 0];
-        int d[4];
-        mma_s8_16832(qv, bf, d);
-        acc[q][0] = fmaf(__fmul_rn(ds.x, sx), (float)(d[0] * 128 + d[1]), acc[q][0]);
-        acc[q][1] = fmaf(__fmul_rn(ds.y, sx), (float)(d[2] * 128 + d[3]), acc[q][1]);
+    for (int q = 0; q < NP; q++) acc[q][0] = acc[q][1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kIB; i++) {
+      const int b = kc * kIB + i;
+      if (b < g.nb) {
+        const uint4 qv = lds128(rec + i * kQ8Rec + lane * 16);
+        const uint32_t sw = lds32(rec + i * kQ8Rec + 512 + (lane >> 2) * 4);
+        const float2 ds = __half22float2(*reinterpret_cast<const __half2*>(&sw));
+        const int bi = b - p.b_lo;
+#pragma unroll
+        for (int q = 0; q < NP; q++) {
+          const uint2 bf = sm.bfr[bi][q][bl];
+          const int tok = MT == 1 ? 0 : 2 * q + ((lane >> 1) & 1);
+          const float sx = sm.sxs[bi][tok < MT ? tok : 0];
+          int d[4];
+          mma_s8_16832(qv, bf, d);
+          acc[q][0] = fmaf(__fmul_rn(ds.x, sx), (float)(d[0] * 128 + d[1]), acc[q][0]);
+          acc[q][1] = fmaf(__fmul_rn(ds.y, sx), (float)(d[2] * 128 + d[3]), acc[q][1]);
+        }
       }
     }
-  };
-  // release an item's slot and write its row sums
-  auto finish = [&](const ItemPos<MT>& it, float (&acc)[NP][2]) {
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[it.slot]);
+    if (lane == 0) mbar_arrive(&empty[slot]);
     const float wgt = (lane & 1) ? 0x1p-21f : 0x1p-7f;
 #pragma unroll
     for (int q = 0; q < NP; q++) {
@@ -343,37 +331,15 @@ __device__ __noinline__ void gemv_consume(Smem<MT>& sm, uint8_t* ring, uint64_t*
       v1 += __shfl_down_sync(0xffffffffu, v1, 1);
       const int tok = 2 * q + ((lane >> 1) & 1);
       if ((lane & 1) == 0 && tok < MT) {
-        float* P = part + ((size_t)tok * NR + it.vt * 16 + (lane >> 2)) * ncp + it.kc;
+        float* P = part + ((size_t)tok * NR + vt * 16 + (lane >> 2)) * ncp + kc;
         __stcg(P, v0);
         __stcg(P + (size_t)8 * ncp, v1);
       }
     }
-  };
-  for (int j = warp; j < p.n; j += 2 * kCW) {
-    const bool two = j + kCW < p.n;
-    ItemPos<MT> a1 = a0;
-    item_advance<MT>(a1, kCW, nslot, g);
-    float acc0[NP][2], acc1[NP][2];
-#pragma unroll
-    for (int q = 0; q < NP; q++) acc0[q][0] = acc0[q][1] = acc1[q][0] = acc1[q][1] = 0.f;
-    mbar_wait_bounded(&full[a0.slot], (uint32_t)(a0.round & 1), err);
-    const uint8_t* rec0 = ring + (size_t)a0.slot * kItemBytes;
-    if (two) {
-      mbar_wait_bounded(&full[a1.slot], (uint32_t)(a1.round & 1), err);
-      const uint8_t* rec1 = ring + (size_t)a1.slot * kItemBytes;
-#pragma unroll
-      for (int i = 0; i < kIB; i++) {
-        block(rec0, a0.kc, i, acc0);
-        block(rec1, a1.kc, i, acc1);
-      }
-      finish(a0, acc0);
-      finish(a1, acc1);
-    } else {
-#pragma unroll
-      for (int i = 0; i < kIB; i++) block(rec0, a0.kc, i, acc0);
-      finish(a0, acc0);
-    }
-    item_advance<MT>(a0, 2 * kCW, nslot, g);
+    slot += kCW;
+    if (slot >= nslot) slot -= nslot, round++;
+    vt += kCW;
+    while (vt >= g.n_vt) vt -= g.n_vt, kc++;
   }
   ctr += p.n;
 }
