@@ -271,15 +271,69 @@ def bench_device(args):
         "prefill_s": round(t_prefill, 3),
         "sampled": sampled,
     }
-    if rank == 0 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
     be.close()
     model.close()
+    if not args.no_b8:
+        res["b8"] = bench_b8(args, local, stream, dist, world, peak, peak_kind)
+    if rank == 0 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res), flush=True)
+
+
+def bench_b8(args, local, stream, dist, world, peak, peak_kind):
+    """Config 4 on each GPU: the Qwen3-4B-shaped dual-AR in Q4_K, 8 utterances (prompts 256-1024
+    tokens, seeded) prefilled into one paged cache and decoded as one greedy batch of 8 (every
+    batched step streams the weights once for all 8 frames). frames/s counts every
+    utterance's frames; the roofline counts the weights once per step plus each utterance's
+    KV read (f32 cache, and at bf16 as the path defines it)."""
+    import torch
+    import syrinx_b200 as sx
+    from syrinx_b200 import dp
+    from syrinx_b200.configs import SX_DTYPE_Q4_K, frame_bytes
+    from syrinx_b200.workloads import config4_prompts
+
+    cfg = sx.QWEN3_4B
+    K, W = min(args.steps, 64), max(3, min(args.warmup, 8))
+    model = sx.Model(cfg, sx.synth_blob(cfg, SX_DTYPE_Q4_K, seed=SEED), device=local)
+    prompts = config4_prompts(cfg, 8)
+    lens = [p.shape[1] for p in prompts]
+    be = sx.B200DualAr(model, max_ctx=max(lens) + K + W + 8, max_batch=8)
+    be.set_stream(stream.cuda_stream)
+    t0 = time.time()
+    be.prefill_batch(prompts)
+    t_prefill = time.time() - t0
+    be.decode_greedy_batch(8, W, mask_stop=True)
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        s1.record(stream)
+        got = be.decode_greedy_batch(8, K, mask_stop=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = dp.max_over_ranks(s1.elapsed_time(e1), dist, device="cuda")
+    assert got.shape[:2] == (8, K), got.shape
+    ctx_mean = [T + W + (K - 1) / 2.0 for T in lens]
+    w_bytes = frame_bytes(cfg, SX_DTYPE_Q4_K, ctx=0, semantic_head=True)["total"]
+    kv_f32 = sum(frame_bytes(cfg, SX_DTYPE_Q4_K, ctx=c, kv_elem=4)["kv"] for c in ctx_mean)
+    kv_bf16 = sum(frame_bytes(cfg, SX_DTYPE_Q4_K, ctx=c, kv_elem=2)["kv"] for c in ctx_mean)
+    steps_per_s = K / (ms * 1e-3)
+    be.close()
+    model.close()
+    return {"value": round(8 * K * world / (ms * 1e-3), 2), "unit": "frames/s", "per_gpu_batch": 8,
+            "ms_per_batched_step": round(ms / K, 4), "steps": K, "warmup": W,
+            "workload": "config4 qwen3-4b-shaped dual-AR Q4_K, 8 utterances per GPU batched (prompts " +
+                        "/".join(str(t) for t in lens) + "), greedy, stop masked",
+            "prefill_batch_s": round(t_prefill, 3),
+            "hbm_roofline": {"bytes_per_step": w_bytes + kv_f32, "frac_of_peak": round(
+                (w_bytes + kv_f32) * steps_per_s / (peak * 1e9), 4), "bytes_per_step_kv_bf16": w_bytes + kv_bf16,
+                "frac_of_peak_kv_bf16": round((w_bytes + kv_bf16) * steps_per_s / (peak * 1e9), 4),
+                "peak_gbs": peak, "peak_kind": peak_kind}}
 
 
 TP_METRIC = "semantic frames/s per tensor-parallel group, config 5 (4B-shape Q8_0 dual-AR b1, KV grown to 8192)"
@@ -459,6 +513,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-b8", action="store_true", help="skip the config-4 batch-8 Q4_K measurement")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--tp", type=int, default=0, help="config 5: tensor-parallel group of N GPUs")
     ap.add_argument("--tp-ctx", type=int, default=8192)

@@ -6,6 +6,7 @@ Qwen3-4B-shaped model with fewer layers, so an `ncu --set full` capture stays sm
   python -m syrinx_b200.profile --what frames --layers 8 --frames 4 --prompt 512
   python -m syrinx_b200.profile --what stack --layers 36 --prompt 512   (phase timing, printed)
   python -m syrinx_b200.profile --what prefill --layers 36 --prompt 512  (prefill time, printed)
+  python -m syrinx_b200.profile --what batch --layers 8 --q4k --frames 4   (8 utterances batched)
 """
 from __future__ import annotations
 
@@ -19,7 +20,7 @@ from .workloads import dual_ar_prompt
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill"], default="gemv")
+    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill", "batch"], default="gemv")
     ap.add_argument("--kind", type=int, default=2, help="0 wqkv, 1 wo, 2 w1|w3, 3 w2")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--launches", type=int, default=16)
@@ -30,6 +31,15 @@ def main():
     cfg = shrink(QWEN3_4B, args.layers, min(4, args.layers))
     wtype = SX_DTYPE_Q4_K if args.q4k else SX_DTYPE_Q8_0
     model = Model(cfg, synth_blob(cfg, wtype, seed=2))
+    if args.what == "batch":  # 8 utterances of args.prompt .. args.prompt + 7 tokens, decoded batched
+        be = B200DualAr(model, max_ctx=args.prompt + 16 + args.frames, max_batch=8)
+        be.prefill_batch([dual_ar_prompt(cfg, args.prompt + i, (args.prompt + i) * 3 // 4, seed=20 + i)
+                          for i in range(8)])
+        be.decode_greedy_batch(8, args.frames, mask_stop=True)
+        be.close()
+        model.close()
+        print("profile run ok")
+        return
     be = B200DualAr(model, max_ctx=args.prompt + 64 + args.frames)
     prompt = dual_ar_prompt(cfg, args.prompt, max(1, args.prompt * 3 // 4), seed=2)
     t0 = time.perf_counter()

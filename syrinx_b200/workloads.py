@@ -36,3 +36,10 @@ def prompt_for(cfg: ModelConfig, T: int, seed: int, semantic_frac: float = 430 /
     if cfg.num_codebooks == 0:
         return lm_prompt(cfg, T, seed)
     return dual_ar_prompt(cfg, T, int(round(T * semantic_frac)), seed)
+
+
+def config4_prompts(cfg: ModelConfig, n: int = 8) -> list:
+    """Config 4's batch: n utterances with prompt lengths uniform in [256, 1024] (seeded),
+    each with the config-3 share of reference-voice positions."""
+    lens = np.random.default_rng(4).integers(256, 1025, n)
+    return [dual_ar_prompt(cfg, int(T), int(round(T * 430 / 512)), seed=40 + i) for i, T in enumerate(lens)]

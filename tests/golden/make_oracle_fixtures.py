@@ -29,10 +29,9 @@ CONFIG4_UTTERANCES = 8
 
 
 def config4_prompts(cfg):
-    from syrinx_b200.workloads import dual_ar_prompt
+    from syrinx_b200.workloads import config4_prompts as prompts
 
-    lens = np.random.default_rng(4).integers(256, 1025, CONFIG4_UTTERANCES)
-    return [dual_ar_prompt(cfg, int(T), int(round(T * 430 / 512)), seed=40 + i) for i, T in enumerate(lens)]
+    return prompts(cfg, CONFIG4_UTTERANCES)
 
 
 def config4() -> None:
