@@ -317,7 +317,7 @@ def bench_b8(args, local, stream, dist, world, peak, peak_kind):
         e1.record(stream)
     torch.cuda.synchronize()
     ms = dp.max_over_ranks(s1.elapsed_time(e1), dist, device="cuda")
-    assert got.shape[:2] == (8, K), got.shape
+    assert len(got) == 8 and all(g.shape[0] == K for g in got), [g.shape for g in got]
     ctx_mean = [T + W + (K - 1) / 2.0 for T in lens]
     w_bytes = frame_bytes(cfg, SX_DTYPE_Q4_K, ctx=0, semantic_head=True)["total"]
     kv_f32 = sum(frame_bytes(cfg, SX_DTYPE_Q4_K, ctx=c, kv_elem=4)["kv"] for c in ctx_mean)
