@@ -214,6 +214,188 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   }
 }
 
+// ---- Q4_K tile records (sx_internal.hpp, kQ4Rec): the same integer tensor-core scheme ----
+// A Q4_K weight of sub-block j is d * sc_j * q - dmin * m_j (q a nibble 0..15, sc_j / m_j 6-bit),
+// so per row and sub-block sum_k w_k x_k = d * sc_j * sum_k q_k x_k - dmin * m_j * sum_k x_k.
+// The first sum is exact on the tensor cores exactly as for Q8_0 (nibbles widened in the A
+// fragment registers with one mask and one shift per word; d * sc_j is an exact f32); the
+// second uses the block sum of the normed x, one warp sum per (block, token) beside the limb
+// split, added on the lanes that carry the limb pair (0, 1). A k chunk is one super-block.
+struct ItemQ4 {
+  uint4 q[4];     // the 4 sub-block pairs' quants of this lane
+  uint4 sc, mn;   // 6-bit scales / mins of rows g (x, y) and g + 8 (z, w)
+  uint2 dd;       // {d, dmin} of row g, then of row g + 8 (f16)
+};
+
+__device__ __forceinline__ void load_item_q4(const uint8_t* W, const Q8Geo& g, int tile, int kc, int lane, ItemQ4& it) {
+  const uint8_t* r = W + ((size_t)tile * g.nc + kc) * kQ4Rec;
+#pragma unroll
+  for (int jp = 0; jp < 4; jp++) it.q[jp] = ldg_stream(r + jp * 512 + lane * 16);
+  it.sc = ldg_stream(r + 2048 + (lane >> 2) * 16);
+  it.mn = ldg_stream(r + 2176 + (lane >> 2) * 16);
+  it.dd.x = ldg_stream32(r + 2304 + (lane >> 2) * 8);
+  it.dd.y = ldg_stream32(r + 2304 + (lane >> 2) * 8 + 4);
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q4k(const GemvArgs a, const Q8Geo g) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int NP = (M + 1) / 2;
+  __shared__ __align__(16) int8_t scr[kWarps][4][32];
+  __shared__ float red[kWarps][M];
+  __shared__ float den[M];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const long long I = (long long)g.n_vt * g.nc;
+  const long long c0 = (long long)blockIdx.x * I / gridDim.x;
+  const long long c1 = (long long)(blockIdx.x + 1) * I / gridDim.x;
+  const int kc_lo = (int)(c0 / g.n_vt), kc_hi = c1 > c0 ? (int)((c1 - 1) / g.n_vt) : kc_lo;
+  const int b_lo = kc_lo * kCB, b_hi = min(g.nb, (kc_hi + 1) * kCB);
+  // shared: B fragments [block - b_lo][NP][32 lanes] | x scales [block - b_lo][M] | x block sums
+  uint2* bfr = reinterpret_cast<uint2*>(smem);
+  float* sxs = reinterpret_cast<float*>(smem + (size_t)(b_hi - b_lo) * NP * 256);
+  float* xsum = sxs + (size_t)(b_hi - b_lo) * M;
+  const long long w0 = c0 + (c1 - c0) * warp / kWarps, w1 = c0 + (c1 - c0) * (warp + 1) / kWarps;
+  int kc = (int)(w0 / g.n_vt), vt = (int)(w0 % g.n_vt), left = (int)(w1 - w0);
+  const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
+
+  pdl_launch_dependents();
+  ItemQ4 it;
+  if (left > 0) load_item_q4(W, g, g.t_first + vt, kc, lane, it);
+  pdl_wait();
+
+  if (a.norm_w) {  // RMSNorm denominators, as k_gemv_q8
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) ss[m] = 0.f;
+    for (int k = threadIdx.x; k < g.K; k += kThreads)
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
+        ss[m] = fmaf(v, v, ss[m]);
+      }
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const float t = warp_sum(ss[m]);
+      if (lane == 0) red[warp][m] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x < M) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
+      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)g.K), a.eps));
+    }
+    __syncthreads();
+  }
+
+  // x limbs (as k_gemv_q8) and the block sums of x, one warp per (block, token)
+  for (int u = warp; u < (b_hi - b_lo) * M; u += kWarps) {
+    const int bi = u / M, m = u % M, k = (b_lo + bi) * 32 + lane;
+    float v = 0.f;
+    if (m < a.M) {
+      v = ld_cg(a.x + (size_t)m * g.K + k);
+      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), a.norm_w[k]);
+    }
+    const float bsum = warp_sum(v);
+    const float mx = warp_max(fabsf(v));
+    const int e = (__float_as_int(mx) >> 23) & 0xff;
+    float sc = 0.f, sx = 0.f;
+    if (e == 255 || __any_sync(0xffffffffu, v != v)) {
+      sx = __int_as_float(0x7fc00000);
+    } else if (e >= 6) {
+      sc = __int_as_float((259 - e) << 23);
+      sx = __int_as_float((e - 5) << 23);
+    }
+    const float s = v * sc;
+    const float l0 = rintf(s);
+    float r = (s - l0) * 128.f;
+    const float l1 = rintf(r);
+    r = (r - l1) * 128.f;
+    const float l2 = rintf(r);
+    r = (r - l2) * 128.f;
+    const float l3 = rintf(r);
+    scr[warp][0][lane] = (int8_t)(int)l0;
+    scr[warp][1][lane] = (int8_t)(int)l1;
+    scr[warp][2][lane] = (int8_t)(int)l2;
+    scr[warp][3][lane] = (int8_t)(int)l3;
+    __syncwarp();
+    if (lane < 16) {
+      const int n = lane >> 2, c = lane & 3;
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&scr[warp][n][4 * c]);
+      w.y = *reinterpret_cast<const uint32_t*>(&scr[warp][n][16 + 4 * c]);
+      bfr[(bi * NP + (m >> 1)) * 32 + (m & 1) * 16 + lane] = w;
+    }
+    if (lane == 0) {
+      sxs[bi * M + m] = sx;
+      xsum[bi * M + m] = bsum;
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+
+  const int bl = M == 1 ? (lane & 15) : lane;
+  const float mmul = (lane & 1) ? 0.f : -128.f;  // the min term rides on the limb-(0, 1) lanes
+  while (left > 0) {
+    float acc[NP][2];
+#pragma unroll
+    for (int p = 0; p < NP; p++) acc[p][0] = acc[p][1] = 0.f;
+    const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&it.dd.x));   // d, dmin of row g
+    const float2 dg8 = __half22float2(*reinterpret_cast<const __half2*>(&it.dd.y));  // of row g + 8
+#pragma unroll
+    for (int j = 0; j < kCB; j++) {
+      const int bi = kc * kCB + j - b_lo;
+      const uint32_t w0 = (j & 1) ? it.q[j >> 1].z : it.q[j >> 1].x;
+      const uint32_t w1 = (j & 1) ? it.q[j >> 1].w : it.q[j >> 1].y;
+      uint4 af;
+      af.x = w0 & 0x0F0F0F0Fu;
+      af.y = w1 & 0x0F0F0F0Fu;
+      af.z = (w0 >> 4) & 0x0F0F0F0Fu;
+      af.w = (w1 >> 4) & 0x0F0F0F0Fu;
+      const int sh = 8 * (j & 3);
+      const uint32_t scg = (((j < 4) ? it.sc.x : it.sc.y) >> sh) & 0xff, scg8 = (((j < 4) ? it.sc.z : it.sc.w) >> sh) & 0xff;
+      const uint32_t mng = (((j < 4) ? it.mn.x : it.mn.y) >> sh) & 0xff, mng8 = (((j < 4) ? it.mn.z : it.mn.w) >> sh) & 0xff;
+      const float d1g = __fmul_rn(dg.x, (float)scg), d1g8 = __fmul_rn(dg8.x, (float)scg8);
+      const float m1g = __fmul_rn(__fmul_rn(dg.y, (float)mng), mmul);
+      const float m1g8 = __fmul_rn(__fmul_rn(dg8.y, (float)mng8), mmul);
+#pragma unroll
+      for (int p = 0; p < NP; p++) {
+        const uint2 bf = bfr[(bi * NP + p) * 32 + bl];
+        const int tok = M == 1 ? 0 : 2 * p + ((lane >> 1) & 1);
+        const float sx = sxs[bi * M + tok];
+        const float xs = xsum[bi * M + tok];
+        int d[4];
+        mma_s8_16832(af, bf, d);
+        acc[p][0] = fmaf(__fmul_rn(d1g, sx), (float)(d[0] * 128 + d[1]), acc[p][0]);
+        acc[p][1] = fmaf(__fmul_rn(d1g8, sx), (float)(d[2] * 128 + d[3]), acc[p][1]);
+        acc[p][0] = fmaf(m1g, xs, acc[p][0]);
+        acc[p][1] = fmaf(m1g8, xs, acc[p][1]);
+      }
+    }
+    const int done_vt = vt, done_kc = kc;
+    if (++vt == g.n_vt) {
+      vt = 0;
+      kc++;
+    }
+    left--;
+    if (left > 0) load_item_q4(W, g, g.t_first + vt, kc, lane, it);
+    const float wgt = (lane & 1) ? 0x1p-21f : 0x1p-7f;
+    float* P = a.part + ((size_t)done_vt * g.nc + done_kc) * M * 16;
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+      float v0 = acc[p][0] * wgt, v1 = acc[p][1] * wgt;
+      v0 += __shfl_down_sync(0xffffffffu, v0, 1);
+      v1 += __shfl_down_sync(0xffffffffu, v1, 1);
+      const int tok = 2 * p + ((lane >> 1) & 1);
+      if ((lane & 1) == 0 && tok < M) {
+        __stcg(P + tok * 16 + (lane >> 2), v0);
+        __stcg(P + tok * 16 + (lane >> 2) + 8, v1);
+      }
+    }
+  }
+}
+
 // Row sums over the k-chunks in a fixed order (four lanes per output unit each add a
 // contiguous quarter of the chunks, then the quarters are added in order), then the
 // epilogue. Units: rows (STORE / ADD / ARGMAX) or gate/up row pairs (SWIGLU) per token.
@@ -396,13 +578,14 @@ template <int M>
 cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st) {
   constexpr int NP = (M + 1) / 2;
   static const int sms = num_sms();
-  if (M >= 16 && tc_enabled() && a.n_extra == 0 && g.t_first == 0) {
+  const bool q4 = a.w.dtype == kDtypeQ4KT;
+  if (!q4 && M >= 16 && tc_enabled() && a.n_extra == 0 && g.t_first == 0) {
     // prefill chunks: the same partials from the tensor-core GEMM
     cudaError_t e = launch_gemm_tc(a, M, g.K, g.nb, g.nc, g.t_first, g.n_vt, sms, st);
     if (e != cudaSuccess) return e;
     return launch_epilogue<M>(a, epi, g, st);
   }
-  auto kern = k_gemv_q8<M>;
+  auto kern = q4 ? k_gemv_q4k<M> : k_gemv_q8<M>;
   const long long I = (long long)g.n_vt * g.nc;
   // persistent grid of up to three CTAs per SM; shared memory holds the limbs of the
   // k-chunks a CTA spans (at most ceil(items per CTA / n_vt) + 1 of them)
@@ -412,7 +595,7 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
     grid = (int)std::max(1LL, std::min(I, (long long)per_sm * sms));
     const long long ipc = (I + grid - 1) / grid;
     const long long spans = std::min<long long>(g.nc, (ipc + g.n_vt - 1) / g.n_vt + 1);
-    smem = (size_t)spans * kCB * (NP * 256 + M * 4);
+    smem = (size_t)spans * kCB * (NP * 256 + M * (q4 ? 8 : 4));
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -482,8 +665,11 @@ size_t q8_part_floats(const DevMat& w, int64_t n_rows, int M) {
 
 cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st) {
   Q8Geo g;
-  if (a.w.dtype != SX_DTYPE_Q8_0 || !a.part || a.M < 1 || a.M > kMaxPrefillTok || !make_geo(a, &g))
+  if ((a.w.dtype != SX_DTYPE_Q8_0 && a.w.dtype != kDtypeQ4KT) || !a.part || a.M < 1 || a.M > kMaxPrefillTok ||
+      !make_geo(a, &g))
     return cudaErrorInvalidValue;
+  // Q4_K records: whole super-blocks, no extra rows
+  if (a.w.dtype == kDtypeQ4KT && (g.nb % kCB || a.n_extra != 0)) return cudaErrorInvalidValue;
   // the SwiGLU pairing is per tile of the whole interleaved matrix
   if (epi == EPI_SWIGLU && (a.row_base != 0 || a.n_extra != 0)) return cudaErrorInvalidValue;
   int Mt = 1;

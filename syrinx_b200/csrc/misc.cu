@@ -246,6 +246,45 @@ __global__ void k_repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols,
   }
 }
 
+// GGML Q4_K super-blocks -> tile records (sx_internal.hpp, kQ4Rec): one thread per (row,
+// super-block). The 6-bit scale / min of sub-block j unpacked as ggml's get_scale_min_k4 does;
+// sub-block j's 32 nibbles are the low (even j) or high (odd j) halves of qs[32 (j / 2) ..].
+// Rows land at dr = (r / grp) * grp * row_mul + row_add * grp + r % grp (w1 / w3 interleave per
+// 16-row tile, as the Q8_0 records).
+__global__ void k_repack_q4k_tiles(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul,
+                                   int row_add, int grp) {
+  const int64_t nsb = cols / 256;
+  const int64_t total = rows * nsb;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / nsb, sb = i % nsb;
+    const uint8_t* src = blocks + i * 144;
+    const int64_t dr = (r / grp) * grp * row_mul + (int64_t)row_add * grp + r % grp;
+    const int rr = (int)(dr % kQ8Tile);
+    uint8_t* dst = rec + ((dr / kQ8Tile) * nsb + sb) * kQ4Rec;
+    const uint8_t* sc12 = src + 4;
+    const uint8_t* qs = src + 16;
+    for (int j = 0; j < 8; j++) {
+      uint32_t sc, mn;
+      if (j < 4) {
+        sc = sc12[j] & 63;
+        mn = sc12[j + 4] & 63;
+      } else {
+        sc = (sc12[j + 4] & 0xF) | ((sc12[j - 4] >> 6) << 4);
+        mn = (sc12[j + 4] >> 4) | ((sc12[j] >> 6) << 4);
+      }
+      dst[q4_sc_off(rr, j)] = (uint8_t)sc;
+      dst[q4_sc_off(rr, j) + 128] = (uint8_t)mn;
+      for (int k = 0; k < 16; k++) {
+        const uint8_t b0 = qs[(j >> 1) * 32 + k], b1 = qs[(j >> 1) * 32 + k + 16];
+        const uint8_t q0 = (j & 1) ? (b0 >> 4) : (b0 & 0xF), q1 = (j & 1) ? (b1 >> 4) : (b1 & 0xF);
+        dst[q4_quant_off(rr, j, k)] = (uint8_t)(q0 | (q1 << 4));
+      }
+    }
+    for (int b = 0; b < 4; b++) dst[q4_dd_off(rr) + b] = src[b];  // d, dmin (f16)
+  }
+}
+
 __global__ void k_dequant(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out) {
   const int64_t per = dtype == SX_DTYPE_Q8_0 ? 32 : 256;
   const int64_t total = n_blocks * per;
@@ -349,6 +388,14 @@ cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8
                         int row_mul, int row_add, cudaStream_t st) {
   (void)cudaGetLastError();  // report this launch's status, not an earlier one
   k_repack_q4_k<<<1184, 256, 0, st>>>(blocks, rows, cols, q, meta, row_mul, row_add);
+  return cudaGetLastError();
+}
+
+cudaError_t repack_q4k_tiles(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul,
+                             int row_add, int grp, cudaStream_t st) {
+  if (grp < 1 || cols % 256) return cudaErrorInvalidValue;
+  (void)cudaGetLastError();  // report this launch's status, not an earlier one
+  k_repack_q4k_tiles<<<1184, 256, 0, st>>>(blocks, rows, cols, rec, row_mul, row_add, grp);
   return cudaGetLastError();
 }
 

@@ -24,6 +24,7 @@ size_t DevMat::bytes() const {
   switch (dtype) {
     case SX_DTYPE_Q8_0: return (size_t)q8_tiles(rows) * (cols / 32) * kQ8Rec;
     case SX_DTYPE_Q4_K: return (size_t)rows * cols / 2 + (size_t)rows * (cols / 256) * 16;
+    case kDtypeQ4KT: return (size_t)q8_tiles(rows) * (cols / 256) * kQ4Rec;
     case SX_DTYPE_F32: return (size_t)rows * cols * 4;
   }
   return 0;
@@ -171,8 +172,9 @@ struct Loader {
 
   // Upload `name` [rows x cols] (or its shard `sl`) into dst at destination rows
   // r*row_mul + row_add; dst spans total_rows rows and is allocated on first use.
+  // A layer matrix (`tiled`) in Q4_K becomes tile records for the integer tensor-core GEMV.
   int mat(const std::string& name, int64_t rows, int64_t cols, DevMat* dst, int64_t total_rows,
-          int row_mul = 1, int row_add = 0, const Slice* sl = nullptr) {
+          int row_mul = 1, int row_add = 0, const Slice* sl = nullptr, bool tiled = false) {
     const BlobTensor* full = get(name, rows, cols);
     if (!full) return SX_E_BLOB;
     BlobTensor view = *full;
@@ -185,11 +187,12 @@ struct Loader {
       set_error("weight blob: " + name + " has an unsupported dtype (Q8_0, Q4_K or F32)");
       return SX_E_UNSUPPORTED;
     }
+    const int dtype = (tiled && t->dtype == SX_DTYPE_Q4_K) ? kDtypeQ4KT : t->dtype;
     if (dst->dtype < 0) {
-      dst->dtype = t->dtype;
+      dst->dtype = dtype;
       dst->rows = total_rows;
       dst->cols = cols;
-      if (t->dtype == SX_DTYPE_Q8_0) {
+      if (dtype == SX_DTYPE_Q8_0 || dtype == kDtypeQ4KT) {
         uint8_t* q;
         SX_RC(dalloc(m->allocs, &q, dst->bytes()));
         SX_CU(cudaMemset(q, 0, dst->bytes()));  // rows past N of the last tile stay zero
@@ -205,7 +208,7 @@ struct Loader {
         dst->q = q;
       }
       m->weight_bytes += dst->bytes();
-    } else if (dst->dtype != t->dtype) {
+    } else if (dst->dtype != dtype) {
       set_error("weight blob: " + name + " dtype differs from its fused partner");
       return SX_E_BLOB;
     }
@@ -224,6 +227,8 @@ struct Loader {
     // Q8_0 interleaves w1/w3 per 16-row tile (8 gate rows, then their 8 up rows)
     if (t->dtype == SX_DTYPE_Q8_0)
       SX_CU(repack_q8_0(staging, rows, cols, (uint8_t*)dst->q, row_mul, row_add, row_mul == 2 ? 8 : 1, 0));
+    else if (dtype == kDtypeQ4KT)
+      SX_CU(repack_q4k_tiles(staging, rows, cols, (uint8_t*)dst->q, row_mul, row_add, row_mul == 2 ? 8 : 1, 0));
     else
       SX_CU(repack_q4_k(staging, rows, cols, (uint8_t*)dst->q, dst->meta, row_mul, row_add, 0));
     SX_CU(cudaStreamSynchronize(0));
@@ -254,7 +259,7 @@ struct Loader {
       const std::string p = std::string(prefix) + "." + std::to_string(l) + ".";
       DevLayer L;
       SX_RC(vec(p + "attention_norm.weight", td.dim, &L.attn_norm));
-      SX_RC(mat(p + "attention.wqkv.weight", qkv, td.dim, &L.wqkv, qkv_l, 1, 0, sh ? &s_qkv : nullptr));
+      SX_RC(mat(p + "attention.wqkv.weight", qkv, td.dim, &L.wqkv, qkv_l, 1, 0, sh ? &s_qkv : nullptr, true));
       if (td.qkv_bias) {
         if (sh)
           SX_RC(vec_slice(p + "attention.wqkv.bias", qkv, s_qkv, &L.bqkv));
@@ -265,12 +270,12 @@ struct Loader {
         SX_RC(vec(p + "attention.q_norm.weight", td.head_dim, &L.qn));
         SX_RC(vec(p + "attention.k_norm.weight", td.head_dim, &L.kn));
       }
-      SX_RC(mat(p + "attention.wo.weight", td.dim, H * hd, &L.wo, td.dim, 1, 0, sh ? &s_wo : nullptr));
+      SX_RC(mat(p + "attention.wo.weight", td.dim, H * hd, &L.wo, td.dim, 1, 0, sh ? &s_wo : nullptr, true));
       if (td.o_bias) SX_RC(vec(p + "attention.wo.bias", td.dim, &L.bo));
       SX_RC(vec(p + "ffn_norm.weight", td.dim, &L.ffn_norm));
-      SX_RC(mat(p + "feed_forward.w1.weight", F, td.dim, &L.w13, 2 * Fl, 2, 0, sh ? &s_f : nullptr));
-      SX_RC(mat(p + "feed_forward.w3.weight", F, td.dim, &L.w13, 2 * Fl, 2, 1, sh ? &s_f : nullptr));
-      SX_RC(mat(p + "feed_forward.w2.weight", td.dim, F, &L.w2, td.dim, 1, 0, sh ? &s_w2 : nullptr));
+      SX_RC(mat(p + "feed_forward.w1.weight", F, td.dim, &L.w13, 2 * Fl, 2, 0, sh ? &s_f : nullptr, true));
+      SX_RC(mat(p + "feed_forward.w3.weight", F, td.dim, &L.w13, 2 * Fl, 2, 1, sh ? &s_f : nullptr, true));
+      SX_RC(mat(p + "feed_forward.w2.weight", td.dim, F, &L.w2, td.dim, 1, 0, sh ? &s_w2 : nullptr, true));
       out->push_back(L);
     }
     return SX_OK;
@@ -522,7 +527,7 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
     // chunk for the layer matrices, a decode batch for the heads
     size_t cap = 0;
     auto need = [&](const DevMat& w, int M) {
-      if (w.dtype == SX_DTYPE_Q8_0) cap = std::max(cap, q8_part_floats(w, w.rows, M));
+      if (w.dtype == SX_DTYPE_Q8_0 || w.dtype == kDtypeQ4KT) cap = std::max(cap, q8_part_floats(w, w.rows, M));
     };
     for (const auto* ls : {&m->slow, &m->fast})
       for (const DevLayer& L : *ls) {

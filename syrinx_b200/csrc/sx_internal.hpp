@@ -56,6 +56,26 @@ struct DevMat {
   size_t bytes() const;
 };
 
+// Q4_K layer matrices as tile records for the integer tensor-core GEMV (the loader's internal
+// dtype; emb / head tables keep the row layout). One record = 16 rows x one 256-wide
+// super-block, kQ4Rec bytes:
+//   [0, 2048)     quants: 4 pairs of 32-wide sub-blocks x 512 B; lane L = 4g + c owns 16 bytes
+//                 of each pair: for sub-block 2jp + h, bytes 8h..8h+3 hold row g and 8h+4..8h+7
+//                 row g + 8, byte i = q[k = 4c + i] | q[k = 16 + 4c + i] << 4 (nibbles 0..15),
+//                 so `& 0x0F0F0F0F` and `>> 4 & ...` give the mma.m16n8k32 A fragment words;
+//   [2048, 2176)  6-bit sub-block scales: per g, 8 bytes of row g then 8 bytes of row g + 8;
+//   [2176, 2304)  6-bit sub-block mins, the same order;
+//   [2304, 2368)  per g: f16 d and dmin of row g, then of row g + 8.
+// 2368 bytes per 4096 weights (GGML: 2304).
+constexpr int kDtypeQ4KT = 64;
+constexpr int kQ4Rec = 2368;
+__host__ __device__ inline int q4_quant_off(int rr, int j, int k) {  // byte of (tile row, sub-block, k); nibble k >> 4
+  const int g = rr & 7, c = (k & 15) >> 2;
+  return (j >> 1) * 512 + (4 * g + c) * 16 + (j & 1) * 8 + (rr >> 3) * 4 + (k & 3);
+}
+__host__ __device__ inline int q4_sc_off(int rr, int j) { return 2048 + (rr & 7) * 16 + (rr >> 3) * 8 + j; }
+__host__ __device__ inline int q4_dd_off(int rr) { return 2304 + (rr & 7) * 8 + (rr >> 3) * 4; }
+
 // Q8_0 tile-record geometry (see the layout above).
 constexpr int kQ8Tile = 16;
 constexpr int kQ8Rec = 544;
@@ -287,6 +307,8 @@ cudaError_t launch_advance(const AdvanceArgs& a, cudaStream_t st);
 // it is (r / grp) * grp * row_mul + row_add * grp + r % grp (grp 8: the per-tile interleave)
 cudaError_t repack_q8_0(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul, int row_add,
                         int grp, cudaStream_t st);
+cudaError_t repack_q4k_tiles(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* rec, int row_mul,
+                             int row_add, int grp, cudaStream_t st);
 cudaError_t repack_q4_k(const uint8_t* blocks, int64_t rows, int64_t cols, uint8_t* q, uint8_t* meta,
                         int row_mul, int row_add, cudaStream_t st);
 cudaError_t dequant_blocks(int dtype, const uint8_t* blocks, int64_t n_blocks, float* out,
