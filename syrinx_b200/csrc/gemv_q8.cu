@@ -238,7 +238,7 @@ __device__ __forceinline__ void load_item_q4(const uint8_t* W, const Q8Geo& g, i
 }
 
 template <int M>
-__global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q4k(const GemvArgs a, const Q8Geo g) {
+__global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const GemvArgs a, const Q8Geo g) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int NP = (M + 1) / 2;
   __shared__ __align__(16) int8_t scr[kWarps][4][32];
@@ -260,8 +260,13 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q4k(const Gem
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
 
   pdl_launch_dependents();
-  ItemQ4 it;
-  if (left > 0) load_item_q4(W, g, g.t_first + vt, kc, lane, it);
+  // two items in registers: the next one loads while this one is multiplied
+  ItemQ4 it0, it1;
+  if (left > 0) load_item_q4(W, g, g.t_first + vt, kc, lane, it0);
+  if (left > 1) {
+    const int vt1 = vt + 1 == g.n_vt ? 0 : vt + 1, kc1 = vt + 1 == g.n_vt ? kc + 1 : kc;
+    load_item_q4(W, g, g.t_first + vt1, kc1, lane, it1);
+  }
   pdl_wait();
 
   if (a.norm_w) {  // RMSNorm denominators, as k_gemv_q8
@@ -337,7 +342,8 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q4k(const Gem
 
   const int bl = M == 1 ? (lane & 15) : lane;
   const float mmul = (lane & 1) ? 0.f : -128.f;  // the min term rides on the limb-(0, 1) lanes
-  while (left > 0) {
+  // one item: multiply, then load the item after the next one into its registers
+  auto run = [&](ItemQ4& it) {
     float acc[NP][2];
 #pragma unroll
     for (int p = 0; p < NP; p++) acc[p][0] = acc[p][1] = 0.f;
@@ -379,7 +385,10 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q4k(const Gem
       kc++;
     }
     left--;
-    if (left > 0) load_item_q4(W, g, g.t_first + vt, kc, lane, it);
+    if (left > 1) {  // the item after the next one, into this buffer
+      const int vt2 = vt + 1 == g.n_vt ? 0 : vt + 1, kc2 = vt + 1 == g.n_vt ? kc + 1 : kc;
+      load_item_q4(W, g, g.t_first + vt2, kc2, lane, it);
+    }
     const float wgt = (lane & 1) ? 0x1p-21f : 0x1p-7f;
     float* P = a.part + ((size_t)done_vt * g.nc + done_kc) * M * 16;
 #pragma unroll
@@ -393,6 +402,10 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q4k(const Gem
         __stcg(P + tok * 16 + (lane >> 2) + 8, v1);
       }
     }
+  };
+  while (left > 0) {
+    run(it0);
+    if (left > 0) run(it1);
   }
 }
 
