@@ -40,6 +40,9 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kCB = 8;  // 32-wide k blocks per item
+// (block, token) units per warp whose x loads go out together: a warp has at most 2M units
+// (a CTA spans at most 16 blocks), so small batches cover all of them in one round trip
+__host__ __device__ constexpr int limb_batch(int M) { return M == 1 ? 2 : M == 2 ? 4 : M <= 8 ? 8 : 4; }
 
 struct Q8Geo {
   int K, nb, nc;      // columns, 32-wide blocks, k-chunks of kCB blocks
@@ -102,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
     float ss[M];
 #pragma unroll
     for (int m = 0; m < M; m++) ss[m] = 0.f;
+#pragma unroll(M <= 8 ? 4 : 1)
     for (int k = threadIdx.x; k < g.K; k += kThreads)
 #pragma unroll
       for (int m = 0; m < M; m++) {
@@ -124,12 +128,27 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   }
 
   // ---- x limbs of this CTA's blocks: one warp per (block, token) ----
-  for (int u = warp; u < (b_hi - b_lo) * M; u += kWarps) {
-    const int bi = u / M, m = u % M, k = (b_lo + bi) * 32 + lane;
+  // batches of up to 8 units per warp: every load of a batch goes out before the first is
+  // used, so the split costs one round trip to L2 per batch instead of one per unit
+  const int n_units = (b_hi - b_lo) * M;
+  for (int u0 = warp; u0 < n_units; u0 += limb_batch(M) * kWarps) {
+    float xv[limb_batch(M)], gv[limb_batch(M)];
+#pragma unroll
+    for (int j = 0; j < limb_batch(M); j++) {
+      const int u = u0 + j * kWarps, m = u % M, k = (b_lo + u / M) * 32 + lane;
+      const bool ok = u < n_units && m < a.M;
+      xv[j] = ok ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
+      gv[j] = (ok && a.norm_w) ? a.norm_w[k] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < limb_batch(M); j++) {
+    const int u = u0 + j * kWarps;
+    if (u >= n_units) break;
+    const int bi = u / M, m = u % M;
     float v = 0.f;
     if (m < a.M) {
-      v = ld_cg(a.x + (size_t)m * g.K + k);
-      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), a.norm_w[k]);
+      v = xv[j];
+      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), gv[j]);
     }
     const float mx = warp_max(fabsf(v));
     const int e = (__float_as_int(mx) >> 23) & 0xff;
@@ -162,6 +181,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
     }
     if (lane == 0) sxs[bi * M + m] = sx;
     __syncwarp();
+    }
   }
   __syncthreads();
 
@@ -273,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
     float ss[M];
 #pragma unroll
     for (int m = 0; m < M; m++) ss[m] = 0.f;
+#pragma unroll(M <= 8 ? 4 : 1)
     for (int k = threadIdx.x; k < g.K; k += kThreads)
 #pragma unroll
       for (int m = 0; m < M; m++) {
@@ -295,12 +316,27 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
   }
 
   // x limbs (as k_gemv_q8) and the block sums of x, one warp per (block, token)
-  for (int u = warp; u < (b_hi - b_lo) * M; u += kWarps) {
-    const int bi = u / M, m = u % M, k = (b_lo + bi) * 32 + lane;
+  // batches of up to 8 units per warp: every load of a batch goes out before the first is
+  // used, so the split costs one round trip to L2 per batch instead of one per unit
+  const int n_units = (b_hi - b_lo) * M;
+  for (int u0 = warp; u0 < n_units; u0 += limb_batch(M) * kWarps) {
+    float xv[limb_batch(M)], gv[limb_batch(M)];
+#pragma unroll
+    for (int j = 0; j < limb_batch(M); j++) {
+      const int u = u0 + j * kWarps, m = u % M, k = (b_lo + u / M) * 32 + lane;
+      const bool ok = u < n_units && m < a.M;
+      xv[j] = ok ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
+      gv[j] = (ok && a.norm_w) ? a.norm_w[k] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < limb_batch(M); j++) {
+    const int u = u0 + j * kWarps;
+    if (u >= n_units) break;
+    const int bi = u / M, m = u % M;
     float v = 0.f;
     if (m < a.M) {
-      v = ld_cg(a.x + (size_t)m * g.K + k);
-      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), a.norm_w[k]);
+      v = xv[j];
+      if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), gv[j]);
     }
     const float bsum = warp_sum(v);
     const float mx = warp_max(fabsf(v));
@@ -337,6 +373,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
       xsum[bi * M + m] = bsum;
     }
     __syncwarp();
+    }
   }
   __syncthreads();
 
