@@ -101,7 +101,8 @@ const char* sx_version(void);
 /* ---- weight blobs -------------------------------------------------------------------- *
  * A blob ("SXW1") is a named-tensor container in the reference's weight naming
  * (s2/load.rs:150-310: layers.{l}.attention.wqkv.weight with rows q|k|v, ...). Quantized
- * tensors hold GGML blocks along the last (input) dimension. Layout, little-endian:
+ * tensors hold GGML blocks along the last (input) dimension; ndim is 1 or 2, or 3 for f32
+ * convolution kernels (the codec's [out, in, K] / [in, out, K]). Layout, little-endian:
  *   char magic[4]="SXW1"; u32 version=1; u32 n_tensors; u32 reserved; u64 data_offset;
  *   n_tensors x { u32 name_len; char name[name_len]; u32 dtype; u32 ndim; u64 shape[ndim];
  *                 u64 offset (from data_offset); u64 nbytes }

@@ -8,7 +8,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 
-from .configs import SxModelDesc, SxSamplingParams
+from .configs import SxCodecInfo, SxModelDesc, SxSamplingParams
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libsyrinx_b200.so")
 
@@ -60,6 +60,14 @@ SIGNATURES = {
     "sx_lm_step_embeds": (C.c_int, [C.c_void_p, _f32p, C.c_int32, _f32p]),
     "sx_dequantize": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, _f32p, C.c_int32]),
     "sx_dequantize_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, _f32p, C.c_int32]),
+    # include/syrinx_codec.h
+    "sx_codec_create": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int32, C.POINTER(C.c_void_p)]),
+    "sx_codec_destroy": (C.c_int, [C.c_void_p]),
+    "sx_codec_get_info": (C.c_int, [C.c_void_p, C.POINTER(SxCodecInfo)]),
+    "sx_codec_reserve": (C.c_int, [C.c_void_p, C.c_int32]),
+    "sx_codec_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "sx_codec_decode": (C.c_int, [C.c_void_p, _u32p, C.c_int32, C.c_int32, _f32p, C.c_size_t]),
+    "sx_codec_decode_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
 }
 
 _LIB = None

@@ -13,7 +13,7 @@ _BLOCK = {SX_DTYPE_Q8_0: (32, 34), SX_DTYPE_Q4_K: (256, 144)}
 
 
 def write_blob(tensors: dict) -> np.ndarray:
-    """tensors: name -> f32 ndarray (1-D or 2-D), or (dtype, shape, raw uint8 blocks)."""
+    """tensors: name -> f32 ndarray (1-D to 3-D), or (dtype, shape, raw uint8 blocks)."""
     entries = []
     for name, v in tensors.items():
         if isinstance(v, tuple):

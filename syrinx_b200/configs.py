@@ -65,6 +65,20 @@ class SxSamplingParams(C.Structure):
     ]
 
 
+class SxCodecInfo(C.Structure):
+    """sx_codec_info of include/syrinx_codec.h."""
+    _fields_ = [
+        ("hop", C.c_int32),
+        ("sample_rate", C.c_int32),
+        ("num_codebooks", C.c_int32),
+        ("semantic_size", C.c_int32),
+        ("residual_size", C.c_int32),
+        ("codebook_dim", C.c_int32),
+        ("latent_dim", C.c_int32),
+        ("n_layers", C.c_int32),
+    ]
+
+
 @dataclasses.dataclass(frozen=True)
 class Stack:
     dim: int

@@ -190,20 +190,26 @@ int parse_blob(const void* blob, size_t size, BlobIndex* out, std::string* err) 
       std::memcpy(&dtype, b + off, 4);
       std::memcpy(&ndim, b + off + 4, 4);
       off += 8;
-      if (ndim < 1 || ndim > 2 || off + 8 * ndim + 16 > size) {
+      if (ndim < 1 || ndim > 3 || off + 8 * ndim + 16 > size) {
         *err = "weight blob: bad rank for " + t.name;
         return SX_E_BLOB;
       }
-      uint64_t shape[2] = {1, 1};
+      uint64_t shape[3] = {1, 1, 1};
       for (uint32_t d = 0; d < ndim; d++) std::memcpy(&shape[d], b + off + 8 * d, 8);
       off += 8 * ndim;
+      if (ndim == 3 && (dtype != SX_DTYPE_F32 || shape[1] > (1ull << 31) || shape[2] > (1ull << 31))) {
+        *err = "weight blob: rank-3 tensors must be f32: " + t.name;
+        return SX_E_BLOB;
+      }
       uint64_t toff, nbytes;
       std::memcpy(&toff, b + off, 8);
       std::memcpy(&nbytes, b + off + 8, 8);
       off += 16;
       t.dtype = (int)dtype;
+      t.ndim = (int)ndim;
+      for (uint32_t d = 0; d < ndim; d++) t.shape[d] = (int64_t)shape[d];
       t.rows = ndim == 1 ? 1 : (int64_t)shape[0];
-      t.cols = ndim == 1 ? (int64_t)shape[0] : (int64_t)shape[1];
+      t.cols = ndim == 1 ? (int64_t)shape[0] : (int64_t)(shape[1] * shape[2]);
       const size_t rb = row_bytes(t.dtype, t.cols);
       if (rb == 0) {
         *err = "weight blob: unsupported dtype / block alignment for " + t.name;

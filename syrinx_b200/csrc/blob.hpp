@@ -14,7 +14,9 @@ namespace sx {
 struct BlobTensor {
   std::string name;
   int dtype = -1;
-  int64_t rows = 0, cols = 0;
+  int64_t rows = 0, cols = 0;  // a rank-3 tensor [d0, d1, d2] is held as rows d0, cols d1*d2
+  int ndim = 0;
+  int64_t shape[3] = {1, 1, 1};
   const uint8_t* data = nullptr;
   size_t nbytes = 0;
 };

@@ -8,11 +8,13 @@
 
 #include <algorithm>
 #include <cstring>
+#include <memory>
 #include <new>
 #include <string>
 #include <vector>
 
 #include "blob.hpp"
+#include "codec.hpp"
 #include "model.hpp"
 #include "sampling.hpp"
 
@@ -674,6 +676,162 @@ int sx_dequantize(int32_t dtype, const void* blocks, int64_t n_blocks, float* ou
 
 int sx_dequantize_noalloc(int32_t dtype, const void* blocks, int64_t n_blocks, float* out, int32_t device) {
   SX_GUARD({ return dequantize_noalloc(dtype, blocks, n_blocks, out, device); })
+}
+
+// ---- codec decode (include/syrinx_codec.h) --------------------------------------------
+
+int sx_codec_create(const void* blob, size_t blob_size, int32_t device, sx_codec** out) {
+  SX_GUARD({
+    if (!blob || !out) {
+      set_error("null argument");
+      return SX_E_INVALID;
+    }
+    *out = nullptr;
+    std::unique_ptr<sx_codec> c(new sx_codec());
+    std::string err;
+    const int rc = c->load(blob, blob_size, device, &err);
+    if (rc) {
+      set_error(err);
+      return rc;
+    }
+    *out = c.release();
+    return SX_OK;
+  })
+}
+
+int sx_codec_destroy(sx_codec* codec) {
+  SX_GUARD({
+    delete codec;
+    return SX_OK;
+  })
+}
+
+int sx_codec_get_info(const sx_codec* codec, sx_codec_info* out) {
+  if (!codec || !out) {
+    set_error("null argument");
+    return SX_E_INVALID;
+  }
+  out->hop = codec->hop;
+  out->sample_rate = 44100;
+  out->num_codebooks = 1 + codec->n_res;
+  out->semantic_size = codec->sem_size;
+  out->residual_size = codec->res_size;
+  out->codebook_dim = codec->cb_dim;
+  out->latent_dim = codec->latent;
+  out->n_layers = codec->n_layers;
+  return SX_OK;
+}
+
+static int codec_device(const sx_codec* c) {
+  if (cudaSetDevice(c->device) != cudaSuccess) {
+    set_error("cudaSetDevice failed");
+    return SX_E_CUDA;
+  }
+  return SX_OK;
+}
+
+static int codec_check_shape(const sx_codec* c, int32_t n_codebooks, int32_t n_frames) {
+  if (n_codebooks < 1 || n_codebooks > 1 + c->n_res || n_frames < 0) {
+    set_error("codec decode: n_codebooks must be 1.." + std::to_string(1 + c->n_res) +
+              " and n_frames >= 0");
+    return SX_E_INVALID;
+  }
+  return SX_OK;
+}
+
+int sx_codec_reserve(sx_codec* codec, int32_t max_frames) {
+  SX_GUARD({
+    if (!codec || max_frames < 0) {
+      set_error("bad argument");
+      return SX_E_INVALID;
+    }
+    int rc = codec_device(codec);
+    if (rc) return rc;
+    std::string err;
+    rc = codec->reserve(max_frames, &err);
+    if (rc) set_error(err);
+    return rc;
+  })
+}
+
+int sx_codec_set_stream(sx_codec* codec, void* cuda_stream) {
+  if (!codec) {
+    set_error("null codec");
+    return SX_E_INVALID;
+  }
+  codec->stream = static_cast<cudaStream_t>(cuda_stream);
+  return SX_OK;
+}
+
+int sx_codec_decode(sx_codec* codec, const uint32_t* codes, int32_t n_codebooks, int32_t n_frames,
+                    float* wav_out, size_t wav_capacity) {
+  SX_GUARD({
+    if (!codec || !codes || !wav_out) {
+      set_error("null argument");
+      return SX_E_INVALID;
+    }
+    int rc = codec_check_shape(codec, n_codebooks, n_frames);
+    if (rc) return rc;
+    const size_t n_wav = (size_t)n_frames * (size_t)codec->hop;
+    if (wav_capacity < n_wav) {
+      set_error("codec decode: wav_out holds " + std::to_string(wav_capacity) + " samples, " +
+                std::to_string(n_wav) + " needed");
+      return SX_E_RANGE;
+    }
+    if (n_frames == 0) return SX_OK;
+    rc = codec_device(codec);
+    if (rc) return rc;
+    if ((size_t)n_frames > codec->io_frames) {
+      cudaFree(codec->codes_dev);
+      cudaFree(codec->wav_dev);
+      codec->codes_dev = nullptr, codec->wav_dev = nullptr, codec->io_frames = 0;
+      const size_t ncb_max = (size_t)(1 + codec->n_res);
+      if (cudaMalloc((void**)&codec->codes_dev, ncb_max * n_frames * sizeof(uint32_t)) != cudaSuccess ||
+          cudaMalloc((void**)&codec->wav_dev, n_wav * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("codec decode: device allocation failed");
+        return SX_E_OOM;
+      }
+      codec->io_frames = (size_t)n_frames;
+    }
+    cudaStream_t st = codec->stream;
+    if (cudaMemcpyAsync(codec->codes_dev, codes, (size_t)n_codebooks * n_frames * sizeof(uint32_t),
+                        cudaMemcpyHostToDevice, st) != cudaSuccess) {
+      set_error("codec decode: codes upload failed");
+      return SX_E_CUDA;
+    }
+    std::string err;
+    rc = codec->decode_device(codec->codes_dev, n_codebooks, n_frames, codec->wav_dev, &err);
+    if (rc) {
+      set_error(err);
+      return rc;
+    }
+    if (cudaMemcpyAsync(wav_out, codec->wav_dev, n_wav * sizeof(float), cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+      set_error(std::string("codec decode: ") + cudaGetErrorString(cudaGetLastError()));
+      return SX_E_CUDA;
+    }
+    return SX_OK;
+  })
+}
+
+int sx_codec_decode_device(sx_codec* codec, const uint32_t* codes_dev, int32_t n_codebooks,
+                           int32_t n_frames, float* wav_dev) {
+  SX_GUARD({
+    if (!codec || !codes_dev || !wav_dev) {
+      set_error("null argument");
+      return SX_E_INVALID;
+    }
+    int rc = codec_check_shape(codec, n_codebooks, n_frames);
+    if (rc) return rc;
+    rc = codec_device(codec);
+    if (rc) return rc;
+    std::string err;
+    rc = codec->decode_device(codes_dev, n_codebooks, n_frames, wav_dev, &err);
+    if (rc) set_error(err);
+    return rc;
+  })
 }
 
 }  // extern "C"
