@@ -275,6 +275,8 @@ def bench_device(args):
     model.close()
     if not args.no_b8:
         res["b8"] = bench_b8(args, local, stream, dist, world, peak, peak_kind)
+    if not args.no_codec:
+        res["codec"] = bench_codec(args, local, stream, dist, world, rank)
     if rank == 0 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
     if dist:
@@ -334,6 +336,77 @@ def bench_b8(args, local, stream, dist, world, peak, peak_kind):
                 (w_bytes + kv_f32) * steps_per_s / (peak * 1e9), 4), "bytes_per_step_kv_bf16": w_bytes + kv_bf16,
                 "frac_of_peak_kv_bf16": round((w_bytes + kv_bf16) * steps_per_s / (peak * 1e9), 4),
                 "peak_gbs": peak, "peak_kind": peak_kind}}
+
+
+CODEC_FRAMES = 256  # 11.9 s of 44.1 kHz audio per decode
+
+
+def bench_codec(args, local, stream, dist, world, rank):
+    """Row f2 on each GPU: the s2 causal-DAC codec decode (codes [10, 256] -> 524,288
+    samples) with seeded synthetic weights of the s2 shape. Device time over K decodes with
+    inputs resident; e2e through sx_codec_decode (host codes in, host waveform out). The
+    weights (0.74 GB) and activations exceed L2, so no flush is needed between decodes."""
+    import torch
+    from syrinx_b200 import dp
+    from syrinx_b200.codec import S2_CODEC, RvqCodec, decode_flops, synth_codec_weights, synth_codes
+
+    T = CODEC_FRAMES
+    K, W = min(args.steps, 8), 3
+    weights = synth_codec_weights(S2_CODEC, seed=SEED)
+    codec = RvqCodec(weights, device=local)
+    codec.reserve(T)
+    codes = synth_codes(S2_CODEC, T, seed=SEED)
+    dcodes = torch.from_numpy(codes.astype(np.int32)).cuda()
+    wav = torch.empty(T * codec.hop, dtype=torch.float32, device="cuda")
+    codec.set_stream(stream.cuda_stream)
+    for _ in range(W):
+        codec.decode_device(dcodes.data_ptr(), codes.shape[0], T, wav.data_ptr())
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s1.record(stream)
+    for _ in range(K):
+        codec.decode_device(dcodes.data_ptr(), codes.shape[0], T, wav.data_ptr())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = dp.max_over_ranks(s1.elapsed_time(e1), dist, device="cuda") / K
+    host_wav = codec.decode(codes)  # e2e warm-up
+    t0 = time.perf_counter()
+    for _ in range(K):
+        host_wav = codec.decode(codes)
+    ms_e2e = dp.max_over_ranks((time.perf_counter() - t0) * 1e3, dist, device="cuda") / K
+    assert host_wav.shape == (T * codec.hop,) and np.isfinite(host_wav).all()
+    assert np.array_equal(host_wav, wav.cpu().numpy())
+    flops = decode_flops(S2_CODEC, T)
+    tflops = flops / (ms * 1e-3) / 1e12
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # FP32 lanes x 2 x clocks.max.sm, nominal
+    out = {"value": round(T * world / (ms * 1e-3), 1), "unit": "codec frames/s",
+           "audio_s_per_s": round(T * codec.hop / 44100 * world / (ms * 1e-3), 1),
+           "ms_per_decode": round(ms, 3), "steps": K, "warmup": W,
+           "workload": f"s2 codec decode, {T} frames x 10 codebooks -> {T * codec.hop} samples, "
+                       "synthetic weights of the s2 shape (seed %d)" % SEED,
+           "dtype": "f32",
+           "roofline": {"bound": "fp32", "achieved": round(tflops, 2), "unit": "TFLOP/s",
+                        "flops_per_decode": flops, "peak": round(fp32_peak, 1),
+                        "frac": round(tflops / fp32_peak, 4),
+                        "peak_source": "nominal FP32 CUDA-core rate at clocks.max.sm (148 SMs x 128 lanes "
+                                       "x 2 x 1965 MHz); not in MEASURED_PEAKS.json"},
+           "e2e": {"value": round(T * world / (ms_e2e * 1e-3), 1), "unit": "codec frames/s",
+                   "h2d_bytes_per_step": int(codes.size * 4), "d2h_bytes_per_step": int(T * codec.hop * 4),
+                   "api": "sx_codec_decode (host codes in, host waveform out)"}}
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle import codec_oracle
+        n = 8
+        t0 = time.perf_counter()
+        codec_oracle.decode(weights, codes[:, :n])
+        secs = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": round(n / secs, 3), "unit": "codec frames/s",
+                               "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"the first {n} frames of the same codes on the float64 numpy "
+                                         f"oracle ({secs:.1f} s)"}
+    codec.close()
+    return out
 
 
 TP_METRIC = "semantic frames/s per tensor-parallel group, config 5 (4B-shape Q8_0 dual-AR b1, KV grown to 8192)"
@@ -514,6 +587,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-b8", action="store_true", help="skip the config-4 batch-8 Q4_K measurement")
+    ap.add_argument("--no-codec", action="store_true", help="skip the codec decode measurement")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--tp", type=int, default=0, help="config 5: tensor-parallel group of N GPUs")
     ap.add_argument("--tp-ctx", type=int, default=8192)

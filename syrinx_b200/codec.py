@@ -62,7 +62,7 @@ def synth_codec_weights(shape: CodecShape = S2_CODEC, seed: int = 0) -> dict:
     w = {}
 
     def normal(shp, std):
-        return (rng.standard_normal(shp) * std).astype(np.float32)
+        return rng.standard_normal(shp, dtype=np.float32) * np.float32(std)
 
     def unif(shp, lo, hi):
         return rng.uniform(lo, hi, shp).astype(np.float32)
@@ -175,7 +175,6 @@ class RvqCodec:
 
     def __init__(self, weights, device: int = 0):
         blob = weights if isinstance(weights, np.ndarray) and weights.dtype == np.uint8 else write_blob(weights)
-        self._blob = blob
         L = _lib.lib()
         h = C.c_void_p()
         _lib.check(L.sx_codec_create(blob.ctypes.data, blob.nbytes, device, C.byref(h)))

@@ -7,6 +7,7 @@ Qwen3-4B-shaped model with fewer layers, so an `ncu --set full` capture stays sm
   python -m syrinx_b200.profile --what stack --layers 36 --prompt 512   (phase timing, printed)
   python -m syrinx_b200.profile --what prefill --layers 36 --prompt 512  (prefill time, printed)
   python -m syrinx_b200.profile --what batch --layers 8 --q4k --frames 4   (8 utterances batched)
+  python -m syrinx_b200.profile --what codec --frames 32 --launches 2   (s2 codec decodes, timed)
 """
 from __future__ import annotations
 
@@ -18,9 +19,28 @@ from .configs import SX_DTYPE_Q4_K, SX_DTYPE_Q8_0
 from .workloads import dual_ar_prompt
 
 
+def codec_run(frames: int, n: int):
+    """`n` decodes of `frames` frames through the s2-shaped codec, each timed on the host
+    after a synchronisation (the first one includes nothing but the decode)."""
+    import numpy as np
+
+    from .codec import S2_CODEC, RvqCodec, synth_codec_weights, synth_codes
+
+    codec = RvqCodec(synth_codec_weights(S2_CODEC, seed=2))
+    codes = synth_codes(S2_CODEC, frames, seed=2)
+    codec.reserve(frames)
+    for i in range(n):
+        t0 = time.perf_counter()
+        wav = codec.decode(codes)
+        print(f"decode {i}: {frames} frames in {1e3 * (time.perf_counter() - t0):.2f} ms")
+    assert np.isfinite(wav).all()
+    codec.close()
+    print("profile run ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill", "batch"], default="gemv")
+    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill", "batch", "codec"], default="gemv")
     ap.add_argument("--kind", type=int, default=2, help="0 wqkv, 1 wo, 2 w1|w3, 3 w2")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--launches", type=int, default=16)
@@ -28,6 +48,9 @@ def main():
     ap.add_argument("--q4k", action="store_true")
     ap.add_argument("--prompt", type=int, default=8, help="prompt positions prefilled before the run")
     args = ap.parse_args()
+    if args.what == "codec":
+        codec_run(args.frames, args.launches)
+        return
     cfg = shrink(QWEN3_4B, args.layers, min(4, args.layers))
     wtype = SX_DTYPE_Q4_K if args.q4k else SX_DTYPE_Q8_0
     model = Model(cfg, synth_blob(cfg, wtype, seed=2))
