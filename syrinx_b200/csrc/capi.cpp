@@ -806,11 +806,18 @@ int sx_codec_decode(sx_codec* codec, const uint32_t* codes, int32_t n_codebooks,
       set_error(err);
       return rc;
     }
+    int flag = 0;
     if (cudaMemcpyAsync(wav_out, codec->wav_dev, n_wav * sizeof(float), cudaMemcpyDeviceToHost, st) !=
             cudaSuccess ||
+        cudaMemcpyAsync(&flag, codec->err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         cudaStreamSynchronize(st) != cudaSuccess) {
       set_error(std::string("codec decode: ") + cudaGetErrorString(cudaGetLastError()));
       return SX_E_CUDA;
+    }
+    if (flag != 0) {
+      cudaMemset(codec->err, 0, sizeof(int));
+      set_error("codec decode: a tensor-core pipeline wait timed out");
+      return SX_E_DEVICE;
     }
     return SX_OK;
   })

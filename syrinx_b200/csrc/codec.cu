@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -520,22 +521,35 @@ struct Loader {
     image.resize(off + ((n + 15) & ~size_t(15)), 0.f);
     return off;
   }
-  void copy(float** dst, const BlobTensor* t) {
-    if (!t) return;
+  size_t copy(float** dst, const BlobTensor* t) {
+    if (!t) return 0;
     const size_t n = (size_t)(t->rows * t->cols);
     const size_t off = reserve_floats(n);
     std::memcpy(&image[off], t->data, n * sizeof(float));
     fix.push_back({dst, off});
+    return off;
+  }
+  // The tensor-core weight images of the packed matrix at image offset `off` (codec_tc.cu).
+  void tc_pack(Conv* c, size_t off) {
+    const int M = c->cout * c->stride, R = c->cin * c->taps;
+    std::vector<float> a(image.begin() + off, image.begin() + off + (size_t)M * R);
+    const size_t bytes = tc_image_bytes(M, R);
+    const size_t o = reserve_floats(bytes / sizeof(float));
+    tc_image(a.data(), M, R, reinterpret_cast<uint32_t*>(&image[o]));
+    fix.push_back({&c->tc, o});
   }
   void vec(float** dst, const std::string& n, int64_t elems) { copy(dst, need(n, elems)); }
   // Stacks two [rows][cols] matrices into one [2 rows][cols].
-  void stack2(float** dst, const BlobTensor* a, const BlobTensor* b) {
+  // Two [rows][cols] linear weights stacked into one [2 rows][cols] k=1 product.
+  void stack2(Conv* c, const BlobTensor* a, const BlobTensor* b) {
     if (!a || !b) return;
     const size_t n = (size_t)(a->rows * a->cols);
     const size_t off = reserve_floats(2 * n);
     std::memcpy(&image[off], a->data, n * sizeof(float));
     std::memcpy(&image[off + n], b->data, n * sizeof(float));
-    fix.push_back({dst, off});
+    fix.push_back({&c->w, off});
+    c->cout = (int)(2 * a->rows), c->cin = (int)a->cols, c->taps = 1, c->stride = 1, c->dil = 1;
+    tc_pack(c, off);
   }
   // A causal convolution [cout][cin][k] (codec.rs:93-115): used as is.
   void conv(Conv* c, const std::string& w, const std::string& b, int64_t cin, int dil,
@@ -548,20 +562,21 @@ struct Loader {
       return;
     }
     c->cout = (int)d[0], c->cin = (int)d[1], c->taps = (int)d[2], c->stride = 1, c->dil = dil;
-    copy(&c->w, t);
+    tc_pack(c, copy(&c->w, t));
     vec(&c->b, b, d[0]);
   }
-  // A linear layer [out][in] as a k=1 convolution.
-  void linear(Conv* c, const std::string& w, const std::string& b, int64_t in) {
+  // A linear layer [out][in] as a k=1 convolution; no bias when `b` is empty. `out` >= 0
+  // requires that many rows.
+  void linear(Conv* c, const std::string& w, const std::string& b, int64_t in, int64_t out = -1) {
     const BlobTensor* t = need(w, -1);
     if (!t) return;
-    if (t->cols != in) {
+    if (t->cols != in || (out >= 0 && t->rows != out) || (t->ndim == 3 && t->shape[2] != 1)) {
       fail(w + " has an unexpected shape");
       return;
     }
     c->cout = (int)t->rows, c->cin = (int)t->cols, c->taps = 1, c->stride = 1, c->dil = 1;
-    copy(&c->w, t);
-    vec(&c->b, b, t->rows);
+    tc_pack(c, copy(&c->w, t));
+    if (!b.empty()) vec(&c->b, b, t->rows);
   }
   // A transposed convolution [cin][cout][kt] of stride s = kt / per (codec.rs:117-137),
   // repacked into its s stride phases of kt / s taps each.
@@ -587,18 +602,31 @@ struct Loader {
                 src[((size_t)ci * Co + co) * Kt + kk];
           }
     fix.push_back({&c->w, off});
+    tc_pack(c, off);
     vec(&c->b, b, Co);
   }
 };
 
-void conv_launch(cudaStream_t st, const Conv& c, const float* x, int L, float* y,
-                 const float* scale, const float* resid, int act) {
+// One product on the tensor cores (weight images present, SYRINX_CODEC_TC not 0) or on
+// the FP32 CUDA cores.
+cudaError_t conv_launch(const Codec& cd, const Conv& c, const float* x, int L, float* y, const float* scale,
+                        const float* resid, int act) {
+  if (cd.use_tc && c.tc) {
+    TcConvArgs t;
+    t.a_img = reinterpret_cast<const uint8_t*>(c.tc);
+    t.x = x, t.y = y, t.bias = c.b, t.scale = scale, t.resid = resid;
+    t.M = c.cout * c.stride, t.R = c.cin * c.taps, t.N = L;
+    t.k = c.taps, t.dil = c.dil, t.phase = c.stride, t.cout = c.cout, t.act = act;
+    t.err = cd.err;
+    return launch_conv_tc(t, cd.sms, cd.stream);
+  }
   ConvGemm p;
   p.w = c.w, p.x = x, p.y = y, p.bias = c.b, p.scale = scale, p.resid = resid;
   p.M = c.cout * c.stride, p.R = c.cin * c.taps, p.N = L;
   p.k = c.taps, p.dil = c.dil, p.phase = c.stride, p.cout = c.cout, p.act = act;
   const dim3 grid((L + kBN - 1) / kBN, (p.M + kBM - 1) / kBM);
-  k_conv_gemm<<<grid, 256, 0, st>>>(p);
+  k_conv_gemm<<<grid, 256, 0, cd.stream>>>(p);
+  return cudaSuccess;
 }
 
 inline unsigned cols_grid(int L, int per_block) {
@@ -614,6 +642,7 @@ Codec::~Codec() {
   cudaFree(grn);
   cudaFree(codes_dev);
   cudaFree(wav_dev);
+  cudaFree(err);
 }
 
 int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
@@ -675,13 +704,13 @@ int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
       const std::string p = tp + ".layers." + std::to_string(l);
       Layer& y = layers[l];
       ld.vec(&y.attn_norm, p + ".attention_norm.weight", D);
-      ld.vec(&y.wqkv, p + ".attention.wqkv.weight", 3 * D * D);
-      ld.vec(&y.wo, p + ".attention.wo.weight", D * D);
+      ld.linear(&y.wqkv, p + ".attention.wqkv.weight", "", D, 3 * D);
+      ld.linear(&y.wo, p + ".attention.wo.weight", "", D, D);
       ld.vec(&y.attn_gamma, p + ".attention_layer_scale.gamma", D);
       ld.vec(&y.ffn_norm, p + ".ffn_norm.weight", D);
       ld.stack2(&y.w13, ld.need(p + ".feed_forward.w1.weight", F * D),
                 ld.need(p + ".feed_forward.w3.weight", F * D));
-      ld.vec(&y.w2, p + ".feed_forward.w2.weight", D * F);
+      ld.linear(&y.w2, p + ".feed_forward.w2.weight", "", F, D);
       ld.vec(&y.ffn_gamma, p + ".ffn_layer_scale.gamma", D);
     }
     ld.vec(&post_norm, tp + ".norm.weight", D);
@@ -762,6 +791,14 @@ int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
   if (cudaSetDevice(device) != cudaSuccess) {
     *err = "cudaSetDevice failed";
     return SX_E_CUDA;
+  }
+  const char* tc_env = getenv("SYRINX_CODEC_TC");
+  use_tc = !(tc_env && tc_env[0] == '0');
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (cudaMalloc(&this->err, sizeof(int)) != cudaSuccess || cudaMemset(this->err, 0, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    *err = "device allocation failed";
+    return SX_E_OOM;
   }
   weight_bytes = ld.image.size() * sizeof(float);
   const size_t tab_off = (weight_bytes + 255) & ~size_t(255);
@@ -844,18 +881,14 @@ int Codec::decode_device(const uint32_t* codes, int ncb, int T, float* wav, std:
     const int D = latent, F = ffn;
     for (const Layer& y : layers) {
       k_chan_norm<<<(T + 31) / 32, 256, 0, st>>>(X, y.attn_norm, nullptr, S, D, T, kNormEps);
-      Conv qkv{y.wqkv, nullptr, 3 * D, D, 1, 1, 1};
-      conv_launch(st, qkv, S, T, Z, nullptr, nullptr, 0);
+      conv_launch(*this, y.wqkv, S, T, Z, nullptr, nullptr, 0);
       k_rope_cf<<<dim3((T + 127) / 128, D), 128, 0, st>>>(Z, D, T, inv_freq, kHeadDim / 2);
       k_attn_causal_cf<<<dim3((T + kQt - 1) / kQt, n_head), 256, 0, st>>>(Z, S, D, T);
-      Conv wo{y.wo, nullptr, D, D, 1, 1, 1};
-      conv_launch(st, wo, S, T, X, y.attn_gamma, X, 0);
+      conv_launch(*this, y.wo, S, T, X, y.attn_gamma, X, 0);
       k_chan_norm<<<(T + 31) / 32, 256, 0, st>>>(X, y.ffn_norm, nullptr, S, D, T, kNormEps);
-      Conv w13{y.w13, nullptr, 2 * F, D, 1, 1, 1};
-      conv_launch(st, w13, S, T, Z, nullptr, nullptr, 0);
+      conv_launch(*this, y.w13, S, T, Z, nullptr, nullptr, 0);
       k_swiglu_cf<<<cols_grid(F * T, 256), 256, 0, st>>>(Z, P, F, T);
-      Conv w2{y.w2, nullptr, D, F, 1, 1, 1};
-      conv_launch(st, w2, P, T, X, y.ffn_gamma, X, 0);
+      conv_launch(*this, y.w2, P, T, X, y.ffn_gamma, X, 0);
     }
     k_chan_norm<<<(T + 31) / 32, 256, 0, st>>>(X, post_norm, nullptr, S, D, T, kNormEps);
     std::swap(X, S);
@@ -863,33 +896,33 @@ int Codec::decode_device(const uint32_t* codes, int ncb, int T, float* wav, std:
 
   int L = T;
   for (const UpStage& u : ups) {
-    conv_launch(st, u.up, X, L, S, nullptr, nullptr, 0);
+    conv_launch(*this, u.up, X, L, S, nullptr, nullptr, 0);
     L *= u.up.stride;
     std::swap(X, S);
     const int C = u.c, C4 = u.pw1.cout;
     k_dwconv_causal<<<dim3(cols_grid(L, 256), C), 256, 0, st>>>(X, u.dw_w, u.dw_b, S, L, 7);
     k_chan_norm<<<(L + 31) / 32, 256, 0, st>>>(S, u.ln_w, u.ln_b, Z, C, L, kLnEps);
-    conv_launch(st, u.pw1, Z, L, P, nullptr, nullptr, 2);
+    conv_launch(*this, u.pw1, Z, L, P, nullptr, nullptr, 2);
     if (u.grn_g) {
       k_grn_norm<<<C4, 256, 0, st>>>(P, grn, L);
       k_grn_scale<<<1, 1024, 0, st>>>(grn, C4);
       k_grn_apply<<<dim3(cols_grid(L, 256), C4), 256, 0, st>>>(P, grn, u.grn_g, u.grn_b, L);
     }
-    conv_launch(st, u.pw2, P, L, X, u.gamma, X, 0);
+    conv_launch(*this, u.pw2, P, L, X, u.gamma, X, 0);
   }
 
-  conv_launch(st, conv0, X, L, S, nullptr, nullptr, 0);
+  conv_launch(*this, conv0, X, L, S, nullptr, nullptr, 0);
   std::swap(X, S);
   for (const DecBlock& b : blocks) {
     k_snake<<<dim3(cols_grid(L, 256), b.up.cin), 256, 0, st>>>(X, b.alpha, S, b.up.cin, L);
-    conv_launch(st, b.up, S, L, X, nullptr, nullptr, 0);
+    conv_launch(*this, b.up, S, L, X, nullptr, nullptr, 0);
     L *= b.up.stride;
     const int C = b.up.cout;
     for (const ResUnit& u : b.ru) {
       k_snake<<<dim3(cols_grid(L, 256), C), 256, 0, st>>>(X, u.a0, S, C, L);
-      conv_launch(st, u.c1, S, L, Z, nullptr, nullptr, 0);
+      conv_launch(*this, u.c1, S, L, Z, nullptr, nullptr, 0);
       k_snake<<<dim3(cols_grid(L, 256), C), 256, 0, st>>>(Z, u.a2, S, C, L);
-      conv_launch(st, u.c3, S, L, X, nullptr, X, 0);
+      conv_launch(*this, u.c3, S, L, X, nullptr, X, 0);
     }
   }
   k_snake<<<dim3(cols_grid(L, 256), final_cin), 256, 0, st>>>(X, final_alpha, S, final_cin, L);

@@ -32,11 +32,30 @@ struct Conv {
   int taps = 0;    // taps of the packed (per-phase) kernel
   int stride = 1;  // > 1: transposed convolution of this stride (phase-packed)
   int dil = 1;
+  float* tc = nullptr;  // the same matrix as tensor-core weight images (codec_tc.cu)
 };
 
 struct Layer {
-  float *attn_norm, *wqkv, *wo, *attn_gamma, *ffn_norm, *w13, *w2, *ffn_gamma;
+  float *attn_norm = nullptr, *attn_gamma = nullptr, *ffn_norm = nullptr, *ffn_gamma = nullptr;
+  Conv wqkv, wo, w13, w2;  // linear layers (k = 1, no bias); w13 stacks w1 over w3
 };
+
+// The product of codec_tc.cu: Y = W * im2col(X) on tcgen05 (kind::tf32, three-term split).
+struct TcConvArgs {
+  const uint8_t* a_img = nullptr;  // weight images [n_mt][n_kb] of 16 KB
+  const float* x = nullptr;
+  float* y = nullptr;
+  const float* bias = nullptr;
+  const float* scale = nullptr;
+  const float* resid = nullptr;
+  int M = 0, R = 0, N = 0, k = 1, dil = 1, phase = 1, cout = 0, act = 0;
+  int n_mt = 0, n_kb = 0, n_nt = 0, bn = 0;  // set by launch_conv_tc
+  int* err = nullptr;
+};
+size_t tc_image_bytes(int M, int R);
+// Weight images of the row-major [M][R] matrix A into out (tc_image_bytes(M, R) bytes).
+void tc_image(const float* A, int M, int R, uint32_t* out);
+cudaError_t launch_conv_tc(const TcConvArgs& a, int sms, cudaStream_t st);
 
 struct UpStage {
   Conv up;  // transposed conv, kernel = stride = factor
@@ -77,6 +96,9 @@ struct Codec {
   float* final_b = nullptr;
   int final_cin = 0;
   CbTab* tabs = nullptr;  // device array [1 + n_res]
+  int* err = nullptr;     // device error flag of the tensor-core product's bounded waits
+  bool use_tc = true;     // SYRINX_CODEC_TC=0 selects the FP32 CUDA-core product
+  int sms = 148;
   void* weights = nullptr;
   size_t weight_bytes = 0;
   // activation buffers, grown by reserve()
