@@ -25,7 +25,8 @@
 //   - warp 8, one lane: bulk copies of the weight images into a 6-stage ring; the warp also
 //     owns the TMEM allocation (4 accumulators of 128 columns);
 //   - warp 9, one lane: issues 6 MMAs per k block (2 k steps x 3 products) and the commits;
-//   - warps 10-17: stage the k block's B operand: im2col gather, split, swizzled stores.
+//   - warps 10-17: stage the B operands (im2col gather, split, swizzled stores), four
+//     groups of two warps taking every fourth k block, so four gathers are in flight.
 // Every wait is bounded by %globaltimer and raises the error flag; TMEM is freed on every path.
 #include <cuda_runtime.h>
 
@@ -46,6 +47,7 @@ constexpr int kStagesTc = 6;
 constexpr int kChunkKB = 4;   // k blocks accumulated in TMEM before the register sum
 constexpr int kAccBufs = 4;   // TMEM accumulators of kBN columns
 constexpr int kEpiW = 8, kProdW = 8;
+constexpr int kGroups = kProdW / 2;  // staging groups of two warps
 constexpr int kCopyW = kEpiW, kMmaW = kEpiW + 1;
 constexpr int kWarpsTc = kEpiW + 2 + kProdW;
 constexpr int kThreadsTc = kWarpsTc * 32;
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_conv_tc(const __grid_constant
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesTc; s++) {
-      mbar_init(&sm.full[s], 1 + kProdW);  // the weight copy (with its bytes) + the staging warps
+      mbar_init(&sm.full[s], 1 + 2);  // the weight copy (with its bytes) + one staging group
       mbar_init(&sm.empty[s], 1);          // the k block's MMAs (commit)
     }
     for (int b = 0; b < kAccBufs; b++) {
@@ -200,14 +202,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_conv_tc(const __grid_constant
       }
     }
   } else if (warp > kMmaW) {
-    // ---- staging: thread i covers row n = i % kBN (consecutive across lanes) of the
-    // 4-wide k piece i / kBN; both items of a thread are loaded before either is stored ----
-    const int pt = (warp - kMmaW - 1) * 32 + lane;
-    constexpr int kItems = kBN * 4 / (kProdW * 32);
+    // ---- staging: kGroups groups of two warps; group j stages the k blocks g with
+    // g % kGroups == j, so that kGroups blocks' gathers are in flight at once. In a block,
+    // thread i of a group covers rows n = i and i + 64 of each 4-wide k piece c, and all its
+    // 32 loads are issued before the first store and before the wait for the ring stage ----
+    const int sw = warp - kMmaW - 1, grp = sw >> 1, gt = (sw & 1) * 32 + lane;
     int g = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
       const int n0 = (t / p.n_mt) * kBN;
       for (int kb = 0; kb < p.n_kb; kb++, g++) {
+        if (g % kGroups != grp) continue;
         const int s = g % kStagesTc;
         // the k block's 16 reduction rows: lane j (< 16) resolves row kb*16 + j to its
         // channel and causal shift once, the warp reads them by shuffle
@@ -220,34 +224,42 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_conv_tc(const __grid_constant
             shift = (p.k - 1 - tap) * p.dil;
           }
         }
-        float v[kItems][4];
+        float v[4][2][4];  // [piece c][row n = gt + 64 hh][k in piece]
 #pragma unroll
-        for (int it = 0; it < kItems; it++) {
-          const int i = pt + it * kProdW * 32;
-          const int n = i % kBN, c = i / kBN, col = n0 + n;
+        for (int c = 0; c < 4; c++) {
+          int ci[4], sh[4];
 #pragma unroll
           for (int q = 0; q < 4; q++) {
-            const int ci = __shfl_sync(0xffffffffu, base, c * 4 + q);
-            const int sh = __shfl_sync(0xffffffffu, shift, c * 4 + q);
-            const int src = col - sh;
-            v[it][q] = (ci >= 0 && col < p.N && src >= 0) ? __ldg(p.x + (size_t)ci * p.N + src) : 0.f;
+            ci[q] = __shfl_sync(0xffffffffu, base, c * 4 + q);
+            sh[q] = __shfl_sync(0xffffffffu, shift, c * 4 + q);
+          }
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            const int col = n0 + gt + 64 * hh;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              const int src = col - sh[q];
+              v[c][hh][q] = (ci[q] >= 0 && col < p.N && src >= 0) ? __ldg(p.x + (size_t)ci[q] * p.N + src) : 0.f;
+            }
           }
         }
         if (g >= kStagesTc) tcw(&sm.empty[s], (uint32_t)((g / kStagesTc - 1) & 1), p.err);
         uint8_t* Bh = sm.B[s];
         uint8_t* Bl = Bh + kBN * 64;
 #pragma unroll
-        for (int it = 0; it < kItems; it++) {
-          const int i = pt + it * kProdW * 32;
-          const int n = i % kBN, c = i / kBN;
-          float4 hi, lo;
-          hi.x = tf32_hi(v[it][0]), hi.y = tf32_hi(v[it][1]), hi.z = tf32_hi(v[it][2]), hi.w = tf32_hi(v[it][3]);
-          lo.x = v[it][0] - hi.x, lo.y = v[it][1] - hi.y, lo.z = v[it][2] - hi.z, lo.w = v[it][3] - hi.w;
-          int o = (n >> 3) * 512 + (n & 7) * 64 + c * 16;
-          o ^= ((o >> 7) & 3) << 4;
-          *reinterpret_cast<float4*>(Bh + o) = hi;
-          *reinterpret_cast<float4*>(Bl + o) = lo;
-        }
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            const int n = gt + 64 * hh;
+            const float* w = v[c][hh];
+            float4 hi, lo;
+            hi.x = tf32_hi(w[0]), hi.y = tf32_hi(w[1]), hi.z = tf32_hi(w[2]), hi.w = tf32_hi(w[3]);
+            lo.x = w[0] - hi.x, lo.y = w[1] - hi.y, lo.z = w[2] - hi.z, lo.w = w[3] - hi.w;
+            int o = (n >> 3) * 512 + (n & 7) * 64 + c * 16;
+            o ^= ((o >> 7) & 3) << 4;
+            *reinterpret_cast<float4*>(Bh + o) = hi;
+            *reinterpret_cast<float4*>(Bl + o) = lo;
+          }
         fence_async();  // generic-proxy stores become visible to the tensor core
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.full[s]);

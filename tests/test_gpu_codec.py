@@ -76,17 +76,18 @@ def test_clamped_codes(tiny):
     _check(w, c, big)
 
 
-def test_s2_long_prefix_is_bitwise_stable(s2):
-    """Without GRN every stage is causal and each column's reductions run in a fixed order,
-    so a prefix of the codes decodes to exactly the prefix of the waveform (a
-    size-independent check at 480 frames, 22 s of audio)."""
+def test_s2_long_prefix_is_stable(s2):
+    """Without GRN every stage is causal, so a prefix of the codes decodes to the prefix of
+    the waveform (a size-independent check at 480 frames, 22 s of audio). The two decodes
+    may run a product on different units (tensor cores when it fills the GPU, CUDA cores
+    otherwise), so the check is to 1e-4, ten times inside the parity bound."""
     _, c = s2
     codes = synth_codes(S2_CODEC, 480, seed=5)
     full = c.decode(codes)
     assert full.shape == (480 * S2_CODEC.hop,)
     assert np.isfinite(full).all() and 0.05 < full.std() < 0.9
     head = c.decode(codes[:, :100])
-    assert np.array_equal(head, full[: head.size])
+    assert float(np.max(np.abs(head - full[: head.size]))) < 1e-4
 
 
 def test_device_entry_point_matches_host(tiny):
