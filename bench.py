@@ -42,6 +42,15 @@ METRIC = "semantic frames/s/GPU, 4B-shape Q8_0 dual-AR decode b1/b8; % of HBM ro
 W13_DRAM_BYTES = 53085184
 
 
+def peak_bf16():
+    """(bf16 dense TFLOP/s burst, "measured" | "fallback")."""
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -348,7 +357,7 @@ def bench_codec(args, local, stream, dist, world, rank):
     weights (0.74 GB) and activations exceed L2, so no flush is needed between decodes."""
     import torch
     from syrinx_b200 import dp
-    from syrinx_b200.codec import S2_CODEC, RvqCodec, decode_flops, synth_codec_weights, synth_codes
+    from syrinx_b200.codec import S2_CODEC, RvqCodec, decode_flops, decode_launches, synth_codec_weights, synth_codes
 
     T = CODEC_FRAMES
     K, W = min(args.steps, 8), 3
@@ -380,18 +389,25 @@ def bench_codec(args, local, stream, dist, world, rank):
     assert np.array_equal(host_wav, wav.cpu().numpy())
     flops = decode_flops(S2_CODEC, T)
     tflops = flops / (ms * 1e-3) / 1e12
-    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # FP32 lanes x 2 x clocks.max.sm, nominal
+    if os.environ.get("SYRINX_CODEC_TC", "1") == "0":
+        bound, cpeak = "fp32", 148 * 128 * 2 * 1.965e9 / 1e12
+        psrc = ("nominal FP32 CUDA-core rate at clocks.max.sm (148 SMs x 128 lanes x 2 x 1965 MHz); "
+                "not in MEASURED_PEAKS.json")
+    else:
+        bf16, kind = peak_bf16()
+        bound, cpeak = "tensor", bf16 / 2 / 3
+        psrc = (f"{kind} bf16 dense {bf16} TFLOP/s (MEASURED_PEAKS.json) / 2 (kind::tf32 runs at half the "
+                "bf16 rate) / 3 (three tf32 products per f32 product): the useful-f32 ceiling of the split")
     out = {"value": round(T * world / (ms * 1e-3), 1), "unit": "codec frames/s",
            "audio_s_per_s": round(T * codec.hop / 44100 * world / (ms * 1e-3), 1),
            "ms_per_decode": round(ms, 3), "steps": K, "warmup": W,
+           "gpu_launches": decode_launches(S2_CODEC) * K,
            "workload": f"s2 codec decode, {T} frames x 10 codebooks -> {T * codec.hop} samples, "
                        "synthetic weights of the s2 shape (seed %d)" % SEED,
-           "dtype": "f32",
-           "roofline": {"bound": "fp32", "achieved": round(tflops, 2), "unit": "TFLOP/s",
-                        "flops_per_decode": flops, "peak": round(fp32_peak, 1),
-                        "frac": round(tflops / fp32_peak, 4),
-                        "peak_source": "nominal FP32 CUDA-core rate at clocks.max.sm (148 SMs x 128 lanes "
-                                       "x 2 x 1965 MHz); not in MEASURED_PEAKS.json"},
+           "dtype": "f32 (products: tf32 three-term split on tcgen05, f32 sums)" if bound == "tensor" else "f32",
+           "roofline": {"bound": bound, "achieved": round(tflops, 2), "unit": "TFLOP/s",
+                        "flops_per_decode": flops, "peak": round(cpeak, 1),
+                        "frac": round(tflops / cpeak, 4), "peak_source": psrc},
            "e2e": {"value": round(T * world / (ms_e2e * 1e-3), 1), "unit": "codec frames/s",
                    "h2d_bytes_per_step": int(codes.size * 4), "d2h_bytes_per_step": int(T * codec.hop * 4),
                    "api": "sx_codec_decode (host codes in, host waveform out)"}}

@@ -168,6 +168,16 @@ def decode_flops(shape: CodecShape, frames: int) -> int:
     return int(fl)
 
 
+def decode_launches(shape: CodecShape) -> int:
+    """Kernel launches of one device decode (the sequence of Codec::decode_device)."""
+    n = 1  # RVQ from_codes
+    if shape.n_layers:
+        n += 9 * shape.n_layers + 1  # norm, wqkv, rope, attention, wo, norm, w1|w3, SwiGLU, w2; final norm
+    n += sum(5 + (3 if g else 0) for g in shape.grn)  # transposed conv, dwconv, LayerNorm, pwconv1, [GRN], pwconv2
+    n += 1 + 14 * len(shape.decoder_rates) + 2  # first conv; Snake + transposed conv + 3 units; Snake + last conv
+    return n
+
+
 class RvqCodec:
     """Codes -> waveform on one GPU (`RvqCodec::decode`, common/codec.rs:26; `EvaGanDac::
     decode`, s2/codec.rs:342-379). `weights` is a dict of f32 arrays (reference names) or
