@@ -1,5 +1,7 @@
-"""CPU restatement of the s2 codec decode, `EvaGanDac::decode`
-(crates/syrinx-fish/src/s2/codec.rs:342-379), in float64 numpy.
+"""CPU restatement of the codec decode, in float64 numpy: the s2 `EvaGanDac::decode`
+(crates/syrinx-fish/src/s2/codec.rs:342-379) and the s1 `ModdedDac::decode`
+(crates/syrinx-fish/src/s1/codec.rs:262-290), which is the same decoder without the
+post_module transformer and with its tensors at the top level of the names.
 
 TEST INFRASTRUCTURE ONLY: imported by tests/ and by nothing on the product path.
 
@@ -175,13 +177,13 @@ def decode_codebook(w, prefix, codes):
     return causal_conv1d(zp, _f(w, f"{prefix}.out_proj.weight"), _f(w, f"{prefix}.out_proj.bias"))
 
 
-def upsample(w, z):
+def upsample(w, z, qp="quantizer."):
     """codec.rs:278-300: per stage a transposed conv (kernel = stride) then ConvNeXt."""
     s = 0
-    while f"quantizer.upsample.{s}.0.conv.weight" in w:
-        wt = _f(w, f"quantizer.upsample.{s}.0.conv.weight")
-        z = causal_transpose1d(z, wt, _f(w, f"quantizer.upsample.{s}.0.conv.bias"), wt.shape[2])
-        z = convnext(w, f"quantizer.upsample.{s}.1", z)
+    while f"{qp}upsample.{s}.0.conv.weight" in w:
+        wt = _f(w, f"{qp}upsample.{s}.0.conv.weight")
+        z = causal_transpose1d(z, wt, _f(w, f"{qp}upsample.{s}.0.conv.bias"), wt.shape[2])
+        z = convnext(w, f"{qp}upsample.{s}.1", z)
         s += 1
     return z
 
@@ -204,18 +206,22 @@ def run_generator(w, z):
 
 
 def decode(w, codes):
-    """codes [n_codebooks, T] -> waveform [T * hop] (float64)."""
+    """codes [n_codebooks, T] -> waveform [T * hop] (float64). The s2 codec
+    (`EvaGanDac::decode`) nests the RVQ, upsample and post_module under `quantizer.`; the s1
+    modded DAC (`ModdedDac::decode`, crates/syrinx-fish/src/s1/codec.rs:262-290) has them at
+    the top level and no post_module."""
     codes = np.asarray(codes)
     if codes.ndim == 3:
         codes = codes[0]
     n_cb, T = codes.shape
-    sem = "quantizer.semantic_quantizer.quantizers.0"
+    qp = "quantizer." if "quantizer.semantic_quantizer.quantizers.0.codebook.weight" in w else ""
+    sem = f"{qp}semantic_quantizer.quantizers.0"
     sem_max = w[f"{sem}.codebook.weight"].shape[0] - 1
     z = decode_codebook(w, sem, np.minimum(codes[0].astype(np.int64), sem_max))
     for i in range(n_cb - 1):
-        pre = f"quantizer.quantizer.quantizers.{i}"
+        pre = f"{qp}quantizer.quantizers.{i}"
         res_max = w[f"{pre}.codebook.weight"].shape[0] - 1
         z = z + decode_codebook(w, pre, np.minimum(codes[i + 1].astype(np.int64), res_max))
-    z = transformer(w, "quantizer.post_module", z)
-    z = upsample(w, z)
+    z = transformer(w, f"{qp}post_module", z)
+    z = upsample(w, z, qp)
     return run_generator(w, z).reshape(-1)

@@ -36,6 +36,7 @@ class CodecShape:
     decoder_dim: int = 1536       # decoder.model.0 output channels
     decoder_rates: tuple = (8, 8, 4, 2)
     sample_rate: int = 44100
+    variant: str = "s2"           # "s1": modded-DAC names at the top level, no post_module
 
     @property
     def hop(self) -> int:
@@ -47,6 +48,9 @@ class CodecShape:
 
 
 S2_CODEC = CodecShape()
+# The s1 modded DAC (ModdedDac, crates/syrinx-fish/src/s1/codec.rs): the same decoder and
+# upsample, the RVQ and upsample at the top level of the names, no post_module transformer.
+S1_CODEC = CodecShape(variant="s1", n_layers=0)
 # A small codec of the same structure for quick checks: every branch (GRN and no GRN,
 # layer scale and none) is present.
 TINY_CODEC = CodecShape(latent=128, n_layers=2, ffn=256, semantic_size=64, residual_size=32,
@@ -68,16 +72,17 @@ def synth_codec_weights(shape: CodecShape = S2_CODEC, seed: int = 0) -> dict:
         return rng.uniform(lo, hi, shp).astype(np.float32)
 
     D, cbd = shape.latent, shape.codebook_dim
+    qp = "quantizer." if shape.variant == "s2" else ""
     for i in range(shape.num_codebooks):
-        pre = ("quantizer.semantic_quantizer.quantizers.0" if i == 0
-               else f"quantizer.quantizer.quantizers.{i - 1}")
+        pre = (f"{qp}semantic_quantizer.quantizers.0" if i == 0
+               else f"{qp}quantizer.quantizers.{i - 1}")
         size = shape.semantic_size if i == 0 else shape.residual_size
         w[f"{pre}.codebook.weight"] = normal((size, cbd), 1.0)
         w[f"{pre}.out_proj.weight"] = normal((D, cbd, 1), 0.3 / np.sqrt(cbd))
         w[f"{pre}.out_proj.bias"] = normal((D,), 0.02)
     F = shape.ffn
     for layer in range(shape.n_layers):
-        p = f"quantizer.post_module.layers.{layer}"
+        p = f"{qp}post_module.layers.{layer}"
         w[f"{p}.attention_norm.weight"] = unif((D,), 0.8, 1.2)
         w[f"{p}.attention.wqkv.weight"] = normal((3 * D, D), 1.0 / np.sqrt(D))
         w[f"{p}.attention.wo.weight"] = normal((D, D), 1.0 / np.sqrt(D))
@@ -88,10 +93,10 @@ def synth_codec_weights(shape: CodecShape = S2_CODEC, seed: int = 0) -> dict:
         w[f"{p}.feed_forward.w2.weight"] = normal((D, F), 1.0 / np.sqrt(F))
         w[f"{p}.ffn_layer_scale.gamma"] = unif((D,), 0.05, 0.3)
     if shape.n_layers:
-        w["quantizer.post_module.norm.weight"] = unif((D,), 0.8, 1.2)
+        w[f"{qp}post_module.norm.weight"] = unif((D,), 0.8, 1.2)
     C = D
     for s, f in enumerate(reversed(shape.up_factors)):
-        p = f"quantizer.upsample.{s}"
+        p = f"{qp}upsample.{s}"
         w[f"{p}.0.conv.weight"] = normal((C, C, f), 1.0 / np.sqrt(C))
         w[f"{p}.0.conv.bias"] = normal((C,), 0.02)
         b, C4 = f"{p}.1", shape.convnext_mult * C

@@ -652,8 +652,12 @@ int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
   if (rc) return rc;
   Loader ld(ix, err);
 
+  // Tensor names: the s2 codec nests the RVQ, its upsample and its post_module under
+  // `quantizer.` (s2/codec.rs:348-372); the s1 modded DAC has them at the top level and no
+  // post_module transformer (s1/codec.rs:255-290).
+  const std::string qp = ld.has("quantizer.semantic_quantizer.quantizers.0.codebook.weight") ? "quantizer." : "";
   // RVQ tables (codec.rs:259-276, 342-367)
-  const std::string sem = "quantizer.semantic_quantizer.quantizers.0";
+  const std::string sem = qp + "semantic_quantizer.quantizers.0";
   const BlobTensor* cb0 = ld.need(sem + ".codebook.weight", -1);
   if (!cb0) return SX_E_BLOB;
   sem_size = (int)cb0->rows, cb_dim = (int)cb0->cols;
@@ -667,11 +671,11 @@ int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
     }
     latent = (int)d[0];
   }
-  while (ld.has("quantizer.quantizer.quantizers." + std::to_string(n_res) + ".codebook.weight")) n_res++;
+  while (ld.has(qp + "quantizer.quantizers." + std::to_string(n_res) + ".codebook.weight")) n_res++;
   std::vector<float*> cb(1 + n_res), pw(1 + n_res), pb(1 + n_res);
   std::vector<int> sizes(1 + n_res);
   for (int i = 0; i <= n_res; i++) {
-    const std::string pre = i == 0 ? sem : "quantizer.quantizer.quantizers." + std::to_string(i - 1);
+    const std::string pre = i == 0 ? sem : qp + "quantizer.quantizers." + std::to_string(i - 1);
     const BlobTensor* c = ld.need(pre + ".codebook.weight", -1);
     if (!c) return SX_E_BLOB;
     if (c->cols != cb_dim) {
@@ -687,7 +691,7 @@ int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
   if (!ld.ok) return SX_E_BLOB;
 
   // post_module transformer (codec.rs:559-626); the layer count is read from the blob
-  const std::string tp = "quantizer.post_module";
+  const std::string tp = qp + "post_module";
   while (ld.has(tp + ".layers." + std::to_string(n_layers) + ".attention_norm.weight")) n_layers++;
   if (n_layers) {
     if (latent % kHeadDim) {
@@ -725,11 +729,11 @@ int Codec::load(const void* blob, size_t size, int dev, std::string* err) {
 
   // ConvNeXt upsample (codec.rs:278-300): kernel = stride = factor per stage
   int n_up = 0;
-  while (ld.has("quantizer.upsample." + std::to_string(n_up) + ".0.conv.weight")) n_up++;
+  while (ld.has(qp + "upsample." + std::to_string(n_up) + ".0.conv.weight")) n_up++;
   ups.resize(n_up);
   int64_t C = latent;
   for (int s = 0; s < n_up; s++) {
-    const std::string p = "quantizer.upsample." + std::to_string(s);
+    const std::string p = qp + "upsample." + std::to_string(s);
     UpStage& u = ups[s];
     ld.tconv(&u.up, p + ".0.conv.weight", p + ".0.conv.bias", C, 1);
     if (!ld.ok) return SX_E_BLOB;

@@ -14,7 +14,7 @@ import torch.nn.functional as F
 from oracle import codec_oracle as co
 from syrinx_b200 import _lib
 from syrinx_b200.blob import read_blob, write_blob
-from syrinx_b200.codec import TINY_CODEC, CodecShape, synth_codec_weights, synth_codes
+from syrinx_b200.codec import S1_CODEC, TINY_CODEC, CodecShape, synth_codec_weights, synth_codes
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 RNG = np.random.default_rng(7)
@@ -146,6 +146,26 @@ def test_oracle_clamps_codes():
     ref[0, 1] = NO_GRN.semantic_size - 1
     ref[2, 3] = NO_GRN.residual_size - 1
     assert np.array_equal(co.decode(w, big), co.decode(w, ref))
+
+
+TINY_S1 = CodecShape(variant="s1", latent=128, n_layers=0, semantic_size=64, residual_size=32,
+                     n_residual=3, decoder_dim=96)
+
+
+def test_s1_names_and_oracle():
+    """The s1 modded DAC: RVQ and upsample at the top level of the names, no post_module."""
+    w = synth_codec_weights(TINY_S1, seed=2)
+    assert "semantic_quantizer.quantizers.0.codebook.weight" in w and "upsample.0.0.conv.weight" in w
+    assert not any(k.startswith("quantizer.semantic") or "post_module" in k for k in w)
+    assert {k for k in synth_codec_weights(S1_CODEC, seed=0) if "post_module" in k} == set()
+    y = co.decode(w, synth_codes(TINY_S1, 6, seed=1))
+    assert y.shape == (6 * TINY_S1.hop,) and 0.05 < y.std() < 0.9
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device error path")
+def test_s1_blob_parses_before_the_device():
+    rc, msg = _create(write_blob(synth_codec_weights(TINY_S1, seed=2)))
+    assert rc == -2 and "cuda" in msg.lower()
 
 
 def test_codec_blob_round_trip_keeps_rank3_kernels():

@@ -9,7 +9,7 @@ import torch
 
 from oracle import codec_oracle as co
 from syrinx_b200 import _lib
-from syrinx_b200.codec import S2_CODEC, TINY_CODEC, RvqCodec, synth_codec_weights, synth_codes
+from syrinx_b200.codec import S1_CODEC, S2_CODEC, TINY_CODEC, RvqCodec, synth_codec_weights, synth_codes
 
 pytestmark = pytest.mark.gpu
 WAV_TOL = 1e-3
@@ -61,6 +61,16 @@ def test_fewer_codebooks(tiny, ncb):
 def test_s2_matches_oracle(s2, T):
     w, c = s2
     _check(w, c, synth_codes(S2_CODEC, T, seed=100 + T))
+
+
+def test_s1_modded_dac_matches_oracle():
+    """The s1 codec (ModdedDac::decode, s1/codec.rs:262-290): no post_module, top-level names."""
+    w = synth_codec_weights(S1_CODEC, seed=13)
+    c = RvqCodec(w)
+    assert c.info.n_layers == 0 and c.info.num_codebooks == 10 and c.hop == 2048
+    _check(w, c, synth_codes(S1_CODEC, 8, seed=14))
+    _check(w, c, synth_codes(S1_CODEC, 5, seed=15, n_codebooks=8))  # config 2 emits 8 codebooks
+    c.close()
 
 
 def test_clamped_codes(tiny):
