@@ -43,9 +43,19 @@ __device__ double next_f64(SampleState* st) {
   return (double)(z >> 11) * (1.0 / 9007199254740992.0);
 }
 
+// Whether shared memory also holds the kept ids' f64 softmax terms (8 bytes per id), so that
+// every thread makes them: up to 4096-odd ids (the Fish semantic and codebook draws); the
+// CosyVoice heads (6564 / 6761 ids) make them on one thread.
+__host__ __device__ __forceinline__ bool sample_smem_par(int n) {
+  int np = 1;
+  while (np < n) np <<= 1;
+  return (size_t)np * 8 + (size_t)n * (8 + 4 + 4 + 4 + 1 + 8) <= 200 * 1024;
+}
+
 struct Smem {
   unsigned long long* keys;  // [np] sort keys, then rank order
-  double* exps;              // [n] by rank: exp(logit - max)
+  double* exps;              // [n] by rank: exp(logit - max), then that over the sum
+  double* ed;                // [n] the kept ids' exp terms in index order, or null (no room)
   float* lg;                 // [n] logits in index order
   float* pf;                 // [n] probabilities in index order (kept ids only)
   int* kept;                 // [n] the kept ids' indices, ascending
@@ -95,13 +105,14 @@ __device__ uint32_t draw(const SampleArgs& a, const Smem& m, int n, double sum, 
   __shared__ uint32_t s_pick;
   const int tid = threadIdx.x;
   if (tid == 0) {
-    // the kept ids are the rank prefix [0, rend)
+    // the kept ids are the rank prefix [0, rend); exps[r] already holds exps[r] / sum, so
+    // the one sequential chain left here is the reference's f64 additions
     const int k_cap = top_k == 0 ? n : top_k;
     double cum = 0.0;
     int r = 0;
     for (; r < n; r++) {
       if (r > 0 && !(cum <= (double)top_p && r < k_cap)) break;
-      cum += m.exps[r] / sum;
+      cum += m.exps[r];
     }
     s_rend = r;
   }
@@ -119,9 +130,26 @@ __device__ uint32_t draw(const SampleArgs& a, const Smem& m, int n, double sum, 
   if ((tid & 31) == 0) s_red[tid >> 5] = mx;
   __syncthreads();
   compact_kept(m, n);  // the index-order loops below visit only the rend kept ids
-  if (tid == 0) {
-    float kept_max = -INFINITY;
-    for (int w = 0; w < kThreadsS / 32; w++) kept_max = fmaxf(kept_max, s_red[w]);
+  // The temperature softmax over the kept ids. The terms (an f64 exp each) are independent:
+  // every thread makes some; the sums over them stay one thread's sequential f64 chain in
+  // index order, as in the reference.
+  __shared__ double s_psum;
+  float kept_max = -INFINITY;
+  for (int w = 0; w < kThreadsS / 32; w++) kept_max = fmaxf(kept_max, s_red[w]);
+  if (m.ed) {
+    for (int j = tid; j < rend; j += kThreadsS) {
+      const int i = m.kept[j];
+      const double e = exp((double)(__fdiv_rn(m.lg[i], t) - kept_max));
+      m.pf[i] = (float)e;
+      m.ed[j] = e;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      double psum = 0.0;
+      for (int j = 0; j < rend; j++) psum += m.ed[j];
+      s_psum = psum;
+    }
+  } else if (tid == 0) {
     double psum = 0.0;
     for (int j = 0; j < rend; j++) {
       const int i = m.kept[j];
@@ -129,8 +157,14 @@ __device__ uint32_t draw(const SampleArgs& a, const Smem& m, int n, double sum, 
       m.pf[i] = (float)e;
       psum += e;
     }
-    if (psum > 0.0)
-      for (int j = 0; j < rend; j++) m.pf[m.kept[j]] = (float)((double)m.pf[m.kept[j]] / psum);
+    s_psum = psum;
+  }
+  __syncthreads();
+  const double psum = s_psum;
+  if (psum > 0.0)
+    for (int j = tid; j < rend; j += kThreadsS) m.pf[m.kept[j]] = (float)((double)m.pf[m.kept[j]] / psum);
+  __syncthreads();
+  if (tid == 0) {
     double total = 0.0;
     for (int j = 0; j < rend; j++) total += (double)m.pf[m.kept[j]];
     uint32_t pick = 0;
@@ -163,7 +197,8 @@ __global__ void __launch_bounds__(kThreadsS, 1) k_sample(const SampleArgs a) {
   Smem m;
   m.keys = reinterpret_cast<unsigned long long*>(sm);
   m.exps = reinterpret_cast<double*>(m.keys + np);
-  m.lg = reinterpret_cast<float*>(m.exps + n);
+  m.ed = sample_smem_par(n) ? m.exps + n : nullptr;
+  m.lg = reinterpret_cast<float*>(m.exps + (m.ed ? 2 * n : n));
   m.pf = m.lg + n;
   m.kept = reinterpret_cast<int*>(m.pf + n);
   m.keep = reinterpret_cast<uint8_t*>(m.kept + n);
@@ -218,6 +253,9 @@ __global__ void __launch_bounds__(kThreadsS, 1) k_sample(const SampleArgs a) {
   }
   __syncthreads();
   const double sum = s_sum;
+  // the top-p cut's terms exps[r] / sum, made once for both draws (independent divisions)
+  for (int r = tid; r < n; r += kThreadsS) m.exps[r] = m.exps[r] / sum;
+  __syncthreads();
   const sx_sampling_params p = *a.params;
   uint32_t pick = draw(a, m, n, sum, p.temperature, p.top_p, p.top_k);
   if (a.semantic) {
@@ -244,7 +282,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) k_sample(const SampleArgs a) {
 size_t sample_smem_bytes(int n) {
   int np = 1;
   while (np < n) np <<= 1;
-  return (size_t)np * 8 + (size_t)n * (8 + 4 + 4 + 4 + 1);
+  return (size_t)np * 8 + (size_t)n * (8 + 4 + 4 + 4 + 1) + (sample_smem_par(n) ? (size_t)n * 8 : 0);
 }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {

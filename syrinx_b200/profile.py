@@ -8,6 +8,7 @@ Qwen3-4B-shaped model with fewer layers, so an `ncu --set full` capture stays sm
   python -m syrinx_b200.profile --what prefill --layers 36 --prompt 512  (prefill time, printed)
   python -m syrinx_b200.profile --what batch --layers 8 --q4k --frames 4   (8 utterances batched)
   python -m syrinx_b200.profile --what codec --frames 32 --launches 2   (s2 codec decodes, timed)
+  python -m syrinx_b200.profile --what sample --layers 8 --frames 4 --prompt 512  (sampled frames)
 """
 from __future__ import annotations
 
@@ -40,7 +41,7 @@ def codec_run(frames: int, n: int):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill", "batch", "codec"], default="gemv")
+    ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill", "batch", "codec", "sample"], default="gemv")
     ap.add_argument("--kind", type=int, default=2, help="0 wqkv, 1 wo, 2 w1|w3, 3 w2")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--launches", type=int, default=16)
@@ -86,6 +87,9 @@ def main():
         be.decode_greedy(args.frames, mask_stop=True)
     elif args.what == "gemv":
         be.profile_gemv(args.kind, args.launches)  # close() below synchronizes the stream
+    elif args.what == "sample":  # the reference's default sampling (temperature, top-p, RAS)
+        from . import SamplingParams
+        be.decode_sample(args.frames, seed=7, sampling=SamplingParams())
     else:
         be.decode_greedy(args.frames, mask_stop=True)
     be.close()
