@@ -113,10 +113,13 @@ class Clocks:
 
 def kernels_per_frame(cfg, stack: bool = True) -> int:
     """Kernel launches in one greedy frame graph (mirrors the sequence in model.cu). A Q8_0
-    GEMV is two launches: k_gemv_q8 and its k_merge_q8. With the persistent decode kernel a
-    whole stack (36 slow layers, or the 4 fast layers of one codebook step) is one launch."""
+    GEMV is two launches: k_gemv_q8 and its k_merge_q8, except the decode wqkv GEMV, whose
+    partials the attention kernel adds (one launch, unless SYRINX_QKV_MERGE=1). With the
+    persistent decode kernel a whole stack (36 slow layers, or the 4 fast layers of one
+    codebook step) is one launch."""
     gemv = 2
-    per_layer = 4 * gemv + 1  # wqkv, wo, w1|w3, w2 + attention
+    qkv = 2 if os.environ.get("SYRINX_QKV_MERGE", "0") == "1" else 1
+    per_layer = qkv + 3 * gemv + 1  # wqkv, wo, w1|w3, w2 + attention
     n = gemv + 1  # semantic head, take_semantic
     if cfg.has_fast:
         C = cfg.num_codebooks

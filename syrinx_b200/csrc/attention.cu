@@ -135,6 +135,63 @@ __device__ void append_kv(const AttnArgs& a, int m, int seq, int pos, int g, flo
   }
 }
 
+// One q|k|v row of token m for the decode kernel. With the wqkv GEMV's partials (EPI_NONE) the
+// row's k-chunk partials are loaded (all at once, zeros past qkv_nc); otherwise the merged row
+// value goes to pv[0]. row < 0: nothing to load.
+template <int NC>
+__device__ __forceinline__ void qkv_fetch(const AttnArgs& a, int m, int row, float (&pv)[NC]) {
+#pragma unroll
+  for (int kc = 0; kc < NC; kc++) pv[kc] = 0.f;
+  if (row < 0) return;
+  if (a.qkv_part) {
+    const float* p = a.qkv_part + ((size_t)(row >> 4) * a.qkv_nc * a.qkv_mt + m) * 16 + (row & 15);
+#pragma unroll
+    for (int kc = 0; kc < NC; kc++)
+      if (kc < a.qkv_nc) pv[kc] = __ldcg(p + (size_t)kc * a.qkv_mt * 16);
+  } else {
+    pv[0] = ld_cg(a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * a.hd + row);
+  }
+}
+
+// The value k_merge_q8's store epilogue writes for the row (gemv_q8.cu), bit for bit: the
+// k-chunks in four contiguous quarters, each added in chunk order starting from zero, the
+// quarters added in order, then the bias.
+template <int NC>
+__device__ __forceinline__ float qkv_value(const AttnArgs& a, int row, const float (&pv)[NC]) {
+  if (!a.qkv_part) return pv[0];
+  float q[4];
+#pragma unroll
+  for (int qi = 0; qi < 4; qi++) {
+    const int k0 = qi * a.qkv_nc / 4, k1 = (qi + 1) * a.qkv_nc / 4;
+    float s = 0.f;
+#pragma unroll
+    for (int kc = 0; kc < NC; kc++)
+      if (kc >= k0 && kc < k1) s += pv[kc];
+    q[qi] = s;
+  }
+  float v = ((q[0] + q[1]) + q[2]) + q[3];
+  if (a.qkv_bias) v = __fadd_rn(v, a.qkv_bias[row]);
+  return v;
+}
+
+// Decode append: the token's raw K (kbuf) is normed and rotated, K and V are stored at
+// position pos of its sequence, and kbuf / vbuf are left holding what a later read of the
+// cache returns (rounded to KT). One warp.
+template <int HD, typename KT>
+__device__ void store_new_kv(const AttnArgs& a, int seq, int pos, int g, float* kbuf, float* vbuf, int lane) {
+  norm_rope_head<HD>(kbuf, a.kn, a.eps, a.inv_freq, a.interleaved, pos, lane);
+  const size_t off = kv_off(a, seq, pos, g, HD);
+  for (int e = lane; e < HD; e += 32) {
+    KT* kd = static_cast<KT*>(a.kbase) + off + e;
+    KT* vd = static_cast<KT*>(a.vbase) + off + e;
+    const float v = vbuf[e];
+    kv_store(kd, kbuf[e]);
+    kv_store(vd, v);
+    kbuf[e] = kv_round(kbuf[e], kd);
+    vbuf[e] = kv_round(v, vd);
+  }
+}
+
 // GM: compile-time bound on the query heads per kv head (the loops over heads unroll and
 // predicate on the runtime G <= GM).
 template <int HD, typename KT, int GM>
@@ -155,6 +212,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   const int n_split = gridDim.z;  // the splits of (m, g) are one cluster along z
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.H / a.Hkv;
+  // q of the group's heads, one element per thread and step: these loads do not depend on
+  // the position, so they go out first
+  constexpr int NQJ = (GM * HD + kAttnThreads - 1) / kAttnThreads;
+  constexpr int NKJ = (2 * HD + kAttnThreads - 1) / kAttnThreads;
+  const int nq = G * HD;
+  float qp[NQJ][kQkvChunks];
+#pragma unroll
+  for (int j = 0; j < NQJ; j++) {
+    const int idx = threadIdx.x + j * kAttnThreads;
+    qkv_fetch<kQkvChunks>(a, m, idx < nq ? g * G * HD + idx : -1, qp[j]);
+  }
   const int seq = a.tok_seq ? ld_cg(a.tok_seq + m) : 0;
   const int pos = a.tok_pos ? ld_cg(a.tok_pos + m) : a.const_pos;
   const int n_keys = pos + 1;
@@ -188,15 +256,39 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   // the first chunk's loads go out before the query work, so their latency overlaps it
   if (warp < n_chunks) load_chunk(warp);
 
-  // q heads of this group: norm + rope into shared memory
-  const float* qrow = a.qkv + (size_t)m * (a.H + 2 * a.Hkv) * HD;
-  for (int i = warp; i < G; i += kWarpsA) {
-    const float* src = qrow + (size_t)(g * G + i) * HD;
-    for (int e = lane; e < HD; e += 32) qs[i][e] = ld_cg(src + e);
-    __syncwarp();
-    norm_rope_head<HD>(qs[i], a.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
+  // the new token's raw K and V, for the CTA that appends them
+  float kp[NKJ][kQkvChunks];
+#pragma unroll
+  for (int j = 0; j < NKJ; j++) {
+    const int idx = threadIdx.x + j * kAttnThreads;
+    const int row = !own_new || idx >= 2 * HD ? -1
+                    : idx < HD               ? (a.H + g) * HD + idx
+                                             : (a.H + a.Hkv + g) * HD + (idx - HD);
+    qkv_fetch<kQkvChunks>(a, m, row, kp[j]);
   }
-  if (own_new && warp == kWarpsA - 1) append_kv<HD, KT>(a, m, seq, pos, g, kbuf, lane, vbuf);
+  float* qflat = &qs[0][0];  // head i, element e at i * HD + e
+#pragma unroll
+  for (int j = 0; j < NQJ; j++) {
+    const int idx = threadIdx.x + j * kAttnThreads;
+    if (idx < nq) qflat[idx] = qkv_value<kQkvChunks>(a, g * G * HD + idx, qp[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < NKJ; j++) {
+    const int idx = threadIdx.x + j * kAttnThreads;
+    if (own_new && idx < 2 * HD) {
+      if (idx < HD)
+        kbuf[idx] = qkv_value<kQkvChunks>(a, (a.H + g) * HD + idx, kp[j]);
+      else
+        vbuf[idx - HD] = qkv_value<kQkvChunks>(a, (a.H + a.Hkv + g) * HD + (idx - HD), kp[j]);
+    }
+  }
+  __syncthreads();
+
+  // q heads of this group: norm + rope in shared memory; the appending CTA's last warp
+  // stores the new K / V
+  for (int i = warp; i < G; i += kWarpsA)
+    norm_rope_head<HD>(qs[i], a.qn, a.eps, a.inv_freq, a.interleaved, pos, lane);
+  if (own_new && warp == kWarpsA - 1) store_new_kv<HD, KT>(a, seq, pos, g, kbuf, vbuf, lane);
   __syncthreads();
 
   float qv[GM][EPL];

@@ -506,6 +506,7 @@ cudaError_t dispatch_m(const GemvArgs& a, Epi epi, cudaStream_t st) {
 cudaError_t launch_gemv(const GemvArgs& a, Epi epi, cudaStream_t st) {
   if (a.M < 1 || a.M > kMaxPrefillTok || a.n_range + a.n_extra < 1) return cudaErrorInvalidValue;
   if (a.w.dtype == SX_DTYPE_Q8_0 || a.w.dtype == kDtypeQ4KT) return launch_gemv_q8(a, epi, st);
+  if (epi == EPI_NONE) return cudaErrorInvalidValue;  // the row-layout kernel has no partials to leave
   // x and the row partial sums of all M tokens live in shared memory, sized by the
   // kernel's template M (1, 2, 4 or 8): split the tokens into launches that fit
   const size_t K = (size_t)a.w.cols;

@@ -71,6 +71,83 @@ __device__ __forceinline__ void load_item(const uint8_t* W, const Q8Geo& g, int 
   }
 }
 
+// RMSNorm denominators of the M rows of x over K: each thread sums the squares of k = tid,
+// tid + 256, ... in k order, then the warps are added in order (the register kernel's order).
+// KT > 0 loads KT elements per token and thread before the first is used, so K <= KT * 256
+// costs one round trip to L2 (the guarded loads past K add exact zeros); KT = 0 keeps a
+// four-step unrolled loop, for kernels without the registers to hold more loads.
+template <int M, int KT>
+__device__ __forceinline__ void rms_dens(const GemvArgs& a, int K, float (&red)[kWarps][M], float (&den)[M], int warp,
+                                         int lane) {
+  float ss[M];
+#pragma unroll
+  for (int m = 0; m < M; m++) ss[m] = 0.f;
+  if constexpr (KT > 0) {
+    for (int k0 = threadIdx.x; k0 < K; k0 += KT * kThreads) {
+      float v[KT][M];
+#pragma unroll
+      for (int j = 0; j < KT; j++) {
+        const int k = k0 + j * kThreads;
+#pragma unroll
+        for (int m = 0; m < M; m++) v[j][m] = (k < K && m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < KT; j++)
+#pragma unroll
+        for (int m = 0; m < M; m++) ss[m] = fmaf(v[j][m], v[j][m], ss[m]);
+    }
+  } else {
+#pragma unroll(M <= 8 ? 4 : 1)
+    for (int k = threadIdx.x; k < K; k += kThreads)
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
+        ss[m] = fmaf(v, v, ss[m]);
+      }
+  }
+#pragma unroll
+  for (int m = 0; m < M; m++) {
+    const float t = warp_sum(ss[m]);
+    if (lane == 0) red[warp][m] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < M) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
+    den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)K), a.eps));
+  }
+  __syncthreads();
+}
+
+// x (and gain) of one batch of (block, token) units of the limb split: unit u0 + j * kWarps
+// is block b_lo + u / M, token u % M, lane = column within the block. The gains are weights,
+// so their loads may go out before the grid dependency wait; x only after it.
+template <int LB, int M>
+__device__ __forceinline__ void limb_gains(const GemvArgs& a, int K, int b_lo, int n_units, int u0, int lane,
+                                           float (&gv)[LB]) {
+#pragma unroll
+  for (int j = 0; j < LB; j++) {
+    const int u = u0 + j * kWarps, m = u % M, k = (b_lo + u / M) * 32 + lane;
+    gv[j] = (u < n_units && m < a.M && a.norm_w) ? a.norm_w[k] : 0.f;
+  }
+}
+template <int LB, int M>
+__device__ __forceinline__ void limb_x(const GemvArgs& a, int K, int b_lo, int n_units, int u0, int lane,
+                                       float (&xv)[LB]) {
+#pragma unroll
+  for (int j = 0; j < LB; j++) {
+    const int u = u0 + j * kWarps, m = u % M, k = (b_lo + u / M) * 32 + lane;
+    xv[j] = (u < n_units && m < a.M) ? ld_cg(a.x + (size_t)m * K + k) : 0.f;
+  }
+}
+
+// The decode prologue's shape per kernel (registers allow it at 80 per thread for Q8_0 up to
+// two tokens, at 128 for Q4_K up to eight): RMSNorm loads per token and thread in one pass
+// (rms_dens; 0 = the unrolled loop) and whether the first limb batch's loads go out with them
+__host__ __device__ constexpr int rms_kt_q8(int M) { return M == 1 ? 16 : M == 2 ? 4 : 0; }
+__host__ __device__ constexpr int rms_kt_q4k(int M) { return M == 1 ? 16 : M <= 4 ? 8 : M <= 8 ? 4 : 0; }
+
 // Up to 8 tokens (decode) at three CTAs per SM; prefill chunks of 16..64 tokens hold one
 // accumulator pair per token pair and run one CTA per SM.
 template <int M>
@@ -94,54 +171,35 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   int kc = (int)(w0 / g.n_vt), vt = (int)(w0 % g.n_vt), left = (int)(w1 - w0);
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
 
+  // x limbs of this CTA's blocks, one warp per (block, token) unit, in batches of up to 8
+  // units per warp whose loads all go out before the first is used
+  constexpr int LB = limb_batch(M);
+  const int n_units = (b_hi - b_lo) * M;
+  float xv[LB], gv[LB];
+
+  constexpr bool early = rms_kt_q8(M) > 0;
+
   pdl_launch_dependents();
-  // The first item's weights do not depend on the previous kernel: request them now.
+  // The first item's weights and the first batch's gains do not depend on the previous
+  // kernel: request them now.
   Item it;
   if (left > 0) load_item(W, g, vt_tile(a, g, vt), kc, lane, it);
+  if (early) limb_gains<LB, M>(a, g.K, b_lo, n_units, warp, lane, gv);
   pdl_wait();
+  // the first batch's x goes out together with the RMSNorm loads: one round trip for both
+  if (early) limb_x<LB, M>(a, g.K, b_lo, n_units, warp, lane, xv);
 
   // ---- RMSNorm denominators over the full K (same order as the register kernel) ----
-  if (a.norm_w) {
-    float ss[M];
-#pragma unroll
-    for (int m = 0; m < M; m++) ss[m] = 0.f;
-#pragma unroll(M <= 8 ? 4 : 1)
-    for (int k = threadIdx.x; k < g.K; k += kThreads)
-#pragma unroll
-      for (int m = 0; m < M; m++) {
-        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
-        ss[m] = fmaf(v, v, ss[m]);
-      }
-#pragma unroll
-    for (int m = 0; m < M; m++) {
-      const float t = warp_sum(ss[m]);
-      if (lane == 0) red[warp][m] = t;
-    }
-    __syncthreads();
-    if (threadIdx.x < M) {
-      float t = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
-      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)g.K), a.eps));
-    }
-    __syncthreads();
-  }
+  if (a.norm_w) rms_dens<M, rms_kt_q8(M)>(a, g.K, red, den, warp, lane);
 
-  // ---- x limbs of this CTA's blocks: one warp per (block, token) ----
-  // batches of up to 8 units per warp: every load of a batch goes out before the first is
-  // used, so the split costs one round trip to L2 per batch instead of one per unit
-  const int n_units = (b_hi - b_lo) * M;
-  for (int u0 = warp; u0 < n_units; u0 += limb_batch(M) * kWarps) {
-    float xv[limb_batch(M)], gv[limb_batch(M)];
-#pragma unroll
-    for (int j = 0; j < limb_batch(M); j++) {
-      const int u = u0 + j * kWarps, m = u % M, k = (b_lo + u / M) * 32 + lane;
-      const bool ok = u < n_units && m < a.M;
-      xv[j] = ok ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
-      gv[j] = (ok && a.norm_w) ? a.norm_w[k] : 0.f;
+  // ---- x limbs ----
+  for (int u0 = warp; u0 < n_units; u0 += LB * kWarps) {
+    if (!early || u0 != warp) {
+      limb_gains<LB, M>(a, g.K, b_lo, n_units, u0, lane, gv);
+      limb_x<LB, M>(a, g.K, b_lo, n_units, u0, lane, xv);
     }
 #pragma unroll
-    for (int j = 0; j < limb_batch(M); j++) {
+    for (int j = 0; j < LB; j++) {
     const int u = u0 + j * kWarps;
     if (u >= n_units) break;
     const int bi = u / M, m = u % M;
@@ -279,6 +337,10 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
   int kc = (int)(w0 / g.n_vt), vt = (int)(w0 % g.n_vt), left = (int)(w1 - w0);
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
 
+  constexpr int LB = limb_batch(M);
+  const int n_units = (b_hi - b_lo) * M;
+  float xv[LB], gv[LB];
+
   pdl_launch_dependents();
   // two items in registers: the next one loads while this one is multiplied
   ItemQ4 it0, it1;
@@ -287,49 +349,21 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
     const int vt1 = vt + 1 == g.n_vt ? 0 : vt + 1, kc1 = vt + 1 == g.n_vt ? kc + 1 : kc;
     load_item_q4(W, g, g.t_first + vt1, kc1, lane, it1);
   }
+  constexpr bool early = rms_kt_q4k(M) > 0;
+  if (early) limb_gains<LB, M>(a, g.K, b_lo, n_units, warp, lane, gv);
   pdl_wait();
+  if (early) limb_x<LB, M>(a, g.K, b_lo, n_units, warp, lane, xv);  // with the RMSNorm loads, as k_gemv_q8
 
-  if (a.norm_w) {  // RMSNorm denominators, as k_gemv_q8
-    float ss[M];
-#pragma unroll
-    for (int m = 0; m < M; m++) ss[m] = 0.f;
-#pragma unroll(M <= 8 ? 4 : 1)
-    for (int k = threadIdx.x; k < g.K; k += kThreads)
-#pragma unroll
-      for (int m = 0; m < M; m++) {
-        const float v = (m < a.M) ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
-        ss[m] = fmaf(v, v, ss[m]);
-      }
-#pragma unroll
-    for (int m = 0; m < M; m++) {
-      const float t = warp_sum(ss[m]);
-      if (lane == 0) red[warp][m] = t;
-    }
-    __syncthreads();
-    if (threadIdx.x < M) {
-      float t = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; w++) t += red[w][threadIdx.x];
-      den[threadIdx.x] = sqrtf(__fadd_rn(__fdiv_rn(t, (float)g.K), a.eps));
-    }
-    __syncthreads();
-  }
+  if (a.norm_w) rms_dens<M, rms_kt_q4k(M)>(a, g.K, red, den, warp, lane);
 
   // x limbs (as k_gemv_q8) and the block sums of x, one warp per (block, token)
-  // batches of up to 8 units per warp: every load of a batch goes out before the first is
-  // used, so the split costs one round trip to L2 per batch instead of one per unit
-  const int n_units = (b_hi - b_lo) * M;
-  for (int u0 = warp; u0 < n_units; u0 += limb_batch(M) * kWarps) {
-    float xv[limb_batch(M)], gv[limb_batch(M)];
-#pragma unroll
-    for (int j = 0; j < limb_batch(M); j++) {
-      const int u = u0 + j * kWarps, m = u % M, k = (b_lo + u / M) * 32 + lane;
-      const bool ok = u < n_units && m < a.M;
-      xv[j] = ok ? ld_cg(a.x + (size_t)m * g.K + k) : 0.f;
-      gv[j] = (ok && a.norm_w) ? a.norm_w[k] : 0.f;
+  for (int u0 = warp; u0 < n_units; u0 += LB * kWarps) {
+    if (!early || u0 != warp) {
+      limb_gains<LB, M>(a, g.K, b_lo, n_units, u0, lane, gv);
+      limb_x<LB, M>(a, g.K, b_lo, n_units, u0, lane, xv);
     }
 #pragma unroll
-    for (int j = 0; j < limb_batch(M); j++) {
+    for (int j = 0; j < LB; j++) {
     const int u = u0 + j * kWarps;
     if (u >= n_units) break;
     const int bi = u / M, m = u % M;
@@ -452,7 +486,6 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
 template <int M, int EPI>
 __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo g) {
   pdl_launch_dependents();
-  pdl_wait();
   constexpr int R = EPI == EPI_SWIGLU ? 8 : 16;  // units per tile and token
   const int lane = threadIdx.x & 31, q4 = lane & 3;
   const long long u = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
@@ -460,6 +493,26 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
   const int vt = live ? (int)(u / (R * M)) : 0;
   const int m = live ? (int)((u / R) % M) : 0;
   const int r = live ? (int)(u % R) : 0;
+  const bool lead = live && q4 == 0 && m < a.M;
+  // the output row of a non-SwiGLU unit; its bias (a weight) is requested before the wait,
+  // and the residual of an add together with the partials, after it
+  int pr = 0;
+  bool valid = false;
+  if constexpr (EPI != EPI_SWIGLU) {
+    if (vt < g.n_rt) {
+      pr = (g.t_first + vt) * 16 + r;
+      valid = pr >= a.row_base && pr < a.row_base + a.n_range;
+    } else {
+      pr = a.extra[vt - g.n_rt];
+      valid = (pr & 15) == r;
+    }
+    valid = valid && lead;
+  }
+  const float bv = (valid && a.bias) ? a.bias[pr] : 0.f;
+  pdl_wait();
+  float res = 0.f;
+  if constexpr (EPI == EPI_ADD)
+    if (valid) res = ld_cg(a.y + (size_t)m * a.ldy + pr);
   float s0 = 0.f, s1 = 0.f;
   if (live) {
     const float* p = a.part + ((size_t)vt * g.nc * M + m) * 16 + r;
@@ -477,24 +530,13 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
   const float t1 = ((__shfl_sync(0xffffffffu, s1, base) + __shfl_sync(0xffffffffu, s1, base + 1)) +
                     __shfl_sync(0xffffffffu, s1, base + 2)) +
                    __shfl_sync(0xffffffffu, s1, base + 3);
-  const bool lead = live && q4 == 0 && m < a.M;
   if constexpr (EPI == EPI_SWIGLU) {
     // tile j holds gate rows 8j..8j+7 (tile rows 0-7) and up rows 8j..8j+7 (rows 8-15)
     const int j = (g.t_first + vt) * 8 + r;
     if (lead && j < a.n_range / 2) a.y[(size_t)m * a.ldy + j] = __fmul_rn(silu_f(t0), t1);
   } else {
-    int pr;
-    bool valid;
-    if (vt < g.n_rt) {
-      pr = (g.t_first + vt) * 16 + r;
-      valid = pr >= a.row_base && pr < a.row_base + a.n_range;
-    } else {
-      pr = a.extra[vt - g.n_rt];
-      valid = (pr & 15) == r;
-    }
-    valid = valid && lead;
     float v = t0;
-    if (valid && a.bias) v = __fadd_rn(v, a.bias[pr]);
+    if (valid && a.bias) v = __fadd_rn(v, bv);
     if constexpr (EPI == EPI_ARGMAX) {
       unsigned long long key = 0ull;
       if (valid) {
@@ -512,7 +554,7 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
     } else if (valid) {
       float* dst = a.y + (size_t)m * a.ldy + pr;
       if constexpr (EPI == EPI_ADD)
-        *dst = __fadd_rn(ld_cg(dst), v);
+        *dst = __fadd_rn(res, v);
       else
         *dst = v;
     }
@@ -683,6 +725,7 @@ cudaError_t launch_epilogue(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStre
     return cudaLaunchKernelEx(&cfg2, k_merge_q8_tp<M>, a, g);
   }
   switch (epi) {
+    case EPI_NONE: return cudaSuccess;  // the consumer adds the partials itself
     case EPI_STORE: return launch_merge<M, EPI_STORE>(a, g, st);
     case EPI_ADD: return launch_merge<M, EPI_ADD>(a, g, st);
     case EPI_SWIGLU: return launch_merge<M, EPI_SWIGLU>(a, g, st);

@@ -841,6 +841,25 @@ int try_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
   return 1;
 }
 
+// Decode steps leave the wqkv GEMV's k-chunk partials to the attention kernel, which adds
+// them in the merge kernel's order (bit-identical), so the merge launch drops out of every
+// layer. SYRINX_QKV_MERGE=1 keeps the separate merge (for measurement).
+bool qkv_fold_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SYRINX_QKV_MERGE");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
+// k-chunks of the wqkv GEMV when the decode attention can add its partials (0: it cannot)
+int qkv_fold_chunks(const DevMat& w, int M, bool append) {
+  if (!append || M > kMaxTok || !qkv_fold_enabled()) return 0;
+  if (w.dtype != SX_DTYPE_Q8_0 && w.dtype != kDtypeQ4KT) return 0;
+  const int nc = (int)((w.cols / 32 + 7) / 8);  // 8 blocks of 32 per k-chunk (gemv_q8.cu)
+  return nc <= kQkvChunks ? nc : 0;
+}
+
 // One transformer stack over M tokens. resid [M][dim] is updated in place.
 int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos,
               int const_pos, bool append) {
@@ -865,10 +884,19 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     g.ldy = qkv_w;
     g.M = M;
     g.n_range = qkv_w;
-    SX_RC(gemv(g, EPI_STORE, s));
+    const int fold_nc = qkv_fold_chunks(L.wqkv, M, append);
+    SX_RC(gemv(g, fold_nc ? EPI_NONE : EPI_STORE, s));
 
     AttnArgs a;
     a.qkv = s->xqkv;
+    if (fold_nc) {
+      a.qkv_part = s->q8_part;
+      a.qkv_nc = fold_nc;
+      int mt = 1;
+      while (mt < M) mt <<= 1;
+      a.qkv_mt = mt;
+      a.qkv_bias = L.bqkv;
+    }
     a.out = s->attn;
     uint8_t* base = (fast ? s->fkv : s->kv) + l * layer_elems * s->kv_elem;
     a.kbase = base;

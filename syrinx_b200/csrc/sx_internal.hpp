@@ -39,6 +39,7 @@ constexpr int kMaxPrefillTok = 64;  // tokens per prefill chunk (max tokens per 
 constexpr int kAttnThreads = 256;  // 8 warps per attention CTA
 constexpr int kMaxCluster = 8;     // max splits of the attention key axis (one portable cluster)
 constexpr int kMaxGroup = 8;      // max query heads per kv head handled in one CTA
+constexpr int kQkvChunks = 16;    // max wqkv k-chunks the decode attention adds itself (dim <= 4096)
 constexpr int kMaxStops = 256;    // stop ids; more than 4 only right next to the semantic range
 
 // The stop ids [stop_token_id, +num_stop_tokens) continue the semantic range (or end right
@@ -104,6 +105,8 @@ enum Epi : int {
   EPI_ADD = 1,     // y[m][row] = y[m][row] + (acc (+ bias[row]))   (residual add)
   EPI_SWIGLU = 2,  // y[m][j] = silu(gate_j) * up_j, pairs as the w1/w3 interleave places them
   EPI_ARGMAX = 3,  // logits (stored if y != null) + packed argmax over allowed rows
+  EPI_NONE = 4,    // Q8_0 / Q4_K records only: partials, no merge launch; the consumer adds
+                   // the k-chunks itself (decode attention reading the wqkv partials)
 };
 
 // Tensor parallelism: one process per GPU; the wo / w2 residual merges exchange per-rank
@@ -171,6 +174,13 @@ struct AttnArgs {
   int n_split = 1;  // splits of the key axis = cluster size (<= kMaxCluster)
   int append = 1;  // 1: this launch appends each token's own K/V (decode)
   int M = 1;
+  // Decode: when non-null, q|k|v come from the wqkv GEMV's k-chunk partials
+  // [tile][qkv_nc][qkv_mt][16] (EPI_NONE), added here in k_merge_q8's order, plus qkv_bias,
+  // instead of from the merged rows in qkv.
+  const float* qkv_part = nullptr;
+  int qkv_nc = 0;  // k-chunks of the wqkv GEMV (<= kQkvChunks)
+  int qkv_mt = 1;  // its template token count (the power of two >= M)
+  const float* qkv_bias = nullptr;
 };
 
 // ---- launchers (stream-ordered, programmatic dependent launch enabled) ----------------
