@@ -114,12 +114,14 @@ class Clocks:
 def kernels_per_frame(cfg, stack: bool = True) -> int:
     """Kernel launches in one greedy frame graph (mirrors the sequence in model.cu). A Q8_0
     GEMV is two launches: k_gemv_q8 and its k_merge_q8, except the decode wqkv GEMV, whose
-    partials the attention kernel adds (one launch, unless SYRINX_QKV_MERGE=1). With the
+    partials the attention kernel adds (one launch, unless SYRINX_QKV_MERGE=1), and the
+    one-token w1|w3 GEMV, whose partials the w2 GEMV adds (unless SYRINX_GLU_MERGE=1). With the
     persistent decode kernel a whole stack (36 slow layers, or the 4 fast layers of one
     codebook step) is one launch."""
     gemv = 2
     qkv = 2 if os.environ.get("SYRINX_QKV_MERGE", "0") == "1" else 1
-    per_layer = qkv + 3 * gemv + 1  # wqkv, wo, w1|w3, w2 + attention
+    w13 = 2 if os.environ.get("SYRINX_GLU_MERGE", "0") == "1" else 1
+    per_layer = qkv + w13 + 2 * gemv + 1  # wqkv, w1|w3, wo, w2 + attention
     n = gemv + 1  # semantic head, take_semantic
     if cfg.has_fast:
         C = cfg.num_codebooks
@@ -192,7 +194,11 @@ def bench_device(args):
     peak, peak_kind = peaks()
     n_prof = 4 * cfg.slow.n_layer
     d, F = cfg.slow.dim, cfg.slow.intermediate_size
+    # kinds: 0 wqkv, 1 wo, 2 w1|w3 + its SwiGLU merge, 3 w2, 4 w1|w3 alone as the one-token
+    # chain runs it (its SwiGLU is formed by the w2 GEMV)
     kinds = {0: cfg.slow.qkv_rows * d, 1: d * cfg.slow.n_head * cfg.slow.head_dim, 2: 2 * F * d, 3: d * F}
+    if os.environ.get("SYRINX_GLU_MERGE", "0") != "1":
+        kinds[4] = 2 * F * d
     gemv = {}
     for kind, nw in kinds.items():
         be.profile_gemv(kind, cfg.slow.n_layer)  # warm
@@ -205,8 +211,12 @@ def bench_device(args):
         per = s2.elapsed_time(e2) / n_prof
         gemv[kind] = (nw * 34 / 32, per)
     # the largest per-layer matrix (w1|w3, 52.9 MB) is the dominant kernel of the step
-    bytes_w13, ms_w13 = gemv[2]
+    dom = 4 if 4 in gemv else 2
+    bytes_w13, ms_w13 = gemv[dom]
     achieved = bytes_w13 / (ms_w13 * 1e-3) / 1e9
+    dom_name = ("k_gemv_q8<1>: Q8_0 w1|w3 at M=1, partials only, as the one-token chain runs it (its SwiGLU "
+                "merge is formed by the w2 GEMV)" if dom == 4 else
+                "k_gemv_q8<1> + k_merge_q8<1,SwiGLU>: Q8_0 w1|w3 at M=1 (timed as the pair)")
 
     # ---- e2e: the per-frame public call with host buffers (H2D frame in, D2H frame out) ----
     pin_in = torch.empty(cfg.frame_width, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
@@ -267,12 +277,13 @@ def bench_device(args):
             "frac_of_peak_kv_bf16": round(fb_bf16["total"] * value / world / (peak * 1e9), 4),
             "note": "semantic-only head (4097 rows) counted, as streamed; the session's KV cache is f32 "
                     "(bytes_per_frame), the kv_bf16 figures count the same KV at bf16"},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv_q8<1> + k_merge_q8<1,SwiGLU>: Q8_0 w1|w3 at M=1 (timed as the pair)",
+        "roofline": {"bound": "hbm", "kernel": dom_name,
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": W13_DRAM_BYTES,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                      "algorithmic_bytes": int(bytes_w13),
                      "per_kind_ms": {k: round(v[1], 5) for k, v in gemv.items()},
+                     "pair_with_merge_frac": round(gemv[2][0] / (gemv[2][1] * 1e-3) / 1e9 / peak, 4),
                      "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
         "e2e": {"value": round(K_e2e * world / (ms_e2e * 1e-3), 2), "unit": "frames/s",
                 "h2d_bytes_per_step": int(cfg.frame_width * 4), "d2h_bytes_per_step": int(cfg.frame_width * 4),

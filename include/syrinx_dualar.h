@@ -301,7 +301,8 @@ int sx_lm_step_embeds(sx_session* s, const float* embeds, int32_t t_new, float* 
 /* ---- profiling ------------------------------------------------------------------------ */
 
 /* Enqueue n_launches batch-1 decode GEMVs of one slow-layer matrix kind (0 wqkv,
- * 1 wo, 2 w1|w3 with SwiGLU, 3 w2) on the session stream, cycling through the layers so
+ * 1 wo, 2 w1|w3 with SwiGLU, 3 w2, 4 w1|w3 alone as a one-token step runs it: partials
+ * only, the SwiGLU formed by the next w2 GEMV) on the session stream, cycling through the layers so
  * every launch streams its weights from HBM. No host synchronization: bracket with CUDA
  * events on the session stream to time the kernel alone. Requires a prefilled session. */
 int sx_profile_gemv(sx_session* s, int32_t kind, int32_t n_launches);

@@ -148,6 +148,30 @@ __device__ __forceinline__ void limb_x(const GemvArgs& a, int K, int b_lo, int n
 __host__ __device__ constexpr int rms_kt_q8(int M) { return M == 1 ? 16 : M == 2 ? 4 : 0; }
 __host__ __device__ constexpr int rms_kt_q4k(int M) { return M == 1 ? 16 : M <= 4 ? 8 : M <= 8 ? 4 : 0; }
 
+// x[j] of a w2 GEMV fed by the w1|w3 partials (GemvArgs::glu_part), feature j = 32 (b_lo + bi)
+// + lane: tile 4 (b_lo + bi) + lane / 8 holds its gate (row lane % 8) and up (row 8 + lane % 8)
+// partials, staged in shared memory from tile 4 b_lo on. Added exactly as k_merge_q8's SwiGLU
+// epilogue adds them: four contiguous quarters of the k-chunks, each in order from zero, the
+// quarters in order, then silu(gate) * up.
+__device__ __forceinline__ float glu_value(const float* stage, int bi, int lane, int nc) {
+  const float* p = stage + (size_t)(bi * 4 + (lane >> 3)) * nc * 16 + (lane & 7);
+  float tg[4], tu[4];
+#pragma unroll
+  for (int qi = 0; qi < 4; qi++) {
+    const int k0 = qi * nc / 4, k1 = (qi + 1) * nc / 4;
+    float s0 = 0.f, s1 = 0.f;
+    for (int kc = k0; kc < k1; kc++) {
+      s0 += p[kc * 16];
+      s1 += p[kc * 16 + 8];
+    }
+    tg[qi] = s0;
+    tu[qi] = s1;
+  }
+  const float t0 = ((tg[0] + tg[1]) + tg[2]) + tg[3];
+  const float t1 = ((tu[0] + tu[1]) + tu[2]) + tu[3];
+  return __fmul_rn(silu_f(t0), t1);
+}
+
 // Up to 8 tokens (decode) at three CTAs per SM; prefill chunks of 16..64 tokens hold one
 // accumulator pair per token pair and run one CTA per SM.
 template <int M>
@@ -164,9 +188,14 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   const long long c1 = (long long)(blockIdx.x + 1) * I / gridDim.x;
   const int kc_lo = (int)(c0 / g.n_vt), kc_hi = c1 > c0 ? (int)((c1 - 1) / g.n_vt) : kc_lo;
   const int b_lo = kc_lo * kCB, b_hi = min(g.nb, (kc_hi + 1) * kCB);
-  // shared: B fragments [block - b_lo][NP][32 lanes] | block scales of x [block - b_lo][M]
-  uint2* bfr = reinterpret_cast<uint2*>(smem);
-  float* sxs = reinterpret_cast<float*>(smem + (size_t)(b_hi - b_lo) * NP * 256);
+  // one token: a w2 GEMV may form its x from the w1|w3 partials (glu_value)
+  const bool glu = M == 1 && a.glu_part != nullptr;
+  const int stage_f = glu ? (b_hi - b_lo) * 4 * a.glu_nc * 16 : 0;  // floats
+  // shared: staged w1|w3 partials [4 (block - b_lo)][glu_nc][16] (glu only) | B fragments
+  // [block - b_lo][NP][32 lanes] | block scales of x [block - b_lo][M]
+  float* stage = reinterpret_cast<float*>(smem);
+  uint2* bfr = reinterpret_cast<uint2*>(smem + (size_t)stage_f * 4);
+  float* sxs = reinterpret_cast<float*>(smem + (size_t)stage_f * 4 + (size_t)(b_hi - b_lo) * NP * 256);
   const long long w0 = c0 + (c1 - c0) * warp / kWarps, w1 = c0 + (c1 - c0) * (warp + 1) / kWarps;
   int kc = (int)(w0 / g.n_vt), vt = (int)(w0 % g.n_vt), left = (int)(w1 - w0);
   const uint8_t* W = static_cast<const uint8_t*>(a.w.q);
@@ -186,8 +215,15 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   if (left > 0) load_item(W, g, vt_tile(a, g, vt), kc, lane, it);
   if (early) limb_gains<LB, M>(a, g.K, b_lo, n_units, warp, lane, gv);
   pdl_wait();
-  // the first batch's x goes out together with the RMSNorm loads: one round trip for both
-  if (early) limb_x<LB, M>(a, g.K, b_lo, n_units, warp, lane, xv);
+  if (glu) {  // the w1|w3 partials of this CTA's blocks: one contiguous run, straight to shared memory
+    const float* src = a.glu_part + (size_t)b_lo * 4 * a.glu_nc * 16;
+    for (int i = threadIdx.x; i < stage_f / 4; i += kThreads) cp_async16(stage + 4 * i, src + 4 * i);
+    cp_async_wait_all();
+    __syncthreads();
+  } else if (early) {
+    // the first batch's x goes out together with the RMSNorm loads: one round trip for both
+    limb_x<LB, M>(a, g.K, b_lo, n_units, warp, lane, xv);
+  }
 
   // ---- RMSNorm denominators over the full K (same order as the register kernel) ----
   if (a.norm_w) rms_dens<M, rms_kt_q8(M)>(a, g.K, red, den, warp, lane);
@@ -196,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   for (int u0 = warp; u0 < n_units; u0 += LB * kWarps) {
     if (!early || u0 != warp) {
       limb_gains<LB, M>(a, g.K, b_lo, n_units, u0, lane, gv);
-      limb_x<LB, M>(a, g.K, b_lo, n_units, u0, lane, xv);
+      if (!glu) limb_x<LB, M>(a, g.K, b_lo, n_units, u0, lane, xv);
     }
 #pragma unroll
     for (int j = 0; j < LB; j++) {
@@ -205,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
     const int bi = u / M, m = u % M;
     float v = 0.f;
     if (m < a.M) {
-      v = xv[j];
+      v = glu ? glu_value(stage, bi, lane, a.glu_nc) : xv[j];
       if (a.norm_w) v = __fmul_rn(__fdiv_rn(v, den[m]), gv[j]);
     }
     const float mx = warp_max(fabsf(v));
@@ -688,6 +724,7 @@ cudaError_t launch_m(const GemvArgs& a, Epi epi, const Q8Geo& g, cudaStream_t st
     const long long ipc = (I + grid - 1) / grid;
     const long long spans = std::min<long long>(g.nc, (ipc + g.n_vt - 1) / g.n_vt + 1);
     smem = (size_t)spans * kCB * (NP * 256 + M * (q4 ? 8 : 4));
+    if (a.glu_part) smem += (size_t)spans * kCB * 4 * a.glu_nc * 64;  // staged w1|w3 partials
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -765,6 +802,9 @@ cudaError_t launch_gemv_q8(const GemvArgs& a, Epi epi, cudaStream_t st) {
   if (a.w.dtype == kDtypeQ4KT && (g.nb % kCB || a.n_extra != 0)) return cudaErrorInvalidValue;
   // the SwiGLU pairing is per tile of the whole interleaved matrix
   if (epi == EPI_SWIGLU && (a.row_base != 0 || a.n_extra != 0)) return cudaErrorInvalidValue;
+  // x from the w1|w3 partials: one token, Q8_0, no RMSNorm, at most kQkvChunks k-chunks
+  if (a.glu_part && (a.M != 1 || a.w.dtype != SX_DTYPE_Q8_0 || a.norm_w || a.glu_nc < 1 || a.glu_nc > kQkvChunks))
+    return cudaErrorInvalidValue;
   int Mt = 1;
   while (Mt < a.M) Mt <<= 1;
   if ((size_t)g.n_vt * g.nc * Mt * 16 > a.part_cap) return cudaErrorInvalidValue;

@@ -546,6 +546,14 @@ int session_create(sx_model* m, int max_batch, int max_ctx, int kv_dtype, sx_ses
     s->tc_scratch_bytes = gemm_tc_scratch_bytes((int)kmax, kMaxPrefillTok);
     if ((rc = dalloc(s->allocs, &s->tc_scratch, std::max<size_t>(s->tc_scratch_bytes, 16)))) return fail(rc);
     if ((rc = dalloc(s->allocs, &s->q8_part, std::max<size_t>(cap, 1)))) return fail(rc);
+    // one-token w1|w3 partials, kept apart from q8_part because the w2 GEMV that reads them
+    // writes its own partials there
+    size_t cap2 = 0;
+    for (const auto* ls : {&m->slow, &m->fast})
+      for (const DevLayer& L : *ls)
+        if (L.w13.dtype == SX_DTYPE_Q8_0) cap2 = std::max(cap2, q8_part_floats(L.w13, L.w13.rows, 1));
+    s->q8_part2_cap = cap2;
+    if (cap2 && (rc = dalloc(s->allocs, &s->q8_part2, cap2))) return fail(rc);
   }
   {
     int sms = 148;
@@ -728,8 +736,10 @@ int n_split_for(const sx_session* s, int /*M*/, int /*Hkv*/) {
 // Every GEMV gets the session's Q8_0 partial-sum buffer; residual adds of a tensor-parallel
 // model (wo, w2: input columns split over the ranks) also get the exchange communicator.
 int gemv(GemvArgs a, Epi epi, sx_session* s) {
-  a.part = s->q8_part;
-  a.part_cap = s->q8_part_cap;
+  if (!a.part) {  // the session's partial buffer unless the caller chose another
+    a.part = s->q8_part;
+    a.part_cap = s->q8_part_cap;
+  }
   a.err = s->err;
   a.tc_scratch = s->tc_scratch;
   a.tc_scratch_bytes = s->tc_scratch_bytes;
@@ -860,6 +870,27 @@ int qkv_fold_chunks(const DevMat& w, int M, bool append) {
   return nc <= kQkvChunks ? nc : 0;
 }
 
+// One-token steps leave the w1|w3 GEMV's k-chunk partials (in q8_part2) to the w2 GEMV, which
+// forms silu(gate) * up from them in the merge kernel's order (bit-identical), so the SwiGLU
+// merge launch drops out of every layer. SYRINX_GLU_MERGE=1 keeps the separate merge.
+bool glu_fold_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SYRINX_GLU_MERGE");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
+// k-chunks of the w1|w3 GEMV when the w2 GEMV can form its input from their partials (0: no)
+int glu_fold_chunks(const sx_session* s, const DevLayer& L, int M) {
+  if (M != 1 || !glu_fold_enabled() || !s->q8_part2) return 0;
+  if (L.w13.dtype != SX_DTYPE_Q8_0 || L.w2.dtype != SX_DTYPE_Q8_0) return 0;
+  if (L.w13.rows != 2 * L.w2.cols || L.w2.cols % 32) return 0;
+  if (q8_part_floats(L.w13, L.w13.rows, 1) > s->q8_part2_cap) return 0;
+  const int nc = (int)((L.w13.cols / 32 + 7) / 8);
+  return nc <= kQkvChunks ? nc : 0;
+}
+
 // One transformer stack over M tokens. resid [M][dim] is updated in place.
 int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq, const int* tok_pos,
               int const_pos, bool append) {
@@ -945,7 +976,12 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     f.ldy = td.intermediate_size;
     f.M = M;
     f.n_range = 2 * td.intermediate_size;
-    SX_RC(gemv(f, EPI_SWIGLU, s));
+    const int glu_nc = glu_fold_chunks(s, L, M);
+    if (glu_nc) {
+      f.part = s->q8_part2;
+      f.part_cap = s->q8_part2_cap;
+    }
+    SX_RC(gemv(f, glu_nc ? EPI_NONE : EPI_SWIGLU, s));
 
     GemvArgs w2;
     w2.w = L.w2;
@@ -954,6 +990,10 @@ int run_stack(sx_session* s, bool fast, int M, float* resid, const int* tok_seq,
     w2.ldy = td.dim;
     w2.M = M;
     w2.n_range = td.dim;
+    if (glu_nc) {
+      w2.glu_part = s->q8_part2;
+      w2.glu_nc = glu_nc;
+    }
     SX_RC(gemv(w2, EPI_ADD, s));
   }
   return SX_OK;
@@ -1573,8 +1613,8 @@ int run_frames(sx_session* s, int n, int n_frames, int mask_stop, bool sampled, 
 int profile_gemv(sx_session* s, int kind, int n_launches) {
   sx_model* m = s->m;
   const sx_transformer_desc& td = m->d.slow;
-  if (kind < 0 || kind > 3 || n_launches < 0 || m->slow.empty()) {
-    set_error("profile_gemv: kind must be 0..3");
+  if (kind < 0 || kind > 4 || n_launches < 0 || m->slow.empty()) {
+    set_error("profile_gemv: kind must be 0..4");
     return SX_E_INVALID;
   }
   for (int i = 0; i < n_launches; i++) {
@@ -1597,7 +1637,7 @@ int profile_gemv(sx_session* s, int kind, int n_launches) {
       g.y = s->hp;
       g.ldy = td.dim;
       g.n_range = td.dim;
-    } else if (kind == 2) {
+    } else if (kind == 2 || kind == 4) {
       g.w = L.w13;
       g.x = s->h;
       g.norm_w = L.ffn_norm;
@@ -1606,6 +1646,15 @@ int profile_gemv(sx_session* s, int kind, int n_launches) {
       g.ldy = td.intermediate_size;
       g.n_range = 2 * td.intermediate_size;
       epi = EPI_SWIGLU;
+      if (kind == 4) {  // as a one-token step runs it: partials only, the merge left to w2
+        if (!glu_fold_chunks(s, L, 1)) {
+          set_error("profile_gemv: kind 4 needs Q8_0 w1|w3 and w2 with the SwiGLU fold enabled");
+          return SX_E_UNSUPPORTED;
+        }
+        g.part = s->q8_part2;
+        g.part_cap = s->q8_part2_cap;
+        epi = EPI_NONE;
+      }
     } else {
       g.w = L.w2;
       g.x = s->act;

@@ -77,6 +77,8 @@ struct sx_session {
   sx_sampling_params* dparams = nullptr;  // device copy of the sampling parameters
   float* q8_part = nullptr;  // Q8_0 GEMV partial sums [tile][k-chunk][token][16]
   size_t q8_part_cap = 0;    // floats
+  float* q8_part2 = nullptr;  // one-token w1|w3 partials, read by the w2 GEMV that writes q8_part
+  size_t q8_part2_cap = 0;    // floats
   // persistent decode stack scratch: the residual's second buffer, attention split partials,
   // per-chunk sums of squares and the grid barrier counter
   uint8_t* tc_scratch = nullptr;  // tensor-core prefill GEMM: B operands of every k block

@@ -106,7 +106,8 @@ enum Epi : int {
   EPI_SWIGLU = 2,  // y[m][j] = silu(gate_j) * up_j, pairs as the w1/w3 interleave places them
   EPI_ARGMAX = 3,  // logits (stored if y != null) + packed argmax over allowed rows
   EPI_NONE = 4,    // Q8_0 / Q4_K records only: partials, no merge launch; the consumer adds
-                   // the k-chunks itself (decode attention reading the wqkv partials)
+                   // the k-chunks itself (decode attention reading the wqkv partials, the
+                   // one-token w2 GEMV reading the w1|w3 partials)
 };
 
 // Tensor parallelism: one process per GPU; the wo / w2 residual merges exchange per-rank
@@ -146,6 +147,10 @@ struct GemvArgs {
   size_t part_cap = 0;
   // residual add across a tensor-parallel group (EPI_ADD of a K-split matrix, Q8_0 only)
   TpComm tp;
+  // One token, Q8_0, no RMSNorm: x is not read; x[j] = silu(gate_j) * up_j is formed from the
+  // w1|w3 GEMV's partials [tile][glu_nc][1][16] (left by EPI_NONE), added in k_merge_q8's order
+  const float* glu_part = nullptr;
+  int glu_nc = 0;
   int* err = nullptr;  // device error flag (bounded pipeline waits of the tensor-core GEMM)
   uint8_t* tc_scratch = nullptr;  // the tensor-core GEMM's B operands (gemm_tc_scratch_bytes)
   size_t tc_scratch_bytes = 0;
