@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 
 #include "codec.hpp"
@@ -384,13 +385,14 @@ cudaError_t launch_conv_tc(const TcConvArgs& a0, int sms, cudaStream_t st) {
   a.n_kb = (a.R + kKB - 1) / kKB;
   a.bn = kBN;
   a.n_nt = (a.N + kBN - 1) / kBN;
-  static bool attr_set[64] = {false};
+  // the attribute is per device; threads that race here both set it, which is harmless
+  static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
   const int grid = std::max(1, std::min(a.n_mt * a.n_nt, sms));
   k_conv_tc<<<grid, kThreadsTc, kTcSmemBytes, st>>>(a);
