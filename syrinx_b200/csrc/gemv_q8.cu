@@ -124,7 +124,7 @@ __device__ __forceinline__ void rms_dens(const GemvArgs& a, int K, float (&red)[
 // is block b_lo + u / M, token u % M, lane = column within the block. The gains are weights,
 // so their loads may go out before the grid dependency wait; x only after it.
 template <int LB, int M>
-__device__ __forceinline__ void limb_gains(const GemvArgs& a, int K, int b_lo, int n_units, int u0, int lane,
+__device__ __forceinline__ void limb_gains(const GemvArgs& a, int b_lo, int n_units, int u0, int lane,
                                            float (&gv)[LB]) {
 #pragma unroll
   for (int j = 0; j < LB; j++) {
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   // kernel: request them now.
   Item it;
   if (left > 0) load_item(W, g, vt_tile(a, g, vt), kc, lane, it);
-  if (early) limb_gains<LB, M>(a, g.K, b_lo, n_units, warp, lane, gv);
+  if (early) limb_gains<LB, M>(a, b_lo, n_units, warp, lane, gv);
   pdl_wait();
   if (glu) {  // the w1|w3 partials of this CTA's blocks: one contiguous run, straight to shared memory
     const float* src = a.glu_part + (size_t)b_lo * 4 * a.glu_nc * 16;
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 3 : 1) k_gemv_q8(const Gemv
   // ---- x limbs ----
   for (int u0 = warp; u0 < n_units; u0 += LB * kWarps) {
     if (!early || u0 != warp) {
-      limb_gains<LB, M>(a, g.K, b_lo, n_units, u0, lane, gv);
+      limb_gains<LB, M>(a, b_lo, n_units, u0, lane, gv);
       if (!glu) limb_x<LB, M>(a, g.K, b_lo, n_units, u0, lane, xv);
     }
 #pragma unroll
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
     load_item_q4(W, g, g.t_first + vt1, kc1, lane, it1);
   }
   constexpr bool early = rms_kt_q4k(M) > 0;
-  if (early) limb_gains<LB, M>(a, g.K, b_lo, n_units, warp, lane, gv);
+  if (early) limb_gains<LB, M>(a, b_lo, n_units, warp, lane, gv);
   pdl_wait();
   if (early) limb_x<LB, M>(a, g.K, b_lo, n_units, warp, lane, xv);  // with the RMSNorm loads, as k_gemv_q8
 
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, M <= 8 ? 2 : 1) k_gemv_q4k(const Gem
   // x limbs (as k_gemv_q8) and the block sums of x, one warp per (block, token)
   for (int u0 = warp; u0 < n_units; u0 += LB * kWarps) {
     if (!early || u0 != warp) {
-      limb_gains<LB, M>(a, g.K, b_lo, n_units, u0, lane, gv);
+      limb_gains<LB, M>(a, b_lo, n_units, u0, lane, gv);
       limb_x<LB, M>(a, g.K, b_lo, n_units, u0, lane, xv);
     }
 #pragma unroll
