@@ -553,10 +553,26 @@ __global__ void __launch_bounds__(256) k_merge_q8(const GemvArgs a, const Q8Geo 
   if (live) {
     const float* p = a.part + ((size_t)vt * g.nc * M + m) * 16 + r;
     const int k0 = q4 * g.nc / 4, k1 = (q4 + 1) * g.nc / 4;
+    constexpr int KQ = 12;  // a quarter of up to 48 k-chunks (K <= 12288): every load out at once
+    if (k1 - k0 <= KQ) {
+      float v0[KQ], v1[KQ];
+#pragma unroll
+      for (int i = 0; i < KQ; i++) {
+        v0[i] = k0 + i < k1 ? __ldcg(p + (size_t)(k0 + i) * M * 16) : 0.f;
+        v1[i] = EPI == EPI_SWIGLU && k0 + i < k1 ? __ldcg(p + (size_t)(k0 + i) * M * 16 + 8) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < KQ; i++)
+        if (k0 + i < k1) {  // the same additions in the same order as the loop below
+          s0 += v0[i];
+          if (EPI == EPI_SWIGLU) s1 += v1[i];
+        }
+    } else {
 #pragma unroll 4
-    for (int kc = k0; kc < k1; kc++) {
-      s0 += __ldcg(p + (size_t)kc * M * 16);
-      if (EPI == EPI_SWIGLU) s1 += __ldcg(p + (size_t)kc * M * 16 + 8);
+      for (int kc = k0; kc < k1; kc++) {
+        s0 += __ldcg(p + (size_t)kc * M * 16);
+        if (EPI == EPI_SWIGLU) s1 += __ldcg(p + (size_t)kc * M * 16 + 8);
+      }
     }
   }
   const int base = lane & ~3;
