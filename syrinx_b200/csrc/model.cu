@@ -1169,7 +1169,10 @@ int prefill_seq_embeds(sx_session* s, int seq, const float* embeds, int T) {
   return SX_OK;
 }
 
-int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n) {
+// The slow step of n tokens (token i = sequence i), enqueued on the session stream: argument
+// checks, frame and position upload, MCF embed, the slow stack. Nothing waits for the device
+// and the cached lengths do not advance; the caller checks the error flag, then advances them.
+int slow_step_enqueue(sx_session* s, const int* seqs, const uint32_t* frames, int n) {
   const sx_model_desc& d = s->m->d;
   const int width = 1 + d.num_codebooks;
   std::vector<int> ts(n), tp(n);
@@ -1198,7 +1201,11 @@ int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n
   e.h = s->h;
   e.M = n;
   SX_CU(launch_embed(e, s->st));
-  SX_RC(run_stack(s, false, n, s->h, s->tok_seq, s->tok_pos, 0, true));
+  return run_stack(s, false, n, s->h, s->tok_seq, s->tok_pos, 0, true);
+}
+
+int slow_step_seqs(sx_session* s, const int* seqs, const uint32_t* frames, int n) {
+  SX_RC(slow_step_enqueue(s, seqs, frames, n));
   SX_RC(check_err(s));
   for (int i = 0; i < n; i++) s->len[i] += 1;
   return SX_OK;
@@ -1744,16 +1751,20 @@ int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, ui
     set_error("frame_step before prefill");
     return SX_E_STATE;
   }
+  // One synchronisation per frame: the slow step and the front are enqueued back to back and
+  // the error flag is read after the frame (a bad frame still runs the front, whose results
+  // are discarded; the cached length advances only when the step succeeded).
   if (frame_in) {
     const int seq0 = 0;
-    SX_RC(slow_step_seqs(s, &seq0, frame_in, 1));
+    SX_RC(slow_step_enqueue(s, &seq0, frame_in, 1));
   } else {
     const std::vector<int> ts{0}, tp{s->len[0]};
     SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
   }
   SX_RC(greedy_frame_front(s, 1, mask_stop, false));
   SX_CU(cudaMemcpyAsync(frame_out, s->frames, (size_t)width * 4, cudaMemcpyDeviceToHost, s->st));
-  SX_CU(cudaStreamSynchronize(s->st));
+  SX_RC(check_err(s));
+  if (frame_in) s->len[0] += 1;
   if (stopped)
     *stopped = frame_out[0] >= d.stop_token_id && frame_out[0] < d.stop_token_id + (uint32_t)d.num_stop_tokens;
   return SX_OK;

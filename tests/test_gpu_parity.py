@@ -184,6 +184,32 @@ def test_frame_step_and_drive_agree_with_graph_loop(tiny):
     be.close()
 
 
+def test_frame_step_bad_frame_is_an_error_and_keeps_the_length(tiny):
+    """sx_frame_step_greedy reads the device error flag once, after the whole frame: a frame
+    with an out-of-range code returns SX_E_INVALID, leaves the cached length where it was, and
+    the next call continues as if the bad frame had never been given."""
+    cfg, model, _ = tiny
+    prompt = prompt_for(cfg, 10, seed=9)
+    be = sx.B200DualAr(model, max_ctx=64)
+    be.prefill(prompt)
+    f0, _ = be.frame_step_greedy(None, mask_stop=True)
+    n = be.seq_len()
+    bad = f0.copy()
+    bad[1] = cfg.codebook_size + 5
+    with pytest.raises(sx.SyrinxError) as e:
+        be.frame_step_greedy(bad, mask_stop=True)
+    assert e.value.code == -1  # code out of range, reported by the embed kernel's bounds check
+    assert be.seq_len() == n
+    f1, _ = be.frame_step_greedy(f0, mask_stop=True)
+    assert be.seq_len() == n + 1
+    be.reset()
+    be.prefill(prompt)
+    g0, _ = be.frame_step_greedy(None, mask_stop=True)
+    g1, _ = be.frame_step_greedy(g0, mask_stop=True)
+    assert np.array_equal(f0, g0) and np.array_equal(f1, g1)
+    be.close()
+
+
 def test_batched_decode_equals_single(tiny):
     """Sample i of a batch reproduces a batch-1 run (dualar.rs:237-241), with prompts of
     different lengths kept unpadded in the paged cache."""
