@@ -1477,6 +1477,50 @@ int greedy_frame_front(sx_session* s, int n, int mask_stop, bool sampled) {
   return SX_OK;
 }
 
+// Captures what body() enqueues on the session stream into an executable graph.
+template <class F>
+int capture_graph(sx_session* s, F&& body, cudaGraphExec_t* exec) {
+  SX_CU(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+  int rc = body();
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s->st, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error(std::string("graph capture: ") + cudaGetErrorString(e));
+    return SX_E_CUDA;
+  }
+  e = cudaGraphInstantiateWithFlags(exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    set_error(std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return SX_E_CUDA;
+  }
+  return SX_OK;
+}
+
+// sx_frame_step_greedy's frame: the slow step of the frame in s->frames at the position in
+// s->tok_pos (MCF embed, slow stack), then the greedy front (head, first code, fast AR).
+int build_frame_step_graph(sx_session* s, int mask_stop, cudaGraphExec_t* exec) {
+  const int width = 1 + s->m->d.num_codebooks;
+  return capture_graph(
+      s,
+      [&]() -> int {
+        EmbedArgs e = embed_args(s);
+        e.tok_seq = s->tok_seq;
+        e.frames = s->frames;
+        e.frame_stride = width;
+        e.h = s->h;
+        e.M = 1;
+        SX_CU(launch_embed(e, s->st));
+        SX_RC(run_stack(s, false, 1, s->h, s->tok_seq, s->tok_pos, 0, true));
+        return greedy_frame_front(s, 1, mask_stop, false);
+      },
+      exec);
+}
+
 int build_graph(sx_session* s, int n, int mask_stop, bool sampled, cudaGraphExec_t* exec) {
   const sx_model_desc& d = s->m->d;
   const int width = 1 + d.num_codebooks;
@@ -1585,7 +1629,7 @@ int run_frames(sx_session* s, int n, int n_frames, int mask_stop, bool sampled, 
   SX_CU(cudaMemcpyAsync(s->frame_count, zeros.data(), n * 4, cudaMemcpyHostToDevice, s->st));
   GreedyGraph* gg = nullptr;
   for (auto& g : s->graphs)
-    if (g.M == n && g.mask_stop == mask_stop && g.sampled == (int)sampled) gg = &g;
+    if (!g.frame_step && g.M == n && g.mask_stop == mask_stop && g.sampled == (int)sampled) gg = &g;
   if (!gg) {
     GreedyGraph g;
     g.M = n;
@@ -1751,17 +1795,36 @@ int frame_step_greedy(sx_session* s, const uint32_t* frame_in, int mask_stop, ui
     set_error("frame_step before prefill");
     return SX_E_STATE;
   }
-  // One synchronisation per frame: the slow step and the front are enqueued back to back and
+  // One synchronisation per frame: the slow step and the front run as one captured graph and
   // the error flag is read after the frame (a bad frame still runs the front, whose results
   // are discarded; the cached length advances only when the step succeeded).
   if (frame_in) {
-    const int seq0 = 0;
-    SX_RC(slow_step_enqueue(s, &seq0, frame_in, 1));
+    if (s->len[0] + 1 > s->max_ctx) {
+      set_error("frame_step: context exceeds the session's max_ctx");
+      return SX_E_RANGE;
+    }
+    // the frame and its position go to device memory; the captured frame graph reads them
+    const std::vector<int> ts{0}, tp{s->len[0]};
+    SX_CU(cudaMemcpyAsync(s->frames, frame_in, (size_t)width * 4, cudaMemcpyHostToDevice, s->st));
+    SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+    GreedyGraph* gg = nullptr;
+    for (auto& g : s->graphs)
+      if (g.frame_step && g.mask_stop == (mask_stop != 0)) gg = &g;
+    if (!gg) {
+      GreedyGraph g;
+      g.M = 1;
+      g.mask_stop = mask_stop != 0;
+      g.frame_step = 1;
+      SX_RC(build_frame_step_graph(s, g.mask_stop, &g.exec));
+      s->graphs.push_back(g);
+      gg = &s->graphs.back();
+    }
+    SX_CU(cudaGraphLaunch(gg->exec, s->st));
   } else {
     const std::vector<int> ts{0}, tp{s->len[0]};
     SX_RC(upload_tokens(s, s->tok_seq, s->tok_pos, ts, tp));
+    SX_RC(greedy_frame_front(s, 1, mask_stop, false));
   }
-  SX_RC(greedy_frame_front(s, 1, mask_stop, false));
   SX_CU(cudaMemcpyAsync(frame_out, s->frames, (size_t)width * 4, cudaMemcpyDeviceToHost, s->st));
   SX_RC(check_err(s));
   if (frame_in) s->len[0] += 1;

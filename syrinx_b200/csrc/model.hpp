@@ -34,6 +34,7 @@ struct GreedyGraph {
   int M = 0;
   int mask_stop = 0;
   int sampled = 0;  // 1: the device-sampled frame (sx_decode_sample)
+  int frame_step = 0;  // 1: sx_frame_step_greedy's slow step + front (not a decode-loop frame)
 };
 
 struct sx_session {
