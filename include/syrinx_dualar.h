@@ -217,7 +217,11 @@ int sx_fast_expand_greedy(sx_session* s, uint32_t first_code, uint32_t* codes_ou
  * slow_step(frame_in) first; then sample the semantic token from the current logits
  * (constraint = semantic range + stop ids, stop masked when mask_stop), expand it with
  * the fast AR and write the full frame [1+C] (semantic, code0..code_{C-1}) to frame_out.
- * Returns SX_OK; *stopped_out = 1 if the semantic token was a stop id. */
+ * Returns SX_OK; *stopped_out = 1 if the semantic token was a stop id. With a frame, the
+ * device work is one CUDA graph, captured on the session stream by the first such call
+ * (per mask_stop value) and replayed afterwards, with one synchronisation per call. A bad
+ * frame (an id or code out of range) returns SX_E_INVALID and leaves the cached length
+ * unchanged. */
 int sx_frame_step_greedy(sx_session* s, const uint32_t* frame_in, int32_t mask_stop,
                          uint32_t* frame_out, int32_t* stopped_out);
 
