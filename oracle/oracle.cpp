@@ -226,7 +226,7 @@ float dot(const float* a, const float* b, int64_t n) {
 // candle-core 0.8.x is not vendored here, so the published ggml form stands in). Mode B is
 // chaotic in its inputs: a 1-ulp change of the normed activations moves config-1 logits by
 // ~5e-2 (mode A: ~3e-6), so it cannot serve as a parity target for any implementation with
-// another reduction order. Q4_K weights always use mode A here.
+// another reduction order. Mode B for Q4_K weights: linear_q4_k_b below.
 int g_qmode = 0;
 
 void q8_0_quantize_act(const float* x, int64_t K, int8_t* q, float* d) {
@@ -266,12 +266,105 @@ void linear_q8_0_b(const OT& W, const float* b, const float* x, int M, float* y)
   }
 }
 
+// Mode B for Q4_K weights, as candle-core's k-quants restate ggml for the CPU QMatMul (the
+// portable form; candle-core 0.8.x is not vendored, so its published k_quants source stands in).
+// Each activation row is quantized to Q8_K super-blocks of 256 (BlockQ8K::from_float: the
+// element of largest magnitude, with its sign, sets iscale = -128 / max; q = min(127,
+// round(iscale * x)) rounding halves away from zero; d = 1 / iscale kept in f32; bsums = the
+// sums of each 16 consecutive q). Per super-block (BlockQ4K vec_dot): the nibbles widened to
+// int8, int32 lane sums aux[l] += sc_j * (q8 * q4) over the eight lanes of every 8-element
+// group, sumi = sum_j bsums[j] * m_{j/2}; then sums[l] += (d_w * d_x) * aux[l] for each lane
+// and sumf -= (dmin_w * d_x) * sumi, in f32; the row is sumf + (sums[0] + ... + sums[7]).
+struct Q8K {
+  float d = 0.0f;
+  int8_t qs[QK_K];
+  int16_t bsums[QK_K / 16];
+};
+
+void q8_k_quantize_act(const float* x, int64_t K, Q8K* out) {
+  for (int64_t b = 0; b < K / QK_K; b++) {
+    const float* xb = x + b * QK_K;
+    Q8K& y = out[b];
+    float mx = 0.0f, amax = 0.0f;
+    for (int j = 0; j < QK_K; j++)
+      if (amax < std::fabs(xb[j])) {
+        amax = std::fabs(xb[j]);
+        mx = xb[j];
+      }
+    if (amax == 0.0f) {
+      y.d = 0.0f;
+      std::memset(y.qs, 0, sizeof(y.qs));
+      std::memset(y.bsums, 0, sizeof(y.bsums));
+      continue;
+    }
+    const float iscale = -128.0f / mx;
+    for (int j = 0; j < QK_K; j++) y.qs[j] = (int8_t)std::min(127.0f, std::round(iscale * xb[j]));
+    for (int j = 0; j < QK_K / 16; j++) {
+      int32_t sum = 0;
+      for (int i = 0; i < 16; i++) sum += y.qs[16 * j + i];
+      y.bsums[j] = (int16_t)sum;
+    }
+    y.d = 1.0f / iscale;
+  }
+}
+
+void linear_q4_k_b(const OT& W, const float* b, const float* x, int M, float* y) {
+  const int64_t N = W.rows, K = W.cols, nb = K / QK_K;
+  std::vector<Q8K> xq((size_t)M * nb);
+  for (int m = 0; m < M; m++) q8_k_quantize_act(x + (size_t)m * K, K, xq.data() + (size_t)m * nb);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < N; r++) {
+    const uint8_t* row = W.p + (size_t)r * nb * Q4_K_BYTES;
+    for (int m = 0; m < M; m++) {
+      float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      float sumf = 0.0f;
+      for (int64_t bk = 0; bk < nb; bk++) {
+        const uint8_t* blk = row + bk * Q4_K_BYTES;
+        const Q8K& q8 = xq[(size_t)m * nb + bk];
+        uint16_t dh, mh;
+        std::memcpy(&dh, blk, 2);
+        std::memcpy(&mh, blk + 2, 2);
+        const uint8_t* qs = blk + 16;
+        int8_t a[QK_K];
+        for (int j = 0; j < 4; j++)
+          for (int l = 0; l < 32; l++) {
+            a[64 * j + l] = (int8_t)(qs[32 * j + l] & 0xF);
+            a[64 * j + 32 + l] = (int8_t)(qs[32 * j + l] >> 4);
+          }
+        uint8_t sc[8], mn[8];
+        for (int j = 0; j < 8; j++) q4k_scale_min(j, blk + 4, &sc[j], &mn[j]);
+        int32_t sumi = 0;
+        for (int j = 0; j < QK_K / 16; j++) sumi += (int32_t)q8.bsums[j] * (int32_t)mn[j / 2];
+        int32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 8; j++)
+          for (int g = 0; g < 4; g++)
+            for (int l = 0; l < 8; l++) {
+              const int k = 32 * j + 8 * g + l;
+              aux[l] += (int32_t)sc[j] * (int32_t)(int16_t)(q8.qs[k] * a[k]);
+            }
+        const float d = h2f(dh) * q8.d;
+        for (int l = 0; l < 8; l++) sums[l] += d * (float)aux[l];
+        const float dmin = h2f(mh) * q8.d;
+        sumf -= dmin * (float)sumi;
+      }
+      float tot = 0.0f;
+      for (int l = 0; l < 8; l++) tot += sums[l];
+      const float v = sumf + tot;
+      y[(size_t)m * N + r] = b ? v + b[r] : v;
+    }
+  }
+}
+
 // y[M][N] = x[M][K] . W^T (+ b).
 void linear(const OT& W, const OT* bias, const float* x, int M, float* y) {
   const int64_t N = W.rows, K = W.cols;
   const float* b = bias ? (const float*)bias->p : nullptr;
   if (W.dtype == SX_DTYPE_Q8_0 && g_qmode == 1) {
     linear_q8_0_b(W, b, x, M, y);
+    return;
+  }
+  if (W.dtype == SX_DTYPE_Q4_K && g_qmode == 1) {
+    linear_q4_k_b(W, b, x, M, y);
     return;
   }
 #pragma omp parallel
@@ -826,6 +919,16 @@ void oc_linear_q8_0(const float* x, const uint8_t* blocks, int32_t M, int32_t N,
   w.cols = K;
   w.p = blocks;
   w.nbytes = (size_t)N * (K / QK8_0) * Q8_0_BYTES;
+  linear(w, nullptr, x, M, y);
+}
+
+void oc_linear_q4_k(const float* x, const uint8_t* blocks, int32_t M, int32_t N, int32_t K, float* y) {
+  OT w;
+  w.dtype = SX_DTYPE_Q4_K;
+  w.rows = N;
+  w.cols = K;
+  w.p = blocks;
+  w.nbytes = (size_t)N * (K / QK_K) * Q4_K_BYTES;
   linear(w, nullptr, x, M, y);
 }
 

@@ -44,6 +44,8 @@ void oc_set_qmode(int32_t mode);
 int32_t oc_get_qmode(void);
 /* y[M][N] = x[M][K] . W^T for Q8_0 blocks W [N][K/32 blocks], in the current mode. */
 void oc_linear_q8_0(const float* x, const uint8_t* blocks, int32_t M, int32_t N, int32_t K, float* y);
+/* y[M][N] = x[M][K] . W^T for Q4_K blocks W[N][K/256], in the current mode (A or B). */
+void oc_linear_q4_k(const float* x, const uint8_t* blocks, int32_t M, int32_t N, int32_t K, float* y);
 
 /* ---- block formats ---- */
 void oc_q8_0_quantize(const float* x, int64_t n, uint8_t* blocks);       /* n % 32 == 0 */

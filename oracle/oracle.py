@@ -34,6 +34,7 @@ def lib() -> C.CDLL:
             "oc_set_qmode": (None, [C.c_int32]),
             "oc_get_qmode": (C.c_int32, []),
             "oc_linear_q8_0": (None, [_f32p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, _f32p]),
+            "oc_linear_q4_k": (None, [_f32p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, _f32p]),
             "oc_q8_0_quantize": (None, [_f32p, C.c_int64, C.c_void_p]),
             "oc_q8_0_dequantize": (None, [C.c_void_p, C.c_int64, _f32p]),
             "oc_q4_k_dequantize": (None, [C.c_void_p, C.c_int64, _f32p]),
@@ -277,14 +278,24 @@ def set_num_threads(n: int) -> None:
 
 
 def set_qmode(mode: int) -> None:
-    """Quantized matmul numerics for Q8_0 weights: 0 = mode A (exact dequant x f32
-    activations, the default and what the device computes), 1 = mode B (Candle QMatMul /
-    ggml vec_dot_q8_0_q8_0, for analysis)."""
+    """Quantized matmul numerics for Q8_0 and Q4_K weights: 0 = mode A (exact dequant x f32
+    activations, the default and what the device computes), 1 = mode B (Candle QMatMul:
+    activations quantized to Q8_0 / Q8_K, integer block dots; for analysis)."""
     lib().oc_set_qmode(int(mode))
 
 
 def get_qmode() -> int:
     return int(lib().oc_get_qmode())
+
+
+def linear_q4_k(x: np.ndarray, blocks: np.ndarray, n_rows: int) -> np.ndarray:
+    """x [M][K] f32 . W^T for Q4_K blocks W [n_rows][K/256 blocks of 144 B], in the current mode."""
+    x = np.ascontiguousarray(x, np.float32)
+    M, K = x.shape
+    y = np.empty((M, n_rows), np.float32)
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    lib().oc_linear_q4_k(_p(x, C.c_float), blocks.ctypes.data, M, n_rows, K, _p(y, C.c_float))
+    return y
 
 
 def linear_q8_0(x: np.ndarray, blocks: np.ndarray, n_rows: int) -> np.ndarray:
