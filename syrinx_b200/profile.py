@@ -42,7 +42,8 @@ def codec_run(frames: int, n: int):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--what", choices=["gemv", "frames", "stack", "prefill", "batch", "codec", "sample"], default="gemv")
-    ap.add_argument("--kind", type=int, default=2, help="0 wqkv, 1 wo, 2 w1|w3, 3 w2")
+    ap.add_argument("--kind", type=int, default=2,
+                    help="0 wqkv, 1 wo, 2 w1|w3 + SwiGLU merge, 3 w2, 4 w1|w3 alone (as the one-token chain runs it)")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--launches", type=int, default=16)
     ap.add_argument("--frames", type=int, default=4)
