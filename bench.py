@@ -300,7 +300,7 @@ def bench_device(args):
         res["b8"] = bench_b8(args, local, stream, dist, world, peak, peak_kind)
     if not args.no_codec:
         res["codec"] = bench_codec(args, local, stream, dist, world, rank)
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host-core baseline is an N=1 figure
         res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
     if dist:
         dist.barrier()
@@ -425,7 +425,7 @@ def bench_codec(args, local, stream, dist, world, rank):
            "e2e": {"value": round(T * world / (ms_e2e * 1e-3), 1), "unit": "codec frames/s",
                    "h2d_bytes_per_step": int(codes.size * 4), "d2h_bytes_per_step": int(T * codec.hop * 4),
                    "api": "sx_codec_decode (host codes in, host waveform out)"}}
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import codec_oracle
         n = 8
         t0 = time.perf_counter()
